@@ -1,0 +1,37 @@
+// Python bindings of the sm_100a kernels (one extension module, built in-tree).
+#include <torch/extension.h>
+
+#include "ops.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "placemoe_b200 sm_100a kernels";
+  // tcgen05 GEMMs
+  m.def("dense_gemm", &pm::dense_gemm);
+  m.def("moe_fc1_swiglu", &pm::moe_fc1_swiglu);
+  m.def("moe_grouped_gemm", &pm::moe_grouped_gemm);
+  m.def("moe_fc2_dgrad_dswiglu", &pm::moe_fc2_dgrad_dswiglu);
+  m.def("moe_wgrad", &pm::moe_wgrad);
+  // norms / rotary
+  m.def("rmsnorm_fwd", &pm::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &pm::rmsnorm_bwd);
+  m.def("qkv_rope_fwd", &pm::qkv_rope_fwd);
+  m.def("qkv_rope_bwd", &pm::qkv_rope_bwd);
+  // routing
+  m.def("router_topk_fwd", &pm::router_topk_fwd);
+  m.def("router_topk_bwd", &pm::router_topk_bwd);
+  m.def("moe_plan", &pm::moe_plan);
+  m.def("gather_rows", &pm::gather_rows);
+  m.def("sum_rows", &pm::sum_rows);
+  m.def("gather_scalar", &pm::gather_scalar);
+  // optimizer
+  m.def("adamw_build_table", &pm::adamw_build_table);
+  m.def("adamw_step", &pm::adamw_step);
+  m.def("sq_norm_build_table", &pm::sq_norm_build_table);
+  m.def("sq_norm", &pm::sq_norm);
+  // attention
+  m.def("attn_fwd", &pm::attn_fwd);
+  m.def("attn_bwd", &pm::attn_bwd);
+  // loss
+  m.def("ce_fwd_bwd", &pm::ce_fwd_bwd);
+  m.def("device_error", &pm::device_error, "read (and optionally clear) the kernels' error words");
+}

@@ -1,0 +1,12 @@
+// Aggregates the error words of every kernel translation unit.
+#include "ops.h"
+
+namespace pm {
+int device_error(bool reset) {
+  const int codes[] = {pm_error_gemm(reset), pm_error_norm(reset), pm_error_route(reset), pm_error_optim(reset),
+                       pm_error_loss(reset), pm_error_attn(reset)};
+  for (int c : codes)
+    if (c) return c;
+  return 0;
+}
+}  // namespace pm

@@ -1,0 +1,607 @@
+// Causal GQA flash attention on tcgen05 (sm_100a), forward and backward.
+//
+// Layout: q [T, Hq, D], k/v [T, Hkv, D], T = batch * seq_len, seq_len % 128 == 0,
+// D in {64, 128}.  Tiles are 128 queries x 128 keys.
+//
+// Forward, one CTA per (batch, q head, 128-query tile), 192 threads:
+//   warp 0  TMA producer (Q once, K/V double-buffered)
+//   warp 1  MMA issuer: S_j = Q K_j^T into one of two TMEM S buffers, then
+//           O += P_{j-1} V_{j-1} once the softmax of tile j-1 is published,
+//           so S_{j} overlaps softmax_{j-1}
+//   warps 2-5  softmax: one query row per thread, online max/sum in fp32,
+//           O rescaled in TMEM (skipped per warp when no row max moved), P
+//           written bf16 into 128B-swizzled shared memory (the A operand).
+//   TMEM: S0 | S1 | O   (512 columns allocated).
+//
+// Backward, one CTA per (batch, kv head, 128-key tile); loops over the q heads
+// of the GQA group and the q tiles at or after the key tile:
+//   S^T = K Q^T and dP^T = V dO^T (TMEM), softmax threads own one key row:
+//   P^T = exp2(S^T * c - lse), dS^T = P^T (dP^T - delta) * scale, both written
+//   to swizzled smem.  Then dV += P^T dO, dK += dS^T Q (TMEM accumulators over
+//   the whole loop) and dQ_tile = dS K (TMEM, reusing the S^T columns) which
+//   the same threads add to an fp32 dQ buffer with vector reductions.
+//   The same swizzled smem bytes serve as a K-major operand (rows = keys) and,
+//   reinterpreted, as an MN-major operand (rows = queries), so no transposes
+//   are materialised.
+//
+// Reference parity: flash attention forward/backward used by
+// veomni/ops/kernels/attention/__init__.py:151-353 (FA2/FA3/FA4 backends).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tma.h"
+
+namespace pm {
+
+constexpr int kTile = 128;
+constexpr int kAttnThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// K-major SW128 descriptor for a [rows x 128B-atom] tile; k-step of 16 elements
+PM_DEVICE uint64_t kmaj_desc(uint32_t base, int kstep) {
+  return make_sdesc_sw128(base + (kstep >> 2) * 16384 + (kstep & 3) * 32, 16, 1024);
+}
+// MN-major SW128 descriptor over a buffer made of 16 KB atoms (64 MN elements x 128 rows);
+// k-step of 16 rows.
+PM_DEVICE uint64_t mnmaj_desc(uint32_t base, int kstep) {
+  return make_sdesc_sw128(base + kstep * 2048, 16384, 1024);
+}
+
+// write 8 packed bf16 (16 bytes) at chunk c of row r of a 128-row SW128 atom
+PM_DEVICE void st_swz(uint8_t* atom, int r, int c, uint4 v) {
+  *reinterpret_cast<uint4*>(atom + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+struct AttnArgs {
+  int T, S, Hq, Hkv, B;
+  float scale;  // 1/sqrt(D)
+  __nv_bfloat16* o;
+  float* lse;  // [Hq, T] natural-log LSE
+  // backward
+  const float* delta;  // [Hq, T]
+  float* dq_acc;       // [T, Hq, D] fp32
+  __nv_bfloat16* dk;   // [T, Hkv, D]
+  __nv_bfloat16* dv;
+  const float* lse_in;
+};
+
+// ---------------------------------------------------------------- forward
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  constexpr int ND = D / 64;           // 64-element atoms along D
+  constexpr int kQBytes = ND * 16384;  // also K / V stage bytes
+  constexpr uint32_t kIdescS = make_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t kIdescO = make_idesc_bf16(128, D, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = sm;
+  uint8_t* sK = sQ + kQBytes;           // 2 stages
+  uint8_t* sV = sK + 2 * kQBytes;       // 2 stages
+  uint8_t* sP = sV + 2 * kQBytes;       // 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 32768);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;     // [2]
+  uint64_t* v_full = bars + 3;     // [2]
+  uint64_t* kv_empty = bars + 5;   // [2]
+  uint64_t* s_full = bars + 7;     // [2]
+  uint64_t* s_free = bars + 9;     // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 12;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = a.S / kTile;
+  const int L = blockIdx.x;
+  const int qt = nq - 1 - L / (a.B * a.Hq);
+  const int rem = L % (a.B * a.Hq);
+  const int b = rem / a.Hq, h = rem % a.Hq;
+  const int hk = h / (a.Hq / a.Hkv);
+  const int tq0 = b * a.S + qt * kTile;
+  const int nkv = qt + 1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1); mbar_init(&v_full[i], 1); mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1); mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) { tmem_alloc(s_tmem, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kQBytes);
+#pragma unroll
+      for (int d = 0; d < ND; ++d) tma_load_3d(sQ + d * 16384, &tmQ, q_full, d * 64, h, tq0);
+      for (int j = 0; j < nkv; ++j) {
+        const int st = j & 1;
+        if (!mbar_wait_abortable(&kv_empty[st], ((j >> 1) & 1) ^ 1, s_abort)) break;
+        const int tk0 = b * a.S + j * kTile;
+        mbar_arrive_expect_tx(&k_full[st], kQBytes);
+#pragma unroll
+        for (int d = 0; d < ND; ++d) tma_load_3d(sK + st * kQBytes + d * 16384, &tmK, &k_full[st], d * 64, hk, tk0);
+        mbar_arrive_expect_tx(&v_full[st], kQBytes);
+#pragma unroll
+        for (int d = 0; d < ND; ++d) tma_load_3d(sV + st * kQBytes + d * 16384, &tmV, &v_full[st], d * 64, hk, tk0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t aq = smem_u32(sQ), ap = smem_u32(sP);
+      const uint32_t t_o = tmem + 256;
+      bool ok = mbar_wait_abortable(q_full, 0, s_abort);
+      for (int j = 0; ok && j <= nkv; ++j) {
+        if (j < nkv) {
+          const int st = j & 1;
+          if (!mbar_wait_abortable(&k_full[st], (j >> 1) & 1, s_abort)) break;
+          if (!mbar_wait_abortable(&s_free[st], ((j >> 1) & 1) ^ 1, s_abort)) break;
+          tc_fence_after();
+          const uint32_t ak = smem_u32(sK + st * kQBytes);
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) umma_f16(tmem + st * 128, kmaj_desc(aq, k), kmaj_desc(ak, k), kIdescS, k > 0);
+          umma_commit(&s_full[st]);
+        }
+        if (j >= 1) {
+          const int pj = j - 1, st = pj & 1;
+          if (!mbar_wait_abortable(p_full, pj & 1, s_abort)) break;
+          if (!mbar_wait_abortable(&v_full[st], (pj >> 1) & 1, s_abort)) break;
+          tc_fence_after();
+          const uint32_t av = smem_u32(sV + st * kQBytes);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) umma_f16(t_o, kmaj_desc(ap, k), mnmaj_desc(av, k), kIdescO, (pj > 0 || k > 0));
+          umma_commit(&kv_empty[st]);
+          umma_commit(pv_done);
+        }
+      }
+    }
+  } else {
+    // softmax warps: one query row per thread
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
+    const float c = a.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait_abortable(&s_full[st], (j >> 1) & 1, s_abort)) { ok = false; break; }
+      tc_fence_after();
+      float x[128];
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(trow + st * 128 + cc * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) x[cc * 32 + i] = __uint_as_float(v[i]) * c;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[st]);
+      if (j == qt) {  // diagonal tile: key index > query index is masked
+#pragma unroll
+        for (int i = 0; i < 128; ++i)
+          if (i > r) x[i] = -INFINITY;
+      }
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) mx = fmaxf(mx, x[i]);
+      const float alpha = fast_exp2(m - mx);  // 0 on the first tile
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        x[i] = fast_exp2(x[i] - mx);
+        rs += x[i];
+      }
+      l = l * alpha + rs;
+      m = mx;
+      if (j > 0) {
+        if (!mbar_wait_abortable(pv_done, (j - 1) & 1, s_abort)) { ok = false; break; }
+        tc_fence_after();
+        if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
+#pragma unroll
+          for (int cc = 0; cc < D / 16; ++cc) {
+            uint32_t v[16];
+            tmem_ld16(trow + 256 + cc * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+            tmem_st16(trow + 256 + cc * 16, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P (bf16) -> swizzled smem, 2 atoms of 64 keys
+#pragma unroll
+      for (int cch = 0; cch < 16; ++cch) {
+        const int k0 = cch * 8;
+        uint4 pk = make_uint4(pack_bf16(x[k0], x[k0 + 1]), pack_bf16(x[k0 + 2], x[k0 + 3]),
+                              pack_bf16(x[k0 + 4], x[k0 + 5]), pack_bf16(x[k0 + 6], x[k0 + 7]));
+        st_swz(sP + (cch >> 3) * 16384, r, cch & 7, pk);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && mbar_wait_abortable(pv_done, (nkv - 1) & 1, s_abort)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = a.o + ((size_t)(tq0 + r) * a.Hq + h) * D;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(trow + 256 + cc * 32, v);
+        tmem_ld_wait();
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pack_bf16(__uint_as_float(v[8 * i]) * inv, __uint_as_float(v[8 * i + 1]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 2]) * inv, __uint_as_float(v[8 * i + 3]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 4]) * inv, __uint_as_float(v[8 * i + 5]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 6]) * inv, __uint_as_float(v[8 * i + 7]) * inv));
+      }
+      a.lse[(size_t)h * a.T + tq0 + r] = (m + __log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[h, t] = sum_d dO[t, h, d] * O[t, h, d]
+__global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, int T,
+                                  int Hq, int D, float* __restrict__ delta) {
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= T * Hq) return;
+  const int t = w / Hq, h = w % Hq;
+  const __nv_bfloat16* po = o + (size_t)w * D;
+  const __nv_bfloat16* pd = dout + (size_t)w * D;
+  float s = 0.f;
+  for (int i = lane * 2; i < D; i += 64) {
+    const __nv_bfloat162 x = *reinterpret_cast<const __nv_bfloat162*>(po + i);
+    const __nv_bfloat162 y = *reinterpret_cast<const __nv_bfloat162*>(pd + i);
+    s += __low2float(x) * __low2float(y) + __high2float(x) * __high2float(y);
+  }
+  s = warp_sum(s);
+  if (lane == 0) delta[(size_t)h * T + t] = s;
+}
+
+// ---------------------------------------------------------------- backward
+template <int D>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, AttnArgs a) {
+  constexpr int ND = D / 64;
+  constexpr int kTB = ND * 16384;  // one [128 x D] bf16 tile
+  constexpr uint32_t kIdescS = make_idesc_bf16(128, 128, false, false);   // St, dPt
+  constexpr uint32_t kIdescKV = make_idesc_bf16(128, D, false, true);    // dV, dK, dQ (A K-major)
+  constexpr uint32_t kIdescQ = make_idesc_bf16(128, D, true, true);      // dQ (A MN-major)
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sK = sm;
+  uint8_t* sV = sK + kTB;
+  uint8_t* sQ = sV + kTB;
+  uint8_t* sDO = sQ + kTB;
+  uint8_t* sP = sDO + kTB;     // 32 KB: P^T [keys x queries]
+  uint8_t* sDS = sP + 32768;   // 32 KB: dS^T
+  float* sLse = reinterpret_cast<float*>(sDS + 32768);  // [128], log2 units
+  float* sDelta = sLse + 128;                          // [128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + 128);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* s_full = bars + 3;
+  uint64_t* ds_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* st_free = bars + 6;
+  uint64_t* dkv_full = bars + 7;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nq = a.S / kTile;
+  const int G = a.Hq / a.Hkv;
+  const int L = blockIdx.x;
+  const int kt = L / (a.B * a.Hkv);  // light tiles (large kt) last is fine: kt small = more work, scheduled first
+  const int rem = L % (a.B * a.Hkv);
+  const int b = rem / a.Hkv, hk = rem % a.Hkv;
+  const int tk0 = b * a.S + kt * kTile;
+  const int nqt = nq - kt;
+  const int n_it = G * nqt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1); mbar_init(qdo_full, 1); mbar_init(qdo_empty, 1); mbar_init(s_full, 1);
+    mbar_init(ds_full, 128); mbar_init(dq_full, 1); mbar_init(st_free, 128); mbar_init(dkv_full, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) { tmem_alloc(s_tmem, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+  const uint32_t t_st = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + D;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * kTB);
+#pragma unroll
+      for (int d = 0; d < ND; ++d) {
+        tma_load_3d(sK + d * 16384, &tmK, kv_full, d * 64, hk, tk0);
+        tma_load_3d(sV + d * 16384, &tmV, kv_full, d * 64, hk, tk0);
+      }
+      for (int it = 0; it < n_it; ++it) {
+        const int h = hk * G + it / nqt;
+        const int qt = kt + it % nqt;
+        const int tq0 = b * a.S + qt * kTile;
+        if (!mbar_wait_abortable(qdo_empty, (it & 1) ^ 1, s_abort)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * kTB + 1024);
+#pragma unroll
+        for (int d = 0; d < ND; ++d) {
+          tma_load_3d(sQ + d * 16384, &tmQ, qdo_full, d * 64, h, tq0);
+          tma_load_3d(sDO + d * 16384, &tmDO, qdo_full, d * 64, h, tq0);
+        }
+        bulk_load(sLse, a.lse_in + (size_t)h * a.T + tq0, 512, qdo_full);
+        bulk_load(sDelta, a.delta + (size_t)h * a.T + tq0, 512, qdo_full);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
+      const uint32_t aP = smem_u32(sP), aDS = smem_u32(sDS);
+      bool ok = mbar_wait_abortable(kv_full, 0, s_abort);
+      for (int it = 0; ok && it < n_it; ++it) {
+        if (!mbar_wait_abortable(qdo_full, it & 1, s_abort)) break;
+        if (!mbar_wait_abortable(st_free, (it & 1) ^ 1, s_abort)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16(t_st, kmaj_desc(aK, k), kmaj_desc(aQ, k), kIdescS, k > 0);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) umma_f16(t_dp, kmaj_desc(aV, k), kmaj_desc(aDO, k), kIdescS, k > 0);
+        umma_commit(s_full);
+        if (!mbar_wait_abortable(ds_full, it & 1, s_abort)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_f16(t_dv, kmaj_desc(aP, k), mnmaj_desc(aDO, k), kIdescKV, (it > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_f16(t_dk, kmaj_desc(aDS, k), mnmaj_desc(aQ, k), kIdescKV, (it > 0 || k > 0));
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_f16(t_st, mnmaj_desc(aDS, k), mnmaj_desc(aK, k), kIdescQ, k > 0);
+        umma_commit(qdo_empty);
+        umma_commit(dq_full);
+      }
+      umma_commit(dkv_full);
+    }
+  } else {
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;  // key row (S^T, dP^T, dV, dK) / query row (dQ)
+    const uint32_t lrow = (uint32_t)(qd * 32) << 16;
+    const float c = a.scale * kLog2e;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const int h = hk * G + it / nqt;
+      const int qt = kt + it % nqt;
+      const int tq0 = b * a.S + qt * kTile;
+      if (!mbar_wait_abortable(s_full, it & 1, s_abort)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = qt == kt;
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t sv[32], pv[32];
+        tmem_ld32(t_st + lrow + cc * 32, sv);
+        tmem_ld32(t_dp + lrow + cc * 32, pv);
+        tmem_ld_wait();
+        float p[32], ds[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int q = cc * 32 + i;
+          float e = fast_exp2(__uint_as_float(sv[i]) * c - sLse[q]);
+          if (diag && q < r) e = 0.f;
+          p[i] = e;
+          ds[i] = e * (__uint_as_float(pv[i]) - sDelta[q]) * a.scale;
+        }
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int chunk = cc * 4 + g;  // 8 queries per 16-byte chunk
+          uint4 pk = make_uint4(pack_bf16(p[8 * g], p[8 * g + 1]), pack_bf16(p[8 * g + 2], p[8 * g + 3]),
+                                pack_bf16(p[8 * g + 4], p[8 * g + 5]), pack_bf16(p[8 * g + 6], p[8 * g + 7]));
+          uint4 dk = make_uint4(pack_bf16(ds[8 * g], ds[8 * g + 1]), pack_bf16(ds[8 * g + 2], ds[8 * g + 3]),
+                                pack_bf16(ds[8 * g + 4], ds[8 * g + 5]), pack_bf16(ds[8 * g + 6], ds[8 * g + 7]));
+          st_swz(sP + (chunk >> 3) * 16384, r, chunk & 7, pk);
+          st_swz(sDS + (chunk >> 3) * 16384, r, chunk & 7, dk);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(ds_full);
+      // dQ tile (rows = queries) -> fp32 accumulation buffer
+      if (!mbar_wait_abortable(dq_full, it & 1, s_abort)) { ok = false; break; }
+      tc_fence_after();
+      float* dst = a.dq_acc + ((size_t)(tq0 + r) * a.Hq + h) * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(t_st + lrow + cc * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          red_add_v4(dst + cc * 32 + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
+                     __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+      }
+      tc_fence_before();
+      mbar_arrive(st_free);
+    }
+    if (ok && mbar_wait_abortable(dkv_full, 0, s_abort)) {
+      tc_fence_after();
+      __nv_bfloat16* dvrow = a.dv + ((size_t)(tk0 + r) * a.Hkv + hk) * D;
+      __nv_bfloat16* dkrow = a.dk + ((size_t)(tk0 + r) * a.Hkv + hk) * D;
+#pragma unroll 1
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32], w[32];
+        tmem_ld32(t_dv + lrow + cc * 32, v);
+        tmem_ld32(t_dk + lrow + cc * 32, w);
+        tmem_ld_wait();
+        uint4* dv4 = reinterpret_cast<uint4*>(dvrow + cc * 32);
+        uint4* dk4 = reinterpret_cast<uint4*>(dkrow + cc * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          dv4[i] = make_uint4(pack_bf16(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
+                              pack_bf16(__uint_as_float(v[8 * i + 2]), __uint_as_float(v[8 * i + 3])),
+                              pack_bf16(__uint_as_float(v[8 * i + 4]), __uint_as_float(v[8 * i + 5])),
+                              pack_bf16(__uint_as_float(v[8 * i + 6]), __uint_as_float(v[8 * i + 7])));
+          dk4[i] = make_uint4(pack_bf16(__uint_as_float(w[8 * i]), __uint_as_float(w[8 * i + 1])),
+                              pack_bf16(__uint_as_float(w[8 * i + 2]), __uint_as_float(w[8 * i + 3])),
+                              pack_bf16(__uint_as_float(w[8 * i + 4]), __uint_as_float(w[8 * i + 5])),
+                              pack_bf16(__uint_as_float(w[8 * i + 6]), __uint_as_float(w[8 * i + 7])));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// fp32 -> bf16
+__global__ void f32_to_bf16_kernel(const float* __restrict__ src, __nv_bfloat16* __restrict__ dst, long long n) {
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i + 3 < n) {
+    const float4 v = *reinterpret_cast<const float4*>(src + i);
+    *reinterpret_cast<uint2*>(dst + i) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+  } else {
+    for (long long j = i; j < n; ++j) dst[j] = __float2bfloat16(src[j]);
+  }
+}
+
+// ------------------------------------------------------------------ host
+static CUtensorMap head_map(const torch::Tensor& t) {
+  // t: [T, H, D] contiguous bf16 -> dims {D, H, T}, box {64, 1, 128}
+  const int64_t T = t.size(0), H = t.size(1), D = t.size(2);
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)(D * 2), (cuuint64_t)(H * D * 2)};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, t.data_ptr(), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "attention tensor map failed: ", (int)r);
+  return m;
+}
+
+static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t S) {
+  TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q [T,Hq,D] bf16");
+  TORCH_CHECK(k.sizes() == v.sizes() && k.is_contiguous() && v.is_contiguous(), "k/v layout");
+  TORCH_CHECK(k.size(0) == q.size(0) && k.size(2) == q.size(2), "k/v shape");
+  TORCH_CHECK(q.size(1) % k.size(1) == 0, "Hq must be a multiple of Hkv");
+  TORCH_CHECK(S % kTile == 0 && q.size(0) % S == 0, "seq_len must be a multiple of 128 and divide T");
+  TORCH_CHECK(q.size(2) == 64 || q.size(2) == 128, "head_dim must be 64 or 128");
+}
+
+template <int D>
+static int fwd_smem() { return 1024 + (5 * (D / 64) * 16384) + 32768 + 256; }
+template <int D>
+static int bwd_smem() { return 1024 + 4 * (D / 64) * 16384 + 2 * 32768 + 1024 + 256; }
+
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S) {
+  check_qkv(q, k, v, S);
+  c10::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), Hq = (int)q.size(1), Hkv = (int)k.size(1), D = (int)q.size(2);
+  auto o = torch::empty_like(q);
+  auto lse = torch::empty({Hq, T}, q.options().dtype(torch::kFloat32));
+  if (T == 0) return {o, lse};
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.T = T; a.S = (int)S; a.Hq = Hq; a.Hkv = Hkv; a.B = T / (int)S;
+  a.scale = 1.f / sqrtf((float)D);
+  a.o = (__nv_bfloat16*)o.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v);
+  const int grid = a.B * Hq * ((int)S / kTile);
+  auto stream = at::cuda::getCurrentCUDAStream();
+  if (D == 128) {
+    auto kern = attn_fwd_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd_smem<128>()));
+    kern<<<grid, kAttnThreads, fwd_smem<128>(), stream>>>(mq, mk, mv, a);
+  } else {
+    auto kern = attn_fwd_kernel<64>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd_smem<64>()));
+    kern<<<grid, kAttnThreads, fwd_smem<64>(), stream>>>(mq, mk, mv, a);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {o, lse};
+}
+
+std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
+                                    torch::Tensor lse, torch::Tensor dout, int64_t S) {
+  check_qkv(q, k, v, S);
+  TORCH_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes() && o.sizes() == q.sizes(), "dout / o layout");
+  c10::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), Hq = (int)q.size(1), Hkv = (int)k.size(1), D = (int)q.size(2);
+  auto dq = torch::empty_like(q);
+  auto dk = torch::empty_like(k);
+  auto dv = torch::empty_like(v);
+  if (T == 0) return {dq, dk, dv};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto delta = torch::empty({Hq, T}, q.options().dtype(torch::kFloat32));
+  attn_delta_kernel<<<(T * Hq + 7) / 8, 256, 0, stream>>>((const __nv_bfloat16*)o.data_ptr(),
+                                                          (const __nv_bfloat16*)dout.data_ptr(), T, Hq, D,
+                                                          delta.data_ptr<float>());
+  auto dq_acc = torch::zeros({T, Hq, D}, q.options().dtype(torch::kFloat32));
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.T = T; a.S = (int)S; a.Hq = Hq; a.Hkv = Hkv; a.B = T / (int)S;
+  a.scale = 1.f / sqrtf((float)D);
+  a.delta = delta.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dk = (__nv_bfloat16*)dk.data_ptr();
+  a.dv = (__nv_bfloat16*)dv.data_ptr();
+  // the kernel consumes the LSE in log2 units
+  auto lse2 = (lse * kLog2e).contiguous();
+  a.lse_in = lse2.data_ptr<float>();
+  CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v), mdo = head_map(dout);
+  const int grid = a.B * Hkv * ((int)S / kTile);
+  if (D == 128) {
+    auto kern = attn_bwd_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<128>()));
+    kern<<<grid, kAttnThreads, bwd_smem<128>(), stream>>>(mq, mk, mv, mdo, a);
+  } else {
+    auto kern = attn_bwd_kernel<64>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<64>()));
+    kern<<<grid, kAttnThreads, bwd_smem<64>(), stream>>>(mq, mk, mv, mdo, a);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  const long long n = (long long)T * Hq * D;
+  f32_to_bf16_kernel<<<(unsigned)((n / 4 + 255) / 256 + 1), 256, 0, stream>>>(dq_acc.data_ptr<float>(),
+                                                                              (__nv_bfloat16*)dq.data_ptr(), n);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {dq, dk, dv};
+}
+
+}  // namespace pm
+
+PM_DEFINE_ERROR_QUERY(pm_error_attn)

@@ -1,0 +1,434 @@
+// RMSNorm and the fused QK-norm + RoPE kernels (sm_100a).
+//
+// rmsnorm_fwd/bwd: one warp per row, 16-byte vector accesses, fp32 math;
+//   backward accumulates d(weight) per CTA in registers/shared memory and
+//   adds it to the fp32 output with one atomic per element per CTA.
+// qkv_rope_fwd/bwd: one CTA per token splits the fused QKV projection into
+//   q/k/v, applies RMSNorm to q and k (groups of `q_group`/`k_group`
+//   elements: head_dim for Qwen3-MoE per-head norms, the full width for
+//   OLMoE), then rotary embedding (rotate-half convention) from a fp32
+//   inverse-frequency table.
+//
+// Reference parity: RMSNorm/RoPE ops of veomni/ops/liger/__init__.py:52-133,
+// veomni/ops/kernels/rms_norm/triton_batch_invariant.py:27 and the
+// Qwen3-MoE attention of
+// veomni/models/transformers/qwen3_moe/generated/patched_modeling_qwen3_moe_gpu.py.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace pm {
+
+template <typename WT>
+__device__ __forceinline__ float ldw(const WT* w, int i) { return static_cast<float>(w[i]); }
+template <>
+__device__ __forceinline__ float ldw<__nv_bfloat16>(const __nv_bfloat16* w, int i) { return __bfloat162float(w[i]); }
+
+// H is a multiple of 256; each lane owns H/256 vectors of 8 elements.
+template <int VPL, typename WT>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
+                                                          __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                          int rows, int H, float eps) {
+  const int warp = (blockIdx.x * 8) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)warp * H);
+  float v[VPL][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    uint4 q = xr[i * 32 + lane];
+    uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[i][2 * j] = bf16_lo(u[j]);
+      v[i][2 * j + 1] = bf16_hi(u[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / H + eps);
+  if (lane == 0) rstd[warp] = r;
+  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)warp * H);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c0 = (i * 32 + lane) * 8;
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      o[j] = pack_bf16(v[i][2 * j] * r * ldw(w, c0 + 2 * j), v[i][2 * j + 1] * r * ldw(w, c0 + 2 * j + 1));
+    yr[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+template <int VPL, typename WT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                          const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
+                                                          const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                                          float* __restrict__ dw, int rows, int H) {
+  const int lane = threadIdx.x & 31;
+  const int wid = threadIdx.x >> 5;
+  float dwacc[VPL][8];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
+  for (int row = blockIdx.x * 8 + wid; row < rows; row += gridDim.x * 8) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
+    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
+    const float r = rstd[row];
+    float xv[VPL][8], gw[VPL][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      uint4 qx = xr[i * 32 + lane], qg = gr[i * 32 + lane];
+      uint32_t ux[4] = {qx.x, qx.y, qx.z, qx.w}, ug[4] = {qg.x, qg.y, qg.z, qg.w};
+      const int c0 = (i * 32 + lane) * 8;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xv[i][2 * j] = bf16_lo(ux[j]);
+        xv[i][2 * j + 1] = bf16_hi(ux[j]);
+        const float g0 = bf16_lo(ug[j]), g1 = bf16_hi(ug[j]);
+        dwacc[i][2 * j] += g0 * xv[i][2 * j] * r;
+        dwacc[i][2 * j + 1] += g1 * xv[i][2 * j + 1] * r;
+        gw[i][2 * j] = g0 * ldw(w, c0 + 2 * j);
+        gw[i][2 * j + 1] = g1 * ldw(w, c0 + 2 * j + 1);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += gw[i][j] * xv[i][j];
+    }
+    dot = warp_sum(dot);
+    const float c = dot * r * r * r / H;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        o[j] = pack_bf16(r * gw[i][2 * j] - c * xv[i][2 * j], r * gw[i][2 * j + 1] - c * xv[i][2 * j + 1]);
+      dr[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // reduce d(weight) over the 8 warps of the CTA, then one atomic per element
+  extern __shared__ float sdw[];  // [H]
+  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < VPL; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) atomicAdd(&sdw[(i * 32 + lane) * 8 + j], dwacc[i][j]);
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
+}
+
+static int sm_count() {
+  int dev, n;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+#define PM_VPL_DISPATCH(H, ...)                                       \
+  switch ((H) / 256) {                                               \
+    case 1: { constexpr int VPL = 1; __VA_ARGS__; break; }           \
+    case 2: { constexpr int VPL = 2; __VA_ARGS__; break; }           \
+    case 4: { constexpr int VPL = 4; __VA_ARGS__; break; }           \
+    case 8: { constexpr int VPL = 8; __VA_ARGS__; break; }           \
+    case 16: { constexpr int VPL = 16; __VA_ARGS__; break; }         \
+    default: TORCH_CHECK(false, "rmsnorm: hidden size must be 256 * {1,2,4,8,16}"); \
+  }
+
+std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  TORCH_CHECK(w.numel() == H && w.is_contiguous(), "weight size");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  if (rows == 0) return {y, rstd};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int grid = (rows + 7) / 8;
+  if (w.scalar_type() == torch::kFloat32) {
+    PM_VPL_DISPATCH(H, rmsnorm_fwd_kernel<VPL, float><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)x.data_ptr(), w.data_ptr<float>(), (__nv_bfloat16*)y.data_ptr(),
+        rstd.data_ptr<float>(), rows, H, (float)eps));
+  } else {
+    TORCH_CHECK(w.scalar_type() == torch::kBFloat16, "weight must be fp32 or bf16");
+    PM_VPL_DISPATCH(H, rmsnorm_fwd_kernel<VPL, __nv_bfloat16><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+        rstd.data_ptr<float>(), rows, H, (float)eps));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {y, rstd};
+}
+
+// returns dx (bf16) and accumulates into dw (fp32, [H])
+torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == torch::kBFloat16, "dy/x contiguous bf16");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous(), "dw must be fp32");
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  c10::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  if (rows == 0) return dx;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int grid = std::min((rows + 7) / 8, sm_count() * 4);
+  const size_t smem = (size_t)H * sizeof(float);
+  if (w.scalar_type() == torch::kFloat32) {
+    PM_VPL_DISPATCH(H, rmsnorm_bwd_kernel<VPL, float><<<grid, 256, smem, stream>>>(
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), w.data_ptr<float>(),
+        rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), rows, H));
+  } else {
+    PM_VPL_DISPATCH(H, rmsnorm_bwd_kernel<VPL, __nv_bfloat16><<<grid, 256, smem, stream>>>(
+        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(),
+        (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(),
+        dw.data_ptr<float>(), rows, H));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+// ----------------------------------------------------------------------------
+// Fused QK-norm + RoPE
+// ----------------------------------------------------------------------------
+struct QkvArgs {
+  int T, Hq, Hkv, D;
+  int q_group, k_group;  // RMSNorm group sizes (0 = no norm)
+  float eps;
+  const __nv_bfloat16* qkv;  // [T, (Hq + 2 Hkv) D]
+  const int* pos;            // [T]
+  const float* inv_freq;     // [D/2]
+  const float* qw;           // [q_group] or null
+  const float* kw;           // [k_group] or null
+  __nv_bfloat16* q;          // [T, Hq, D]
+  __nv_bfloat16* k;          // [T, Hkv, D]
+  __nv_bfloat16* v;          // [T, Hkv, D]
+  float* rq;                 // [T, Hq D / q_group]
+  float* rk;                 // [T, Hkv D / k_group]
+  // backward
+  const __nv_bfloat16* dq;
+  const __nv_bfloat16* dk;
+  const __nv_bfloat16* dv;
+  __nv_bfloat16* dqkv;
+  float* dqw;
+  float* dkw;
+};
+
+// One CTA (256 threads) per token in the forward pass.
+__global__ void __launch_bounds__(256) qkv_rope_fwd_kernel(QkvArgs a) {
+  extern __shared__ float sm[];
+  const int t = blockIdx.x;
+  const int W = (a.Hq + 2 * a.Hkv) * a.D;
+  const int nq = a.Hq * a.D, nk = a.Hkv * a.D;
+  float* xs = sm;                // [nq + nk]
+  float* ss = sm + nq + nk;      // group sums
+  const int qg = a.q_group ? nq / a.q_group : 0;
+  const int kg = a.k_group ? nk / a.k_group : 0;
+  const __nv_bfloat16* row = a.qkv + (size_t)t * W;
+  for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) ss[i] = 0.f;
+  __syncthreads();
+  for (int i = threadIdx.x * 2; i < nq + nk; i += blockDim.x * 2) {
+    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(row + i);
+    const float x0 = __low2float(p), x1 = __high2float(p);
+    xs[i] = x0;
+    xs[i + 1] = x1;
+    if (i < nq) {
+      if (a.q_group) atomicAdd(&ss[i / a.q_group], x0 * x0 + x1 * x1);
+    } else if (a.k_group) {
+      atomicAdd(&ss[qg + (i - nq) / a.k_group], x0 * x0 + x1 * x1);
+    }
+  }
+  // v passes through
+  for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
+    *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + i) = *reinterpret_cast<const uint4*>(row + nq + nk + i);
+  __syncthreads();
+  for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) {
+    const int G = i < qg ? a.q_group : a.k_group;
+    const float r = rsqrtf(ss[i] / G + a.eps);
+    ss[i] = r;
+    if (i < qg) a.rq[(size_t)t * qg + i] = r;
+    else a.rk[(size_t)t * kg + (i - qg)] = r;
+  }
+  __syncthreads();
+  const float p = (float)a.pos[t];
+  const int half = a.D / 2;
+  const int pairs = (a.Hq + a.Hkv) * half;
+  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
+    const int h = idx / half, i = idx - h * half;
+    const bool isq = h < a.Hq;
+    const int e0 = h * a.D + i, e1 = e0 + half;  // positions in xs (q then k)
+    float x0 = xs[e0], x1 = xs[e1];
+    if (isq && a.q_group) {
+      x0 *= ss[e0 / a.q_group] * a.qw[e0 % a.q_group];
+      x1 *= ss[e1 / a.q_group] * a.qw[e1 % a.q_group];
+    } else if (!isq && a.k_group) {
+      const int k0 = e0 - nq, k1 = e1 - nq;
+      x0 *= ss[qg + k0 / a.k_group] * a.kw[k0 % a.k_group];
+      x1 *= ss[qg + k1 / a.k_group] * a.kw[k1 % a.k_group];
+    }
+    float sn, cs;
+    sincosf(p * a.inv_freq[i], &sn, &cs);
+    const float o0 = x0 * cs - x1 * sn;
+    const float o1 = x1 * cs + x0 * sn;
+    __nv_bfloat16* dst = isq ? a.q + (size_t)t * nq + e0 : a.k + (size_t)t * nk + (e0 - nq);
+    dst[0] = __float2bfloat16(o0);
+    dst[half] = __float2bfloat16(o1);
+  }
+}
+
+// Backward: CTAs stride over tokens, d(weight) accumulated in shared memory.
+__global__ void __launch_bounds__(256) qkv_rope_bwd_kernel(QkvArgs a) {
+  extern __shared__ float sm[];
+  const int W = (a.Hq + 2 * a.Hkv) * a.D;
+  const int nq = a.Hq * a.D, nk = a.Hkv * a.D;
+  const int qg = a.q_group ? nq / a.q_group : 0;
+  const int kg = a.k_group ? nk / a.k_group : 0;
+  float* g = sm;                         // [nq + nk] grad wrt normalized (pre-rope) values
+  float* xs = g + nq + nk;               // [nq + nk] inputs
+  float* dots = xs + nq + nk;            // [qg + kg]
+  float* sdq = dots + qg + kg;           // [q_group]
+  float* sdk = sdq + a.q_group;          // [k_group]
+  for (int i = threadIdx.x; i < a.q_group + a.k_group; i += blockDim.x) sdq[i] = 0.f;
+  const int half = a.D / 2;
+  const int pairs = (a.Hq + a.Hkv) * half;
+  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    __syncthreads();
+    const __nv_bfloat16* row = a.qkv + (size_t)t * W;
+    __nv_bfloat16* drow = a.dqkv + (size_t)t * W;
+    for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) dots[i] = 0.f;
+    const float p = (float)a.pos[t];
+    for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
+      const int h = idx / half, i = idx - h * half;
+      const bool isq = h < a.Hq;
+      const int e0 = h * a.D + i, e1 = e0 + half;
+      const __nv_bfloat16* src = isq ? a.dq + (size_t)t * nq + e0 : a.dk + (size_t)t * nk + (e0 - nq);
+      const float d0 = __bfloat162float(src[0]), d1 = __bfloat162float(src[half]);
+      float sn, cs;
+      sincosf(p * a.inv_freq[i], &sn, &cs);
+      g[e0] = d0 * cs + d1 * sn;
+      g[e1] = -d0 * sn + d1 * cs;
+      xs[e0] = __bfloat162float(row[e0]);
+      xs[e1] = __bfloat162float(row[e1]);
+    }
+    for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(drow + nq + nk + i) = *reinterpret_cast<const uint4*>(a.dv + (size_t)t * nk + i);
+    __syncthreads();
+    // dot_g = sum_j w_j g_j x_j over each norm group; d(weight) partials
+    for (int e = threadIdx.x; e < nq + nk; e += blockDim.x) {
+      if (e < nq) {
+        if (!a.q_group) continue;
+        const int grp = e / a.q_group, j = e % a.q_group;
+        const float r = a.rq[(size_t)t * qg + grp];
+        atomicAdd(&dots[grp], a.qw[j] * g[e] * xs[e]);
+        atomicAdd(&sdq[j], g[e] * xs[e] * r);
+      } else {
+        if (!a.k_group) continue;
+        const int ke = e - nq;
+        const int grp = ke / a.k_group, j = ke % a.k_group;
+        const float r = a.rk[(size_t)t * kg + grp];
+        atomicAdd(&dots[qg + grp], a.kw[j] * g[e] * xs[e]);
+        atomicAdd(&sdk[j], g[e] * xs[e] * r);
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < nq + nk; e += blockDim.x) {
+      float out;
+      if (e < nq) {
+        if (a.q_group) {
+          const int grp = e / a.q_group, j = e % a.q_group;
+          const float r = a.rq[(size_t)t * qg + grp];
+          out = r * a.qw[j] * g[e] - xs[e] * r * r * r * dots[grp] / a.q_group;
+        } else out = g[e];
+      } else {
+        const int ke = e - nq;
+        if (a.k_group) {
+          const int grp = ke / a.k_group, j = ke % a.k_group;
+          const float r = a.rk[(size_t)t * kg + grp];
+          out = r * a.kw[j] * g[e] - xs[e] * r * r * r * dots[qg + grp] / a.k_group;
+        } else out = g[e];
+      }
+      drow[e] = __float2bfloat16(out);
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < a.q_group; i += blockDim.x) atomicAdd(&a.dqw[i], sdq[i]);
+  for (int i = threadIdx.x; i < a.k_group; i += blockDim.x) atomicAdd(&a.dkw[i], sdk[i]);
+}
+
+// Returns q [T,Hq,D], k [T,Hkv,D], v [T,Hkv,D], rstd_q, rstd_k.
+std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+                                        c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw, int64_t Hq,
+                                        int64_t Hkv, int64_t D, int64_t q_group, int64_t k_group, double eps) {
+  TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == torch::kBFloat16 && qkv.is_contiguous(), "qkv contiguous bf16");
+  TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * D, "qkv width");
+  TORCH_CHECK(D % 16 == 0, "head_dim must be a multiple of 16");
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && inv_freq.scalar_type() == torch::kFloat32, "pos int32, inv_freq fp32");
+  const int T = (int)(qkv.numel() / qkv.size(-1));
+  TORCH_CHECK(pos.numel() == T, "positions");
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto opt = qkv.options();
+  auto q = torch::empty({T, Hq, D}, opt);
+  auto k = torch::empty({T, Hkv, D}, opt);
+  auto v = torch::empty({T, Hkv, D}, opt);
+  const int qg = q_group ? (int)(Hq * D / q_group) : 0;
+  const int kg = k_group ? (int)(Hkv * D / k_group) : 0;
+  auto rq = torch::empty({T, std::max(qg, 1)}, opt.dtype(torch::kFloat32));
+  auto rk = torch::empty({T, std::max(kg, 1)}, opt.dtype(torch::kFloat32));
+  if (T == 0) return {q, k, v, rq, rk};
+  QkvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.T = T; a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.D = (int)D; a.q_group = (int)q_group; a.k_group = (int)k_group;
+  a.eps = (float)eps;
+  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>(); a.inv_freq = inv_freq.data_ptr<float>();
+  a.qw = q_group ? qw->data_ptr<float>() : nullptr;
+  a.kw = k_group ? kw->data_ptr<float>() : nullptr;
+  a.q = (__nv_bfloat16*)q.data_ptr(); a.k = (__nv_bfloat16*)k.data_ptr(); a.v = (__nv_bfloat16*)v.data_ptr();
+  a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
+  const size_t smem = (size_t)((Hq + Hkv) * D + qg + kg) * sizeof(float);
+  auto kern = qkv_rope_fwd_kernel;
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  kern<<<T, 256, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {q, k, v, rq, rk};
+}
+
+// Returns dqkv; accumulates d(q_norm weight), d(k_norm weight) into dqw/dkw (fp32).
+torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv, torch::Tensor pos,
+                           torch::Tensor inv_freq, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
+                           torch::Tensor rq, torch::Tensor rk, c10::optional<torch::Tensor> dqw,
+                           c10::optional<torch::Tensor> dkw, int64_t Hq, int64_t Hkv, int64_t D, int64_t q_group,
+                           int64_t k_group) {
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "grads must be contiguous");
+  const int T = (int)(qkv.numel() / qkv.size(-1));
+  c10::cuda::CUDAGuard guard(qkv.device());
+  auto dqkv = torch::empty_like(qkv);
+  if (T == 0) return dqkv;
+  const int qg = q_group ? (int)(Hq * D / q_group) : 0;
+  const int kg = k_group ? (int)(Hkv * D / k_group) : 0;
+  QkvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.T = T; a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.D = (int)D; a.q_group = (int)q_group; a.k_group = (int)k_group;
+  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>(); a.inv_freq = inv_freq.data_ptr<float>();
+  a.qw = q_group ? qw->data_ptr<float>() : nullptr;
+  a.kw = k_group ? kw->data_ptr<float>() : nullptr;
+  a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
+  a.dq = (const __nv_bfloat16*)dq.data_ptr(); a.dk = (const __nv_bfloat16*)dk.data_ptr();
+  a.dv = (const __nv_bfloat16*)dv.data_ptr(); a.dqkv = (__nv_bfloat16*)dqkv.data_ptr();
+  a.dqw = q_group ? dqw->data_ptr<float>() : nullptr;
+  a.dkw = k_group ? dkw->data_ptr<float>() : nullptr;
+  const size_t smem = (size_t)(2 * (Hq + Hkv) * D + qg + kg + q_group + k_group) * sizeof(float);
+  auto kern = qkv_rope_bwd_kernel;
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int grid = std::min(T, sm_count() * 4);
+  kern<<<grid, 256, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dqkv;
+}
+
+}  // namespace pm
+
+PM_DEFINE_ERROR_QUERY(pm_error_norm)

@@ -1,0 +1,12 @@
+// pybind11 module of the PlaceMoE planner cores.
+#include <torch/extension.h>
+
+#include "planner.h"
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "placemoe_b200 planner C++ cores";
+  m.def("accumulate_route_stats", &pmp::accumulate_route_stats, "demand/affinity accumulation for one source rank");
+  m.def("evaluate_routes", &pmp::evaluate_routes, "exact one-level route replay");
+  m.def("optimize_mapping", &pmp::optimize_mapping, "mapping coordinate descent (in place)");
+  m.def("refine_partition", &pmp::refine_partition, "capacity-constrained pairwise exchange (in place)");
+}

@@ -1,0 +1,259 @@
+"""Qwen3-MoE / OLMoE-shaped decoder built from placemoe_b200 ops.
+
+Layer:  h = x + o_proj(attn(qk_norm_rope(qkv_proj(rmsnorm(x)))))
+        y = h + moe(rmsnorm(h))
+
+* Attention projections are one fused QKV weight ``[(Hq + 2 Hkv) D, H]``.
+* The MoE block keeps fp32 master expert weights for the physical slots this
+  rank holds (``gate_up_proj [S, 2I, H]`` with gate rows first, then up rows,
+  and ``down_proj [S, H, I]``) plus bf16 compute copies that the fused AdamW
+  kernel refreshes (``bf16_shadow``).
+* With expert parallelism the block routes through
+  :mod:`placemoe_b200.parallel.ep`; without it through :func:`ops.moe.moe_block`.
+
+CUDA tensors take the sm_100a kernels; CPU tensors take the PyTorch reference
+paths (gloo tests, numerical oracle).
+
+Reference parity: Qwen3MoeDecoderLayer / Qwen3MoeSparseMoeBlock / Qwen3MoeExperts
+(veomni/models/transformers/qwen3_moe/generated/patched_modeling_qwen3_moe_gpu.py:257-378)
+and the OLMoE modeling in veomni/models/transformers/olmoe.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..ops import attention as attn_ops
+from ..ops import gemm as gemm_ops
+from ..ops import loss as loss_ops
+from ..ops import moe as moe_ops
+from ..ops import norm as norm_ops
+from .config import MoEModelConfig, zipf_router_bias
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, dim: int, eps: float):
+        super().__init__()
+        self.weight = nn.Parameter(torch.ones(dim))
+        self.eps = eps
+
+    def forward(self, x):
+        return norm_ops.rmsnorm(x, self.weight, self.eps)
+
+
+class Attention(nn.Module):
+    def __init__(self, cfg: MoEModelConfig):
+        super().__init__()
+        self.cfg = cfg
+        h, d = cfg.hidden_size, cfg.head_dim
+        self.hq, self.hkv, self.d = cfg.num_attention_heads, cfg.num_key_value_heads, d
+        self.qkv_proj = nn.Parameter(torch.empty(cfg.q_size + 2 * cfg.kv_size, h))
+        self.o_proj = nn.Parameter(torch.empty(h, cfg.q_size))
+        if cfg.qk_norm == "per_head":
+            self.q_norm = nn.Parameter(torch.ones(d))
+            self.k_norm = nn.Parameter(torch.ones(d))
+            self.q_group, self.k_group = d, d
+        elif cfg.qk_norm == "full":
+            self.q_norm = nn.Parameter(torch.ones(cfg.q_size))
+            self.k_norm = nn.Parameter(torch.ones(cfg.kv_size))
+            self.q_group, self.k_group = cfg.q_size, cfg.kv_size
+        else:
+            self.q_norm = self.k_norm = None
+            self.q_group = self.k_group = 0
+        self.register_buffer("inv_freq", norm_ops.rope_inv_freq(d, cfg.rope_theta), persistent=False)
+
+    def forward(self, x, pos, seq_len):
+        # x: [T, H] (T = batch * seq_len, packed by sequence)
+        qkv = gemm_ops.linear(x, self.qkv_proj) if x.is_cuda else F.linear(x, self.qkv_proj)
+        q, k, v = norm_ops.qkv_norm_rope(qkv, self.q_norm, self.k_norm, pos, self.inv_freq, self.hq, self.hkv,
+                                         self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps)
+        o = attn_ops.causal_attention(q, k, v, seq_len)  # [T, Hq, D]
+        o = o.reshape(o.shape[0], -1)
+        return gemm_ops.linear(o, self.o_proj) if o.is_cuda else F.linear(o, self.o_proj)
+
+
+class MoEBlock(nn.Module):
+    """Router + experts for the physical slots held by this rank.
+
+    ``placement`` (a :class:`placemoe_b200.parallel.placement.LayerPlacement`)
+    maps logical experts to physical slots; ``ep`` (an
+    :class:`placemoe_b200.parallel.ep.ExpertParallel`) performs the multi-rank
+    dispatch/combine.  Without either, slots == logical experts on one device.
+    """
+
+    def __init__(self, cfg: MoEModelConfig, layer_idx: int, num_local_slots: int | None = None):
+        super().__init__()
+        self.cfg = cfg
+        self.layer_idx = layer_idx
+        h, i, e = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts
+        s = e if num_local_slots is None else num_local_slots
+        self.gate = nn.Parameter(torch.empty(e, h))
+        self.gate_up_proj = nn.Parameter(torch.empty(s, 2 * i, h))
+        self.down_proj = nn.Parameter(torch.empty(s, h, i))
+        seed = layer_idx if cfg.router_bias_seed_per_layer else 0
+        bias = zipf_router_bias(e, cfg.router_bias_zipf_s, cfg.router_bias_scale, seed)
+        self.register_buffer("router_bias", torch.from_numpy(bias), persistent=False)
+        self.placement = None  # set by the placement runtime
+        self.ep = None  # set by parallelize
+        self.layer_key = f"model.layers.{layer_idx}.mlp.experts"
+        self.last_aux_loss = None
+        self.last_route = None  # [T, k] logical routes of the last forward (route capture)
+
+    @property
+    def num_local_slots(self) -> int:
+        return self.gate_up_proj.shape[0]
+
+    # ---------------------------------------------------------------- bf16 copies
+    def compute_weights(self):
+        """bf16 compute copies of the expert weights, refreshed when the masters change."""
+        out = []
+        for p in (self.gate_up_proj, self.down_proj):
+            sh = getattr(p, "bf16_shadow", None)
+            ver = p._version
+            if sh is None or sh.shape != p.shape or sh.device != p.device:
+                sh = p.detach().to(torch.bfloat16)
+                p.bf16_shadow = sh
+                p._shadow_version = ver
+            elif getattr(p, "_shadow_version", None) != ver and not getattr(p, "_shadow_by_optimizer", False):
+                sh.copy_(p.detach())
+                p._shadow_version = ver
+            out.append(sh)
+        return out
+
+    def forward(self, x):
+        cfg = self.cfg
+        t = x.shape[0]
+        bias = self.router_bias if cfg.router_bias_zipf_s else None
+        aux_coef = cfg.router_aux_loss_coef if self.training else 0.0
+        if self.ep is not None:
+            y, aux, route = self.ep.moe_forward(self, x, bias, aux_coef)
+        elif x.is_cuda:
+            w1, w2 = self.compute_weights()
+            lut = self.placement.local_lut_device(x.device) if self.placement is not None else None
+            y, aux, route = moe_ops.moe_block(x, self.gate, bias, w1, w2, self.gate_up_proj, self.down_proj,
+                                              cfg.num_experts_per_tok, cfg.norm_topk_prob, self.num_local_slots,
+                                              lut=lut, aux_coef=aux_coef)
+        else:
+            lut = self.placement.local_lut_cpu() if self.placement is not None else None
+            y, aux = moe_ops.moe_block_reference(x, self.gate, bias, self.gate_up_proj, self.down_proj,
+                                                 cfg.num_experts_per_tok, cfg.norm_topk_prob, aux_coef, lut)
+            route = None
+        self.last_aux_loss = aux
+        self.last_route = route
+        return y
+
+
+class DecoderLayer(nn.Module):
+    def __init__(self, cfg: MoEModelConfig, layer_idx: int, num_local_slots: int | None = None):
+        super().__init__()
+        self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.self_attn = Attention(cfg)
+        self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.mlp = MoEBlock(cfg, layer_idx, num_local_slots)
+
+    def forward(self, x, pos, seq_len):
+        x = x + self.self_attn(self.input_layernorm(x), pos, seq_len)
+        x = x + self.mlp(self.post_attention_layernorm(x))
+        return x
+
+
+class MoEForCausalLM(nn.Module):
+    def __init__(self, cfg: MoEModelConfig, num_local_slots: int | None = None):
+        super().__init__()
+        self.config = cfg
+        self.embed_tokens = nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.layers = nn.ModuleList(DecoderLayer(cfg, i, num_local_slots) for i in range(cfg.num_hidden_layers))
+        self.norm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
+        self.lm_head = None if cfg.tie_word_embeddings else nn.Parameter(torch.empty(cfg.vocab_size, cfg.hidden_size))
+        self.gradient_checkpointing = False
+
+    # ------------------------------------------------------------------ init
+    @torch.no_grad()
+    def init_weights(self, seed: int = 0, expert_init=None):
+        """Random init: N(0, initializer_range) for matrices, ones for norms.
+
+        ``expert_init(layer_idx, name, tensor)`` may fill expert tensors (used to
+        slice logical experts into physical slots consistently across ranks).
+        """
+        g = torch.Generator(device="cpu").manual_seed(seed)
+        std = self.config.initializer_range
+
+        def normal_(t):
+            t.copy_(torch.randn(t.shape, generator=g) * std)
+
+        normal_(self.embed_tokens)
+        if self.lm_head is not None:
+            normal_(self.lm_head)
+        for li, layer in enumerate(self.layers):
+            normal_(layer.self_attn.qkv_proj)
+            normal_(layer.self_attn.o_proj)
+            normal_(layer.mlp.gate)
+            if expert_init is None:
+                normal_(layer.mlp.gate_up_proj)
+                normal_(layer.mlp.down_proj)
+            else:
+                expert_init(li, "gate_up_proj", layer.mlp.gate_up_proj)
+                expert_init(li, "down_proj", layer.mlp.down_proj)
+        return self
+
+    def moe_blocks(self):
+        return [layer.mlp for layer in self.layers]
+
+    def expert_parameters(self):
+        for blk in self.moe_blocks():
+            yield blk.gate_up_proj
+            yield blk.down_proj
+
+    # --------------------------------------------------------------- forward
+    def hidden_states(self, input_ids: torch.Tensor) -> torch.Tensor:
+        b, s = input_ids.shape
+        ids = input_ids.reshape(-1)
+        x = F.embedding(ids, self.embed_tokens)
+        if x.is_cuda:
+            x = x.to(torch.bfloat16)
+        pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)
+        for layer in self.layers:
+            if self.gradient_checkpointing and self.training:
+                x = torch.utils.checkpoint.checkpoint(layer, x, pos, s, use_reentrant=False)
+            else:
+                x = layer(x, pos, s)
+        return self.norm(x)
+
+    def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, loss_denom=None):
+        """Returns (loss, aux_loss) with labels, else logits [B, S, V]."""
+        h = self.hidden_states(input_ids)
+        w = self.embed_tokens if self.lm_head is None else self.lm_head
+        if labels is None:
+            logits = gemm_ops.linear(h, w) if h.is_cuda else F.linear(h, w)
+            return logits.reshape(*input_ids.shape, -1)
+        shifted = torch.full_like(labels, loss_ops.IGNORE_INDEX)
+        shifted[:, :-1] = labels[:, 1:]
+        loss = loss_ops.fused_linear_cross_entropy(h, w, shifted, denom=loss_denom)
+        aux = None
+        for blk in self.moe_blocks():
+            if blk.last_aux_loss is not None:
+                aux = blk.last_aux_loss if aux is None else aux + blk.last_aux_loss
+        return loss, aux
+
+
+def build_model(cfg: MoEModelConfig, num_local_slots: int | None = None, device="cpu", seed: int = 0,
+                expert_init=None) -> MoEForCausalLM:
+    model = MoEForCausalLM(cfg, num_local_slots)
+    model.init_weights(seed, expert_init)
+    return model.to(device)
+
+
+def param_count(model: nn.Module) -> int:
+    return sum(p.numel() for p in model.parameters())
+
+
+def flops_per_token(cfg: MoEModelConfig, seq_len: int) -> float:
+    return cfg.flops_per_token(seq_len)
+
+
+__all__ = ["MoEForCausalLM", "DecoderLayer", "MoEBlock", "Attention", "RMSNorm", "build_model", "param_count",
+           "flops_per_token", "math"]

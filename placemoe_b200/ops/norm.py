@@ -1,0 +1,113 @@
+"""RMSNorm and fused QK-norm + RoPE (``csrc/kernels/norm_rope.cu``).
+
+CPU tensors run the PyTorch reference formulas below; CUDA tensors run the
+sm_100a kernels.  The rotary convention is rotate-half with a fp32
+inverse-frequency table ``theta ** (-2i / head_dim)``.
+
+Reference parity: veomni/ops/liger/__init__.py:52-133 (RMSNorm, RoPE) and the
+Qwen3-MoE / OLMoE attention blocks in veomni/models/transformers/.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import kernels
+
+
+def rmsnorm_reference(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * r * w.float()).to(x.dtype)
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        x2 = x.contiguous()
+        y, rstd = kernels().rmsnorm_fwd(x2, w, eps)
+        ctx.save_for_backward(x2, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+        dx = kernels().rmsnorm_bwd(dy.contiguous().to(torch.bfloat16), x, w, rstd, dw)
+        return dx, dw.to(w.dtype), None
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    if not x.is_cuda:
+        return rmsnorm_reference(x, w, eps)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    return _RMSNorm.apply(x, w, eps)
+
+
+def rope_inv_freq(head_dim: int, theta: float, device=None) -> torch.Tensor:
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32, device=device) / head_dim))
+
+
+def _rotate(x: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    # x: [T, H, D] float
+    ang = pos.float()[:, None] * inv_freq[None, :]
+    c, s = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    half = x.shape[-1] // 2
+    x1, x2 = x[..., :half], x[..., half:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], dim=-1)
+
+
+def qkv_rope_reference(qkv, pos, inv_freq, qw, kw, hq, hkv, d, q_group, k_group, eps):
+    t = qkv.shape[0]
+    x = qkv.float()
+    q = x[:, : hq * d]
+    k = x[:, hq * d: (hq + hkv) * d]
+    v = x[:, (hq + hkv) * d:]
+
+    def norm(z, w, g):
+        if not g:
+            return z
+        zz = z.reshape(t, -1, g)
+        r = torch.rsqrt(zz.pow(2).mean(-1, keepdim=True) + eps)
+        return (zz * r * w.float()).reshape(t, -1)
+
+    q = _rotate(norm(q, qw, q_group).reshape(t, hq, d), pos, inv_freq)
+    k = _rotate(norm(k, kw, k_group).reshape(t, hkv, d), pos, inv_freq)
+    return q.to(qkv.dtype), k.to(qkv.dtype), v.reshape(t, hkv, d).to(qkv.dtype)
+
+
+class _QkvRope(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, qw, kw, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
+        qkv = qkv.contiguous()
+        q, k, v, rq, rk = kernels().qkv_rope_fwd(qkv, pos, inv_freq, qw, kw, hq, hkv, d, q_group, k_group, eps)
+        ctx.save_for_backward(qkv, qw if qw is not None else qkv.new_empty(0), kw if kw is not None else qkv.new_empty(0), pos, inv_freq, rq, rk)
+        ctx.cfg = (hq, hkv, d, q_group, k_group, qw is not None, kw is not None)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, qw, kw, pos, inv_freq, rq, rk = ctx.saved_tensors
+        hq, hkv, d, q_group, k_group, has_q, has_k = ctx.cfg
+        dqw = torch.zeros(qw.shape, device=qkv.device, dtype=torch.float32) if has_q else None
+        dkw = torch.zeros(kw.shape, device=qkv.device, dtype=torch.float32) if has_k else None
+        bf = torch.bfloat16
+        dqkv = kernels().qkv_rope_bwd(
+            dq.contiguous().to(bf), dk.contiguous().to(bf), dv.contiguous().to(bf), qkv, pos, inv_freq,
+            qw if has_q else None, kw if has_k else None, rq, rk, dqw, dkw, hq, hkv, d, q_group, k_group,
+        )
+        return dqkv, dqw, dkw, None, None, None, None, None, None, None, None
+
+
+def qkv_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
+    """Split a fused QKV projection [T, (hq+2hkv)*d] into rotated, normalised q, k and v.
+
+    ``q_group``/``k_group`` are the RMSNorm group sizes (``d`` for per-head
+    norms, the full width for OLMoE-style norms, 0 for none).
+    """
+    if not qkv.is_cuda:
+        return qkv_rope_reference(qkv, pos, inv_freq, q_norm_w, k_norm_w, hq, hkv, d, q_group, k_group, eps)
+    qw = q_norm_w.float() if q_norm_w is not None else None
+    kw = k_norm_w.float() if k_norm_w is not None else None
+    return _QkvRope.apply(qkv.to(torch.bfloat16), qw, kw, pos.to(torch.int32), inv_freq, hq, hkv, d, q_group, k_group, eps)

@@ -1,0 +1,218 @@
+"""Numerics of the memory-bound and attention kernels against fp32 PyTorch references."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
+
+
+def test_rmsnorm_fwd_bwd():
+    from placemoe_b200.ops.norm import rmsnorm, rmsnorm_reference
+
+    torch.manual_seed(0)
+    x = torch.randn(1000, 2048, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(2048, device="cuda")).requires_grad_()
+    y = rmsnorm(x, w, 1e-6)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().clone().requires_grad_()
+    yr = rmsnorm_reference(xr, wr, 1e-6)
+    yr.backward(g.float())
+    assert rel(y, yr) < 1e-2
+    assert rel(x.grad, xr.grad) < 2e-2
+    assert rel(w.grad, wr.grad) < 1e-2
+
+
+@pytest.mark.parametrize("hq,hkv,d,mode", [(16, 16, 128, "full"), (32, 4, 128, "per_head"), (8, 2, 64, "per_head")])
+def test_qkv_norm_rope(hq, hkv, d, mode):
+    from placemoe_b200.ops.norm import qkv_norm_rope, rope_inv_freq
+
+    torch.manual_seed(1)
+    t = 512
+    width = (hq + 2 * hkv) * d
+    qkv = torch.randn(t, width, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    qg, kg = (d, d) if mode == "per_head" else (hq * d, hkv * d)
+    qw = (1 + 0.1 * torch.randn(qg, device="cuda")).requires_grad_()
+    kw = (1 + 0.1 * torch.randn(kg, device="cuda")).requires_grad_()
+    pos = (torch.arange(t, device="cuda") % 256).to(torch.int32)
+    inv = rope_inv_freq(d, 1e6, "cuda")
+    q, k, v = qkv_norm_rope(qkv, qw, kw, pos, inv, hq, hkv, d, qg, kg, 1e-6)
+    gq, gk, gv = torch.randn_like(q), torch.randn_like(k), torch.randn_like(v)
+    (q.float() * gq).sum().add_((k.float() * gk).sum()).add_((v.float() * gv).sum()).backward()
+    qkv_r = qkv.detach().float().requires_grad_()
+    qw_r = qw.detach().clone().requires_grad_()
+    kw_r = kw.detach().clone().requires_grad_()
+    qr, kr, vr = qkv_norm_rope(qkv_r.cpu(), qw_r.cpu(), kw_r.cpu(), pos.cpu(), inv.cpu(), hq, hkv, d, qg, kg, 1e-6)
+    (qr * gq.float().cpu()).sum().add_((kr * gk.float().cpu()).sum()).add_((vr * gv.float().cpu()).sum()).backward()
+    assert rel(q.cpu(), qr) < 1e-2 and rel(k.cpu(), kr) < 1e-2 and rel(v.cpu(), vr) < 1e-2
+    assert rel(qkv.grad.cpu(), qkv_r.grad) < 2e-2
+    assert rel(qw.grad.cpu(), qw_r.grad) < 2e-2
+    assert rel(kw.grad.cpu(), kw_r.grad) < 2e-2
+
+
+@pytest.mark.parametrize("e,k,renorm", [(64, 8, False), (128, 8, True), (16, 4, True)])
+def test_router_topk(e, k, renorm):
+    from placemoe_b200.ops import kernels
+    from placemoe_b200.ops.moe import router_reference
+
+    torch.manual_seed(2)
+    t = 3000
+    logits = torch.randn(t, e, device="cuda")
+    bias = torch.randn(e, device="cuda")
+    idx, w, ps, cnt = kernels().router_topk_fwd(logits, bias, k, renorm)
+    ref = router_reference(logits, bias, k, renorm)
+    assert torch.equal(idx.long().sort(-1).values, ref.idx.long().sort(-1).values)
+    # same order (descending prob) as torch.topk for distinct values
+    assert (w - ref.weight).abs().max().item() < 1e-5
+    assert rel(ps, ref.prob_sum) < 1e-4 and torch.equal(cnt, ref.count)
+    # backward: d(logits) of sum(dw * w) + sum(aux * p)
+    dw = torch.randn(t, k, device="cuda")
+    aux = torch.randn(e, device="cuda") * 0.01
+    dl = kernels().router_topk_bwd(logits, bias, idx, dw, aux, renorm)
+    z = (logits + bias).requires_grad_()
+    p = torch.softmax(z, -1)
+    wsel = p.gather(1, idx.long())
+    if renorm:
+        wsel = wsel / wsel.sum(-1, keepdim=True)
+    ((wsel * dw).sum() + (p * aux).sum()).backward()
+    assert rel(dl, z.grad) < 2e-2
+
+
+def test_moe_plan_and_rows():
+    from placemoe_b200.ops import kernels
+
+    torch.manual_seed(3)
+    t, k, s = 4000, 8, 64
+    idx = torch.randint(0, s, (t, k), device="cuda", dtype=torch.int32)
+    w = torch.rand(t, k, device="cuda")
+    cap = t * k + s * 128
+    offsets, counts, row_of, row_token, row_scale = kernels().moe_plan(idx, None, w, s, cap, 128)
+    off = offsets.cpu()
+    ref_counts = torch.bincount(idx.reshape(-1).long().cpu(), minlength=s)
+    assert torch.equal(counts.cpu().long(), ref_counts)
+    assert all(int(off[i + 1] - off[i]) % 128 == 0 for i in range(s))
+    ro = row_of.cpu().long()
+    flat = idx.reshape(-1).cpu().long()
+    # every assignment lands inside its slot segment, in token order (stable)
+    for e in range(0, s, 7):
+        rows = ro[flat == e]
+        assert bool((rows >= off[e]).all()) and bool((rows < off[e] + ref_counts[e]).all())
+        assert bool((rows[1:] > rows[:-1]).all())
+    assert torch.equal(row_token.cpu().long()[ro], torch.arange(t * k) // k)
+    assert torch.allclose(row_scale.cpu()[ro], w.reshape(-1).cpu())
+    # gather + sum round trip
+    x = torch.randn(t, 256, device="cuda", dtype=torch.bfloat16)
+    xd = torch.empty(cap, 256, device="cuda", dtype=torch.bfloat16)
+    kernels().gather_rows(x, row_token, offsets[s:], xd)
+    out = torch.empty_like(x)
+    kernels().sum_rows(xd, row_of, out)
+    assert rel(out, x.float() * k) < 1e-2
+
+
+@pytest.mark.parametrize("cfg", [(64, 8, False, 2048, 1024), (128, 8, True, 2048, 768), (16, 4, True, 256, 256)])
+def test_moe_block_matches_reference(cfg):
+    from placemoe_b200.ops.moe import moe_block, moe_block_reference
+
+    e, k, renorm, h, inter = cfg
+    torch.manual_seed(4)
+    t = 1024
+    x = torch.randn(t, h, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    wg = (torch.randn(e, h, device="cuda") * 0.02).requires_grad_()
+    bias = torch.randn(e, device="cuda") * 0.5
+    p1 = (torch.randn(e, 2 * inter, h, device="cuda") * 0.02).requires_grad_()
+    p2 = (torch.randn(e, h, inter, device="cuda") * 0.02).requires_grad_()
+    y, aux, _ = moe_block(x, wg, bias, p1.detach().bfloat16(), p2.detach().bfloat16(), p1, p2, k, renorm, e,
+                          aux_coef=0.01)
+    g = torch.randn_like(y)
+    ((y.float() * g.float()).sum() + aux).backward()
+    xr = x.detach().float().requires_grad_()
+    wgr = wg.detach().clone().requires_grad_()
+    p1r = p1.detach().clone().requires_grad_()
+    p2r = p2.detach().clone().requires_grad_()
+    yr, auxr = moe_block_reference(xr, wgr, bias, p1r, p2r, k, renorm, 0.01)
+    ((yr.float() * g.float()).sum() + auxr).backward()
+    assert rel(y, yr) < 3e-2
+    assert abs(aux.item() - auxr.item()) < 1e-4
+    assert rel(x.grad, xr.grad) < 5e-2
+    assert rel(wg.grad, wgr.grad) < 5e-2
+    assert rel(p1.main_grad, p1r.grad) < 5e-2
+    assert rel(p2.main_grad, p2r.grad) < 5e-2
+
+
+def test_fused_adamw_matches_torch():
+    from placemoe_b200.ops.optim import FusedAdamW
+
+    torch.manual_seed(5)
+    ps = [torch.randn(n, device="cuda", requires_grad=True) for n in (1000, 65536 * 3 + 17, 4096)]
+    ref = [p.detach().clone().requires_grad_() for p in ps]
+    shadow = torch.empty(ps[1].shape, device="cuda", dtype=torch.bfloat16)
+    ps[1].bf16_shadow = shadow
+    opt = FusedAdamW(ps, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    topt = torch.optim.AdamW(ref, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    for step in range(3):
+        for p, r in zip(ps, ref):
+            g = torch.randn_like(p)
+            p.grad = g.clone()
+            r.grad = g.clone()
+        opt.step()
+        topt.step()
+    for p, r in zip(ps, ref):
+        assert (p - r).abs().max().item() < 1e-5
+    assert (shadow.float() - ps[1].detach()).abs().max().item() < 1e-2
+
+
+def test_fused_linear_ce():
+    from placemoe_b200.ops.loss import fused_linear_cross_entropy
+
+    torch.manual_seed(6)
+    n, h, v = 3000, 512, 50304
+    x = torch.randn(n, h, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(v, h, device="cuda") * 0.02).to(torch.bfloat16).requires_grad_()
+    lab = torch.randint(0, v, (n,), device="cuda")
+    lab[::7] = -100
+    loss = fused_linear_cross_entropy(x, w, lab, chunk=1024)
+    loss.backward()
+    xr = x.detach().float().requires_grad_()
+    wr = w.detach().float().requires_grad_()
+    lr_ = torch.nn.functional.cross_entropy(xr @ wr.t(), lab, ignore_index=-100)
+    lr_.backward()
+    assert abs(loss.item() - lr_.item()) / lr_.item() < 1e-2
+    assert rel(x.grad, xr.grad) < 3e-2
+    assert rel(w.grad, wr.grad) < 3e-2
+
+
+@pytest.mark.parametrize("b,s,hq,hkv,d", [(1, 128, 1, 1, 128), (2, 512, 4, 2, 128), (1, 1024, 16, 16, 128),
+                                          (2, 256, 8, 2, 64)])
+def test_attention_fwd_bwd(b, s, hq, hkv, d):
+    from placemoe_b200.ops import kernels
+    from placemoe_b200.ops.attention import attention_reference, causal_attention
+
+    assert hasattr(kernels(), "attn_fwd"), "attention kernel must be built in"
+    torch.manual_seed(7)
+    t = b * s
+    q = torch.randn(t, hq, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    k = torch.randn(t, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    v = torch.randn(t, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    o = causal_attention(q, k, v, s)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (z.detach().float().requires_grad_() for z in (q, k, v))
+    orf = attention_reference(qr, kr, vr, s)
+    orf.backward(g.float())
+    assert rel(o, orf) < 2e-2
+    assert rel(q.grad, qr.grad) < 5e-2
+    assert rel(k.grad, kr.grad) < 5e-2
+    assert rel(v.grad, vr.grad) < 5e-2
+    from placemoe_b200.ops import check_device_error
+
+    torch.cuda.synchronize()
+    check_device_error()
+    assert math.isfinite(o.float().sum().item())

@@ -1,0 +1,219 @@
+"""CPU tests of the PlaceMoE planner: invariants, determinism, monotonicity, artifact round-trip."""
+
+import json
+
+import numpy as np
+import pytest
+import torch
+
+from placemoe_b200.placemoe import (
+    LayerPlan,
+    OptimizerConfig,
+    PlaceMoETopology,
+    RouteReplayEvaluator,
+    bounded_group_shortlist,
+    build_placemoe_artifact,
+    candidate_allocations,
+    eplb_plan,
+    fixed_ep_plan,
+    greedy_allocation,
+    identity_plan,
+    initialize_mapping,
+    mirrored_r2_plan,
+    optimize_fixed_layout_mapping,
+    optimize_replica_allocation,
+    profile_route_statistics,
+    project_statistics_to_copies,
+    uniform_copy_statistics,
+    validate_placemoe_artifact,
+)
+from placemoe_b200.placemoe.partition import PartitionConfig, partition_items, partition_objective
+from placemoe_b200.placemoe.routes import load_routes, write_route_bundle
+
+
+def skewed_routes(ep, tokens, experts, k, s=1.0, seed=0, steps=2):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.arange(1, experts + 1, dtype=torch.float64) ** (-s)
+    perm = torch.randperm(experts, generator=g)
+    bias = torch.empty(experts, dtype=torch.float64)
+    bias[perm] = torch.log(w / w.sum())
+    out = []
+    for _ in range(steps):
+        step = []
+        for r in range(ep):
+            logits = torch.randn(tokens, experts, generator=g, dtype=torch.float64) + bias
+            step.append(torch.topk(logits, k, dim=-1).indices)
+        out.append(step)
+    return out
+
+
+def test_statistics_match_bruteforce():
+    routes = skewed_routes(2, 50, 8, 3, steps=1)
+    st = profile_route_statistics(routes, num_experts=8)
+    d = np.zeros((2, 8))
+    a = np.zeros((2, 8, 8))
+    for s, r in enumerate(routes[0]):
+        for row in r.tolist():
+            for i, x in enumerate(row):
+                d[s, x] += 1
+                for y in row[i + 1:]:
+                    a[s, x, y] += 1
+                    a[s, y, x] += 1
+    assert np.array_equal(st.demand, d) and np.array_equal(st.affinity, a)
+
+
+def test_invalid_route_rejected():
+    with pytest.raises(Exception):
+        profile_route_statistics([[torch.tensor([[0, 9]])]], num_experts=4)
+
+
+def test_copy_statistics_preserve_totals():
+    routes = skewed_routes(2, 100, 8, 2, steps=1)
+    st = profile_route_statistics(routes, num_experts=8)
+    c2e = np.array([0, 1, 2, 3, 4, 5, 6, 7, 0, 3])
+    d, a = uniform_copy_statistics(st, c2e)
+    assert np.allclose(d.sum(1), st.demand.sum(1))
+    topo = PlaceMoETopology(2, 2, 8, 5)
+    m = initialize_mapping(st.demand, c2e, topo.slot_ranks(), 2)
+    d2, a2 = project_statistics_to_copies(st, c2e, m)
+    assert np.allclose(d2.sum(1), st.demand.sum(1))
+    assert np.allclose(a2.sum(), st.affinity.sum())
+
+
+def test_bounded_group_shortlist_picks_highest_demand():
+    groups = [np.array([0, 1]), np.array([2, 3]), np.array([4, 5])]
+    demand = np.array([1, 1, 5, 5, 2, 2], dtype=float)
+    best = bounded_group_shortlist(groups, demand, selected_groups=2, candidate_limit=2)
+    assert best[0] == (1, 2)
+
+
+def test_allocations_use_exact_budget():
+    demand = np.array([10, 1, 1, 1, 5, 1, 1, 1], dtype=float)
+    for alloc in candidate_allocations(demand, 4, max_copies=4):
+        assert len(alloc) == 4
+    g = greedy_allocation(demand, 3)
+    assert list(g).count(0) >= 1 and 4 in g
+
+
+def test_partition_respects_capacity_and_uniqueness():
+    rng = np.random.default_rng(0)
+    n = 12
+    a = rng.random((n, n))
+    a = a + a.T
+    np.fill_diagonal(a, 0)
+    d = rng.random(n) * 10
+    item_expert = np.array(list(range(10)) + [0, 1])
+    cfg = PartitionConfig(capacities=(3, 3, 3, 3), ranks_per_group=(1,) * 4, omega=1.0, gamma=0.5)
+    res = partition_items(a, d, item_expert, cfg)
+    assert res and res[0].objective <= res[-1].objective
+    for r in res:
+        assert np.array_equal(np.bincount(r.labels, minlength=4), [3, 3, 3, 3])
+        obj, _, _ = partition_objective(a, d, r.labels, cfg)
+        assert abs(obj - r.objective) < 1e-9
+        for e in (0, 1):
+            assert len(set(r.labels[item_expert == e].tolist())) == 2
+
+
+def test_seed_plans_validate():
+    t8 = PlaceMoETopology(8, 8, 64, 9)
+    fixed_ep_plan(t8).validate(t8)
+    mirrored_r2_plan(PlaceMoETopology(4, 4, 16, 8))
+    demand = np.random.default_rng(1).random((8, 64)) * 100
+    p = eplb_plan(t8, demand)
+    p.validate(t8, additional_copies=8)
+    assert int((p.copy_counts - 1).sum()) == 8
+
+
+def test_evaluator_counts_dedup_and_local_traffic():
+    topo = PlaceMoETopology(2, 2, 4, 2)
+    plan = identity_plan(topo)  # experts 0,1 on rank 0; 2,3 on rank 1
+    routes = [[torch.tensor([[0, 1], [2, 3]]), torch.tensor([[0, 2], [3, 2]])]]
+    ev = RouteReplayEvaluator(routes, topo, hidden_size=4, bytes_per_element=1)
+    c = ev.evaluate(plan)
+    # rank0 token0 local; token1 -> rank1 once (2 assignments); rank1 token0: 0->rank0 once; token1 local
+    assert c.remote_rows == 2 and c.remote_assignments == 3 and c.total_assignments == 8
+    assert c.peak_assignments == 5  # rank0: 3 assignments, rank1: 5
+
+
+def _plan_roundtrip(plan, topo):
+    art = build_placemoe_artifact({"model.layers.0.mlp.experts": plan}, topo)
+    text = json.dumps(art)
+    back = validate_placemoe_artifact(json.loads(text))["model.layers.0.mlp.experts"]
+    assert np.array_equal(back.slot_to_logical, plan.slot_to_logical)
+    assert np.array_equal(back.source_logical_to_physical, plan.source_logical_to_physical)
+    assert np.array_equal(back.owner_slots, plan.owner_slots)
+    assert art["schema_version"] == 2 and art["source"]["algorithm"] == "placemoe-v1"
+
+
+def test_optimizer_beats_baselines_and_is_monotone():
+    ep, e, k = 4, 16, 4
+    topo = PlaceMoETopology(ep, ep, e, e // ep + 1)
+    routes = skewed_routes(ep, 256, e, k, s=1.2, seed=3)
+    st = profile_route_statistics(routes, num_experts=e)
+    ev = RouteReplayEvaluator(routes, topo, hidden_size=256, bytes_per_element=2)
+    res = optimize_replica_allocation(st, topo, ev, OptimizerConfig(rounds=2))
+    best = res.best
+    best.plan.validate(topo, additional_copies=topo.extra_copies)
+    base = ev.evaluate(fixed_ep_plan(topo)).total_ms
+    assert best.cost.total_ms <= base + 1e-9
+    assert all(b <= a + 1e-12 for a, b in zip(res.history, res.history[1:]))
+    _plan_roundtrip(best.plan, topo)
+    # determinism
+    res2 = optimize_replica_allocation(st, topo, ev, OptimizerConfig(rounds=2))
+    assert np.array_equal(res2.best.plan.slot_to_logical, best.plan.slot_to_logical)
+    # mapping-only keeps L and never gets worse than the current M
+    mres = optimize_fixed_layout_mapping(st, topo, best.plan, ev)
+    assert all(np.array_equal(c.plan.slot_to_logical, best.plan.slot_to_logical) for c in mres.candidates)
+    assert mres.best.cost.total_ms <= best.cost.total_ms + 1e-9
+
+
+def test_artifact_validation_rejects_bad_payloads():
+    topo = PlaceMoETopology(2, 2, 4, 3)
+    plan = eplb_plan(topo, np.ones((2, 4)))
+    art = build_placemoe_artifact({"l": plan}, topo)
+    bad = json.loads(json.dumps(art))
+    bad["schema_version"] = 1
+    with pytest.raises(ValueError):
+        validate_placemoe_artifact(bad)
+    bad = json.loads(json.dumps(art))
+    bad["layers"]["l"]["source_logical_to_physical"][0][0] = bad["layers"]["l"]["owner_slots"][1]
+    with pytest.raises(ValueError):
+        validate_placemoe_artifact(bad)
+    bad = json.loads(json.dumps(art))
+    bad["source"]["algorithm"] = "other"
+    with pytest.raises(ValueError):
+        validate_placemoe_artifact(bad)
+
+
+def test_route_bundle_roundtrip(tmp_path):
+    routes = skewed_routes(2, 10, 8, 2, steps=1)[0]
+    write_route_bundle(tmp_path, 3, 1, routes)
+    back = load_routes(tmp_path, steps=(3,), layer=1, ep_size=2)
+    assert len(back) == 1 and all(torch.equal(a, b) for a, b in zip(back[0], routes))
+
+
+def test_planner_cli_end_to_end(tmp_path):
+    from placemoe_b200.placemoe.plan_placemoe import main
+
+    ep, e, k = 2, 8, 2
+    for step, rt in enumerate(skewed_routes(ep, 128, e, k, s=1.1, seed=1, steps=3)):
+        for layer in range(2):
+            write_route_bundle(tmp_path / "routes", step, layer, rt)
+    out = tmp_path / "layout.json"
+    rep = tmp_path / "report.json"
+    assert main(["--route-root", str(tmp_path / "routes"), "--optimize-steps", "0,1", "--validation-steps", "2",
+                 "--layers", "2", "--ep-size", "2", "--num-experts", "8", "--redundant-slots-per-rank", "1",
+                 "--hidden-size", "64", "--output-layout", str(out), "--output-report", str(rep)]) == 0
+    art = json.loads(out.read_text())
+    plans = validate_placemoe_artifact(art)
+    assert set(plans) == {"model.layers.0.mlp.experts", "model.layers.1.mlp.experts"}
+    report = json.loads(rep.read_text())
+    assert report["aggregate"]["validation_speedup"] >= 1.0 - 1e-9
+    # mapping-only update of the produced layout keeps L
+    out2 = tmp_path / "layout2.json"
+    assert main(["--route-root", str(tmp_path / "routes"), "--optimize-steps", "2", "--update-mode", "mapping",
+                 "--input-layout", str(out), "--layers", "2", "--ep-size", "2", "--num-experts", "8",
+                 "--redundant-slots-per-rank", "1", "--hidden-size", "64", "--output-layout", str(out2)]) == 0
+    plans2 = validate_placemoe_artifact(json.loads(out2.read_text()))
+    for key in plans:
+        assert np.array_equal(plans[key].slot_to_logical, plans2[key].slot_to_logical)
