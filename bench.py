@@ -1,0 +1,227 @@
+"""Headline benchmark: MoE training tokens/s (OLMoE-1B-7B shape, FSDP-style DP + EP = world size).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl native|reference] [--model olmoe_1b_7b]
+
+For N > 1 launch with torchrun (one rank per GPU, NCCL).  Per rank: a batch of
+``--batch-per-gpu`` sequences x ``--seq`` tokens of uniform random ids
+(synthetic, seeded), random-init weights of the named architecture, router
+bias 0.5 * log Zipf(s=1.0) redrawn per layer.  A step = forward + backward of
+every micro-batch + replica/DP gradient reduction + grad clipping + AdamW.
+
+Timing: W untimed warm-up steps; then K steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides, timed with CUDA events on the
+launching stream; the max over ranks is reported.  The working set of a step
+(weights, optimizer state, activations: tens of GB) is far larger than the
+126 MB L2, so no separate L2 flush is done.  ``e2e`` repeats the
+measurement through the public Trainer.train_step API with the input copied
+host->device from pinned memory and the loss read back every step.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+BASELINE_METRIC = "MoE train tokens/s (Qwen3-30B-A3B EP8; OLMoE at 1/2/4/8 GPU); exposed a2a ms/step"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=6)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--model", default="olmoe_1b_7b")
+    p.add_argument("--seq", type=int, default=4096)
+    p.add_argument("--batch-per-gpu", type=int, default=8)
+    p.add_argument("--micro-batch", type=int, default=2)
+    p.add_argument("--redundant-slots", type=int, default=0)
+    p.add_argument("--artifact", default="")
+    p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = f"/tmp/pm_clocks_{os.getpid()}.csv"
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+
+        sm = sorted(v for v in (num(r[1]) for r in rows) if v is not None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": num(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max((num(r[3]) or 0) for r in rows)}
+
+
+def run_reference(args):
+    from baseline_reference import run as ref_run  # noqa: E402  (baseline/ helper)
+
+    return ref_run(args)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        try:
+            import baseline_reference
+        except Exception as e:  # pragma: no cover
+            print(json.dumps({"impl": "reference", "unavailable": f"reference harness failed to import: {e}"}))
+            return 0
+        return baseline_reference.main(args)
+
+    import torch
+    import torch.distributed as dist
+
+    from placemoe_b200.data import PinnedBatchPool
+    from placemoe_b200.models.config import get_preset
+    from placemoe_b200.ops import kernels
+    from placemoe_b200.trainer.base import TrainConfig, Trainer, init_distributed
+
+    rank, world = init_distributed()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    overrides = {"num_hidden_layers": args.layers} if args.layers else {}
+    mcfg = get_preset(args.model, **overrides)
+    cfg = TrainConfig(model=args.model, seq_len=args.seq, batch_per_rank=args.batch_per_gpu,
+                      micro_batch_size=args.micro_batch, redundant_slots_per_rank=args.redundant_slots,
+                      placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1)
+    trainer = Trainer(cfg, mcfg)
+    pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank)
+    dev_batches = [b.to("cuda") for b in pool.batches]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        trainer.train_step(next(pool))
+    barrier()
+
+    # ---- device-timed region: inputs already resident, no host reads
+    kn = kernels()
+    kn.reset()
+    kn.counting = True
+    sampler = ClockSampler(local)
+    sampler.start()
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        trainer.train_step(dev_batches[i % len(dev_batches)], read_loss=False)
+    end.record()
+    barrier()
+    clocks = sampler.stop()
+    kn.counting = False
+    launches = kn.launches()
+    ms = start.elapsed_time(end) / args.steps
+
+    # ---- end-to-end through the public API: pinned H2D input + loss D2H every step
+    barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    last = None
+    for i in range(args.steps):
+        last = trainer.train_step(next(pool), read_loss=True)
+    e2.record()
+    barrier()
+    ms_e2e = s2.elapsed_time(e2) / args.steps
+
+    t = torch.tensor([ms, ms_e2e], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = t.tolist()
+    tokens = args.batch_per_gpu * args.seq * world
+    value = tokens / (ms / 1e3)
+    e2e = tokens / (ms_e2e / 1e3)
+    if rank == 0:
+        flops = mcfg.flops_per_token(args.seq) * tokens
+        line = {
+            "metric": "MoE train tokens/s",
+            "value": round(value, 1),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms, 3),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic uniform token ids (seeded), random-init weights",
+            "config": {
+                "model": f"{args.model} ({mcfg.num_hidden_layers}L, H{mcfg.hidden_size}, {mcfg.num_experts}E "
+                         f"top{mcfg.num_experts_per_tok}, I{mcfg.moe_intermediate_size}, V{mcfg.vocab_size})",
+                "global_batch": args.batch_per_gpu * world,
+                "seq_len": args.seq,
+                "micro_batch": args.micro_batch,
+                "parallelism": f"dp{world}+ep{world}",
+                "router_bias": f"{mcfg.router_bias_scale} * log Zipf(s={mcfg.router_bias_zipf_s})",
+                "l2": "working set >> 126 MB L2 (no explicit flush)",
+                "baseline_metric": BASELINE_METRIC,
+            },
+            "clocks": clocks,
+            "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": pool.bytes_per_batch,
+                    "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e, 3), "last_loss": last},
+            "gpu_launches": launches,
+            "model_tflops_per_gpu": round(flops / (ms / 1e3) / world / 1e12, 1),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

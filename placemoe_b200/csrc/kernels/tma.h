@@ -18,7 +18,20 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// Driver-API calls need the primary context current on the calling thread.
+// Autograd's backward threads may not have it yet: cudaSetDevice makes it current.
+inline void ensure_context() {
+  static thread_local bool ready = false;
+  if (!ready) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaSetDevice(dev);
+    ready = true;
+  }
+}
+
 inline EncodeTiledFn encode_tiled_fn() {
+  ensure_context();
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
     void* p = nullptr;

@@ -118,6 +118,19 @@ PRESETS: dict[str, MoEModelConfig] = {
         router_bias_zipf_s=1.1,
         router_bias_scale=0.5,
     ),
+    # small GPU-kernel-compatible shapes (head_dim 128, hidden % 256 == 0) for tests and smoke runs
+    "small_qwen3_moe": MoEModelConfig(
+        model_type="qwen3_moe", vocab_size=4096, hidden_size=1024, num_hidden_layers=2, num_attention_heads=8,
+        num_key_value_heads=2, head_dim=128, moe_intermediate_size=512, num_experts=16, num_experts_per_tok=4,
+        norm_topk_prob=True, rope_theta=1_000_000.0, rms_norm_eps=1e-6, qk_norm="per_head",
+        router_bias_zipf_s=1.0, router_bias_scale=0.5,
+    ),
+    "small_olmoe": MoEModelConfig(
+        model_type="olmoe", vocab_size=4096, hidden_size=1024, num_hidden_layers=2, num_attention_heads=8,
+        num_key_value_heads=8, head_dim=128, moe_intermediate_size=512, num_experts=16, num_experts_per_tok=4,
+        norm_topk_prob=False, rope_theta=10_000.0, rms_norm_eps=1e-5, qk_norm="full", router_aux_loss_coef=0.01,
+        router_bias_zipf_s=1.0, router_bias_scale=0.5, router_bias_seed_per_layer=True,
+    ),
     "olmoe_1b_7b": MoEModelConfig(
         model_type="olmoe",
         vocab_size=50304,

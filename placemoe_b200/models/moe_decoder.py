@@ -28,9 +28,9 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from ..ops import attention as attn_ops
-from ..ops import gemm as gemm_ops
 from ..ops import loss as loss_ops
 from ..ops import moe as moe_ops
+from ..ops import mp as mp_ops
 from ..ops import norm as norm_ops
 from .config import MoEModelConfig, zipf_router_bias
 
@@ -42,7 +42,7 @@ class RMSNorm(nn.Module):
         self.eps = eps
 
     def forward(self, x):
-        return norm_ops.rmsnorm(x, self.weight, self.eps)
+        return mp_ops.rmsnorm(x, self.weight, self.eps)
 
 
 class Attention(nn.Module):
@@ -68,12 +68,12 @@ class Attention(nn.Module):
 
     def forward(self, x, pos, seq_len):
         # x: [T, H] (T = batch * seq_len, packed by sequence)
-        qkv = gemm_ops.linear(x, self.qkv_proj) if x.is_cuda else F.linear(x, self.qkv_proj)
+        qkv = mp_ops.linear(x, self.qkv_proj)
         q, k, v = norm_ops.qkv_norm_rope(qkv, self.q_norm, self.k_norm, pos, self.inv_freq, self.hq, self.hkv,
                                          self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps)
         o = attn_ops.causal_attention(q, k, v, seq_len)  # [T, Hq, D]
         o = o.reshape(o.shape[0], -1)
-        return gemm_ops.linear(o, self.o_proj) if o.is_cuda else F.linear(o, self.o_proj)
+        return mp_ops.linear(o, self.o_proj)
 
 
 class MoEBlock(nn.Module):
@@ -102,6 +102,7 @@ class MoEBlock(nn.Module):
         self.layer_key = f"model.layers.{layer_idx}.mlp.experts"
         self.last_aux_loss = None
         self.last_route = None  # [T, k] logical routes of the last forward (route capture)
+        self.route_sink = None  # RouteRecorder when routes are captured for the planner
 
     @property
     def num_local_slots(self) -> int:
@@ -139,11 +140,13 @@ class MoEBlock(nn.Module):
                                               lut=lut, aux_coef=aux_coef)
         else:
             lut = self.placement.local_lut_cpu() if self.placement is not None else None
-            y, aux = moe_ops.moe_block_reference(x, self.gate, bias, self.gate_up_proj, self.down_proj,
-                                                 cfg.num_experts_per_tok, cfg.norm_topk_prob, aux_coef, lut)
-            route = None
+            y, aux, route = moe_ops.moe_block_reference(x, self.gate, bias, self.gate_up_proj, self.down_proj,
+                                                        cfg.num_experts_per_tok, cfg.norm_topk_prob, aux_coef, lut,
+                                                        return_route=True)
         self.last_aux_loss = aux
         self.last_route = route
+        if self.route_sink is not None and route is not None:
+            self.route_sink.collect(self, route)
         return y
 
 
@@ -174,30 +177,35 @@ class MoEForCausalLM(nn.Module):
     # ------------------------------------------------------------------ init
     @torch.no_grad()
     def init_weights(self, seed: int = 0, expert_init=None):
-        """Random init: N(0, initializer_range) for matrices, ones for norms.
+        """Random init: N(0, initializer_range) for matrices, ones for norms (drawn on the params' device).
 
         ``expert_init(layer_idx, name, tensor)`` may fill expert tensors (used to
         slice logical experts into physical slots consistently across ranks).
         """
-        g = torch.Generator(device="cpu").manual_seed(seed)
         std = self.config.initializer_range
+        gens: dict = {}
 
-        def normal_(t):
-            t.copy_(torch.randn(t.shape, generator=g) * std)
+        def normal_(t, salt):
+            dev = t.device
+            g = torch.Generator(device=dev)
+            g.manual_seed(seed * 1000003 + salt)
+            t.normal_(0.0, std, generator=g)
 
-        normal_(self.embed_tokens)
+        normal_(self.embed_tokens, 1)
         if self.lm_head is not None:
-            normal_(self.lm_head)
+            normal_(self.lm_head, 2)
         for li, layer in enumerate(self.layers):
-            normal_(layer.self_attn.qkv_proj)
-            normal_(layer.self_attn.o_proj)
-            normal_(layer.mlp.gate)
+            base = 16 * (li + 1)
+            normal_(layer.self_attn.qkv_proj, base + 1)
+            normal_(layer.self_attn.o_proj, base + 2)
+            normal_(layer.mlp.gate, base + 3)
             if expert_init is None:
-                normal_(layer.mlp.gate_up_proj)
-                normal_(layer.mlp.down_proj)
+                normal_(layer.mlp.gate_up_proj, base + 4)
+                normal_(layer.mlp.down_proj, base + 5)
             else:
                 expert_init(li, "gate_up_proj", layer.mlp.gate_up_proj)
                 expert_init(li, "down_proj", layer.mlp.down_proj)
+        del gens
         return self
 
     def moe_blocks(self):
@@ -209,12 +217,17 @@ class MoEForCausalLM(nn.Module):
             yield blk.down_proj
 
     # --------------------------------------------------------------- forward
+    def _anchor(self, device):
+        a = getattr(self, "_grad_anchor", None)
+        if a is None or a.device != device:
+            a = torch.zeros((), device=device, requires_grad=True)
+            self._grad_anchor = a
+        return a
+
     def hidden_states(self, input_ids: torch.Tensor) -> torch.Tensor:
         b, s = input_ids.shape
         ids = input_ids.reshape(-1)
-        x = F.embedding(ids, self.embed_tokens)
-        if x.is_cuda:
-            x = x.to(torch.bfloat16)
+        x = mp_ops.embedding(ids, self.embed_tokens, self._anchor(ids.device))
         pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)
         for layer in self.layers:
             if self.gradient_checkpointing and self.training:
@@ -228,7 +241,7 @@ class MoEForCausalLM(nn.Module):
         h = self.hidden_states(input_ids)
         w = self.embed_tokens if self.lm_head is None else self.lm_head
         if labels is None:
-            logits = gemm_ops.linear(h, w) if h.is_cuda else F.linear(h, w)
+            logits = mp_ops.linear(h, w)
             return logits.reshape(*input_ids.shape, -1)
         shifted = torch.full_like(labels, loss_ops.IGNORE_INDEX)
         shifted[:, :-1] = labels[:, 1:]
@@ -242,9 +255,11 @@ class MoEForCausalLM(nn.Module):
 
 def build_model(cfg: MoEModelConfig, num_local_slots: int | None = None, device="cpu", seed: int = 0,
                 expert_init=None) -> MoEForCausalLM:
-    model = MoEForCausalLM(cfg, num_local_slots)
+    """Construct directly on ``device`` (no CPU staging of multi-GB weights) and initialise."""
+    with torch.device(device):
+        model = MoEForCausalLM(cfg, num_local_slots)
     model.init_weights(seed, expert_init)
-    return model.to(device)
+    return model
 
 
 def param_count(model: nn.Module) -> int:

@@ -14,9 +14,40 @@ import functools
 from .. import _build
 
 
+# kernel launches issued by one call of each entry point (for launch accounting)
+LAUNCHES_PER_CALL = {"moe_plan": 4, "attn_bwd": 3}
+
+
+class _CountingModule:
+    """Proxy over the extension module that counts entry-point calls (launch accounting)."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self.calls: dict = {}
+        self.counting = False
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+
+        def wrapped(*args, **kwargs):
+            if self.counting:
+                self.calls[name] = self.calls.get(name, 0) + 1
+            return fn(*args, **kwargs)
+
+        return wrapped
+
+    def launches(self) -> int:
+        return sum(LAUNCHES_PER_CALL.get(k, 1) * v for k, v in self.calls.items() if k != "device_error")
+
+    def reset(self):
+        self.calls = {}
+
+
 @functools.lru_cache(maxsize=1)
 def kernels():
-    return _build.load_kernels()
+    return _CountingModule(_build.load_kernels())
 
 
 def available() -> bool:

@@ -24,8 +24,10 @@ IGNORE_INDEX = -100
 class _FusedLinearCE(torch.autograd.Function):
     @staticmethod
     def forward(ctx, h, w, labels, chunk, denom):
+        from .mp import shadow
+
         h2 = h.reshape(-1, h.shape[-1]).to(torch.bfloat16).contiguous()
-        wb = w.to(torch.bfloat16).contiguous()
+        wb = shadow(w) if w.dtype == torch.float32 else w.to(torch.bfloat16).contiguous()
         n = h2.shape[0]
         labels = labels.reshape(-1).to(torch.int64).contiguous()
         loss_sum = torch.zeros((), device=h.device, dtype=torch.float32)
@@ -41,14 +43,20 @@ class _FusedLinearCE(torch.autograd.Function):
             gemm_tn(logits, h2[s:e], out=dw, accumulate=True)
         ctx.save_for_backward(dh, dw)
         ctx.shape = h.shape
-        ctx.wdtype = w.dtype
+        ctx.master = w
         return loss_sum * scale
 
     @staticmethod
     def backward(ctx, g):
+        from .mp import main_grad
+
         dh, dw = ctx.saved_tensors
         dh = (dh.float() * g).to(torch.bfloat16).reshape(ctx.shape)
-        return dh, (dw * g).to(ctx.wdtype), None, None, None
+        w = ctx.master
+        if w.dtype == torch.float32 and w.requires_grad:
+            main_grad(w).add_(dw * g)
+            return dh, None, None, None, None
+        return dh, (dw * g).to(w.dtype), None, None, None
 
 
 def fused_linear_cross_entropy(h, w, labels, chunk: int = 8192, denom=None):

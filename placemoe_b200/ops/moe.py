@@ -64,7 +64,7 @@ def load_balancing_loss(prob_sum: torch.Tensor, count: torch.Tensor, num_tokens:
     return e * (f * p).sum()
 
 
-def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None):
+def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None, return_route=False):
     """Eager oracle.  x [T, H]; wg [E, H]; w1 [S, 2I, H]; w2 [S, H, I]; lut: logical -> slot."""
     t = x.shape[0]
     logits = x.float() @ wg.float().t()
@@ -88,6 +88,8 @@ def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None):
         count = torch.zeros(p.shape[-1], dtype=torch.float32, device=x.device)
         count.index_add_(0, idx.reshape(-1), torch.ones(idx.numel(), device=x.device))
         aux = aux_coef * load_balancing_loss(p.sum(0), count, t, k)
+    if return_route:
+        return y.to(x.dtype), aux, idx
     return y.to(x.dtype), aux
 
 
@@ -185,12 +187,13 @@ class _ScaleGather(torch.autograd.Function):
     @staticmethod
     def forward(ctx, w, row_scale, row_of):
         ctx.save_for_backward(row_of)
+        ctx.wshape = w.shape
         return row_scale
 
     @staticmethod
     def backward(ctx, dscale):
         (row_of,) = ctx.saved_tensors
-        return kernels().gather_scalar(dscale.contiguous(), row_of), None, None
+        return kernels().gather_scalar(dscale.contiguous(), row_of).view(ctx.wshape), None, None
 
 
 class _Router(torch.autograd.Function):
@@ -250,28 +253,11 @@ def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=N
     xd = _GatherRows.apply(x, row_token, end, row_of, cap)
     yd = ExpertFFN.apply(xd, scale, w1_bf16, w2_bf16, offsets, p1, p2)
     y = _SumRows.apply(yd, row_of, row_token, end, t)
-    return y, aux, (idx, cnt)
-
-
-class _LinearFp32Out(torch.autograd.Function):
-    @staticmethod
-    def forward(ctx, x, w):
-        from .gemm import gemm_nt
-
-        ctx.save_for_backward(x, w)
-        return gemm_nt(x, w, out_dtype=torch.float32)
-
-    @staticmethod
-    def backward(ctx, dl):
-        from .gemm import gemm_nn, gemm_tn
-
-        x, w = ctx.saved_tensors
-        dl = dl.to(torch.bfloat16).contiguous()
-        dx = gemm_nn(dl, w)
-        dw = gemm_tn(dl, x, out_dtype=torch.float32).to(w.dtype)
-        return dx, dw
+    return y, aux, idx
 
 
 def linear_fp32(x, w):
-    """x @ w^T with an fp32 result (router logits)."""
-    return _LinearFp32Out.apply(x.to(torch.bfloat16), w.to(torch.bfloat16))
+    """x @ w^T with an fp32 result (router logits); dW accumulates into w.main_grad."""
+    from .mp import linear
+
+    return linear(x, w, fp32_out=True)

@@ -81,33 +81,47 @@ class _QkvRope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, qw, kw, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
         qkv = qkv.contiguous()
-        q, k, v, rq, rk = kernels().qkv_rope_fwd(qkv, pos, inv_freq, qw, kw, hq, hkv, d, q_group, k_group, eps)
-        ctx.save_for_backward(qkv, qw if qw is not None else qkv.new_empty(0), kw if kw is not None else qkv.new_empty(0), pos, inv_freq, rq, rk)
-        ctx.cfg = (hq, hkv, d, q_group, k_group, qw is not None, kw is not None)
+        qwd = qw.detach() if qw is not None else None
+        kwd = kw.detach() if kw is not None else None
+        q, k, v, rq, rk = kernels().qkv_rope_fwd(qkv, pos, inv_freq, qwd, kwd, hq, hkv, d, q_group, k_group, eps)
+        ctx.save_for_backward(qkv, pos, inv_freq, rq, rk)
+        ctx.masters = (qw, kw)
+        ctx.cfg = (hq, hkv, d, q_group, k_group)
         return q, k, v
 
     @staticmethod
     def backward(ctx, dq, dk, dv):
-        qkv, qw, kw, pos, inv_freq, rq, rk = ctx.saved_tensors
-        hq, hkv, d, q_group, k_group, has_q, has_k = ctx.cfg
-        dqw = torch.zeros(qw.shape, device=qkv.device, dtype=torch.float32) if has_q else None
-        dkw = torch.zeros(kw.shape, device=qkv.device, dtype=torch.float32) if has_k else None
+        from .mp import main_grad
+
+        qkv, pos, inv_freq, rq, rk = ctx.saved_tensors
+        hq, hkv, d, q_group, k_group = ctx.cfg
+        qw, kw = ctx.masters
+
+        def acc(m):
+            if m is None:
+                return None
+            return main_grad(m) if m.requires_grad else torch.zeros(m.shape, device=qkv.device, dtype=torch.float32)
+
         bf = torch.bfloat16
         dqkv = kernels().qkv_rope_bwd(
             dq.contiguous().to(bf), dk.contiguous().to(bf), dv.contiguous().to(bf), qkv, pos, inv_freq,
-            qw if has_q else None, kw if has_k else None, rq, rk, dqw, dkw, hq, hkv, d, q_group, k_group,
+            qw.detach() if qw is not None else None, kw.detach() if kw is not None else None, rq, rk,
+            acc(qw), acc(kw), hq, hkv, d, q_group, k_group,
         )
-        return dqkv, dqw, dkw, None, None, None, None, None, None, None, None
+        return dqkv, None, None, None, None, None, None, None, None, None, None
 
 
 def qkv_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
     """Split a fused QKV projection [T, (hq+2hkv)*d] into rotated, normalised q, k and v.
 
     ``q_group``/``k_group`` are the RMSNorm group sizes (``d`` for per-head
-    norms, the full width for OLMoE-style norms, 0 for none).
+    norms, the full width for OLMoE-style norms, 0 for none).  On CUDA the
+    norm weights are fp32 masters whose gradients accumulate into ``main_grad``.
     """
     if not qkv.is_cuda:
         return qkv_rope_reference(qkv, pos, inv_freq, q_norm_w, k_norm_w, hq, hkv, d, q_group, k_group, eps)
-    qw = q_norm_w.float() if q_norm_w is not None else None
-    kw = k_norm_w.float() if k_norm_w is not None else None
-    return _QkvRope.apply(qkv.to(torch.bfloat16), qw, kw, pos.to(torch.int32), inv_freq, hq, hkv, d, q_group, k_group, eps)
+    for w in (q_norm_w, k_norm_w):
+        if w is not None and w.dtype != torch.float32:
+            raise TypeError("QK-norm weights must be fp32 masters on the CUDA path")
+    return _QkvRope.apply(qkv.to(torch.bfloat16), q_norm_w, k_norm_w, pos.to(torch.int32), inv_freq, hq, hkv, d,
+                          q_group, k_group, eps)

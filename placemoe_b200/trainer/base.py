@@ -1,0 +1,242 @@
+"""Trainer: setup -> build model -> parallelize -> optimizer -> train steps.
+
+Step structure (same order as the reference's BaseTrainer.train_step):
+
+    for each micro-batch: forward (loss / world + aux) -> backward
+    replica-gradient sync (copies of one expert summed)
+    dense gradient reduction (one bucket, one collective)
+    global grad norm (each logical expert counted once) -> clip coefficient on device
+    fused AdamW (clip applied in-kernel, bf16 compute copies rewritten)
+    zero grads -> placement hot update at the step boundary (if configured)
+
+Everything between the input copy and the loss read stays on the device: the
+clip coefficient is a device scalar fed to the optimizer kernel, MoE dispatch
+plans are built by kernels (single GPU), so a step has exactly one host
+synchronisation, the loss read.
+
+Reference parity: veomni/trainer/base.py:239-331 (_setup), :452-535, :695-727
+(forward_backward_step), :755-811 (train_step), :820-863 (train).
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import time
+from dataclasses import dataclass, field
+
+import torch
+import torch.distributed as dist
+
+from ..models.config import MoEModelConfig, get_preset
+from ..models.moe_decoder import build_model
+from ..ops import mp as mp_ops
+from ..ops.optim import FusedAdamW
+from ..parallel.data_parallel import (expert_init_from_full, expert_topology, parallelize_model,
+                                      redundant_slot_weights, sync_replica_gradients)
+from ..placemoe.artifacts import load_artifact
+
+
+@dataclass
+class TrainConfig:
+    model: str = "olmoe_1b_7b"
+    model_overrides: dict = field(default_factory=dict)
+    seq_len: int = 4096
+    batch_per_rank: int = 8  # sequences per rank per step
+    micro_batch_size: int = 2  # sequences per micro-batch
+    lr: float = 3e-4
+    betas: tuple = (0.9, 0.95)
+    eps: float = 1e-8
+    weight_decay: float = 0.1
+    max_grad_norm: float = 1.0
+    warmup_steps: int = 0
+    total_steps: int = 100
+    seed: int = 0
+    redundant_slots_per_rank: int = 0
+    placemoe_artifact: str = ""  # schema-v2 artifact loaded at startup
+    capture_routes: bool = False
+    gradient_checkpointing: bool = False
+    device: str = "cuda"
+    log_interval: int = 10
+    output_dir: str = ""
+    save_steps: int = 0
+
+
+def init_distributed(backend: str | None = None, timeout_s: int = 600):
+    """Initialise torch.distributed from the torchrun environment (no-op for a single process)."""
+    if dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world == 1:
+        return 0, 1
+    from datetime import timedelta
+
+    if backend is None:
+        backend = "nccl" if torch.cuda.is_available() else "gloo"
+    if backend == "nccl":
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    dist.init_process_group(backend=backend, timeout=timedelta(seconds=timeout_s))
+    return dist.get_rank(), dist.get_world_size()
+
+
+class Trainer:
+    def __init__(self, cfg: TrainConfig, model_cfg: MoEModelConfig | None = None):
+        self.cfg = cfg
+        self.rank, self.world = init_distributed()
+        if cfg.device == "cuda":
+            self.device = torch.device("cuda", torch.cuda.current_device() if torch.cuda.is_available() else 0)
+        else:
+            self.device = torch.device(cfg.device)
+        self.model_cfg = model_cfg or get_preset(cfg.model, **cfg.model_overrides)
+        plans = None
+        topology = expert_topology(self.model_cfg.num_experts, self.world, cfg.redundant_slots_per_rank)
+        if cfg.placemoe_artifact:
+            _, topology, plans = load_artifact(cfg.placemoe_artifact)
+            if topology.ep_size != self.world or topology.num_experts != self.model_cfg.num_experts:
+                raise ValueError("PlaceMoE artifact topology does not match the run")
+        self.topology = topology
+        init = expert_init_from_full(self.model_cfg, topology, plans, self.rank, cfg.seed)
+        self.model = build_model(self.model_cfg, topology.slots_per_rank, self.device, cfg.seed, init)
+        self.model.gradient_checkpointing = cfg.gradient_checkpointing
+        self.model.train()
+        self.pstate = parallelize_model(self.model, plans=plans, topology=topology, device=self.device,
+                                        capture_routes=cfg.capture_routes)
+        self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                    weight_decay=cfg.weight_decay)
+        self._norm_table = None
+        self.global_step = 0
+        self.hot_update = None  # set by placement runtime (hot updates)
+        self.metrics: dict = {}
+
+    # ------------------------------------------------------------------ utils
+    def lr_at(self, step: int) -> float:
+        c = self.cfg
+        if c.warmup_steps and step < c.warmup_steps:
+            return c.lr * (step + 1) / c.warmup_steps
+        prog = min(1.0, (step - c.warmup_steps) / max(1, c.total_steps - c.warmup_steps))
+        return c.lr * (0.1 + 0.9 * 0.5 * (1 + math.cos(math.pi * prog)))
+
+    def _grad_sq_norm(self) -> torch.Tensor:
+        """Squared global grad norm (device scalar); redundant expert copies are excluded."""
+        kn = mp_ops.kernels()
+        if self._norm_table is None:
+            grads, weights = [], []
+            for blk in self.model.moe_blocks():
+                w = redundant_slot_weights(blk, blk.placement)
+                for p in (blk.gate_up_proj, blk.down_proj):
+                    mg = mp_ops.main_grad(p)
+                    for j in range(p.shape[0]):
+                        grads.append(mg[j])
+                        weights.append(w[j])
+            if self.pstate.dense_bucket is not None:
+                grads.append(self.pstate.dense_bucket.flat)
+                weights.append(1.0)
+            self._norm_table = kn.sq_norm_build_table(grads, weights)
+        out = torch.zeros((), device=self.device, dtype=torch.float32)
+        kn.sq_norm(self._norm_table[0], self._norm_table[1], out)
+        if self.world > 1:
+            # dense part is replicated (counted once per rank) -> subtract (world-1) copies
+            dense = self.pstate.dense_bucket.flat
+            dsq = dense.float().pow(2).sum()
+            out = out - dsq
+            dist.all_reduce(out)
+            out = out + dsq
+        return out
+
+    # ------------------------------------------------------------------- step
+    def forward_backward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        loss, aux = self.model(input_ids, labels=input_ids)
+        total = loss / self.world
+        if aux is not None:
+            total = total + aux / self.world
+        total.backward()
+        return loss.detach()
+
+    def train_step(self, input_ids: torch.Tensor, *, read_loss: bool = True):
+        """One optimizer step over ``input_ids`` [batch_per_rank, seq] (host or device tensor)."""
+        cfg = self.cfg
+        ids = input_ids.to(self.device, non_blocking=True)
+        mb = max(1, cfg.micro_batch_size)
+        n_micro = max(1, ids.shape[0] // mb)
+        losses = []
+        for i in range(n_micro):
+            losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+        loss = torch.stack(losses).mean()
+        self.optimizer_step()
+        self.global_step += 1
+        if self.hot_update is not None:
+            self.hot_update.on_step_end(self)
+        return float(loss.item()) if read_loss else loss
+
+    def optimizer_step(self):
+        cfg = self.cfg
+        # gradients of micro-batches were accumulated; average them
+        nmb = max(1, cfg.batch_per_rank // max(1, cfg.micro_batch_size))
+        if self.world > 1:
+            sync_replica_gradients(self.model, self.pstate.placements)
+            if self.pstate.dense_bucket is not None:
+                self.pstate.dense_bucket.reduce()
+        if self.device.type == "cuda":
+            sq = self._grad_sq_norm()
+            norm = sq.sqrt() / nmb
+            clip = torch.clamp(cfg.max_grad_norm / (norm + 1e-6), max=1.0) if cfg.max_grad_norm > 0 else \
+                torch.ones((), device=self.device)
+            self.optimizer.grad_scale = (clip / nmb).reshape(1).contiguous()
+            self.metrics["grad_norm"] = norm
+        else:
+            from ..parallel.data_parallel import is_expert_param
+
+            for p in self.model.parameters():
+                if p.grad is not None:
+                    p.grad.div_(nmb)
+            if self.world > 1:
+                for n, p in self.model.named_parameters():
+                    if p.grad is not None and not is_expert_param(n):
+                        dist.all_reduce(p.grad)
+            if cfg.max_grad_norm > 0:
+                # global norm: dense once, each logical expert once (owner copies)
+                dense_sq = sum(p.grad.double().pow(2).sum() for n, p in self.model.named_parameters()
+                               if p.grad is not None and not is_expert_param(n))
+                exp_sq = torch.zeros((), dtype=torch.float64)
+                for blk in self.model.moe_blocks():
+                    w = redundant_slot_weights(blk, blk.placement)
+                    for p in (blk.gate_up_proj, blk.down_proj):
+                        if p.grad is not None:
+                            per = p.grad.double().pow(2).flatten(1).sum(1)
+                            exp_sq = exp_sq + (per * torch.tensor(w, dtype=torch.float64)).sum()
+                if self.world > 1:
+                    dist.all_reduce(exp_sq)
+                norm = float((dense_sq + exp_sq).sqrt())
+                self.metrics["grad_norm"] = norm
+                coef = min(1.0, cfg.max_grad_norm / (norm + 1e-6))
+                if coef < 1.0:
+                    for p in self.model.parameters():
+                        if p.grad is not None:
+                            p.grad.mul_(coef)
+        for g in self.optimizer.param_groups:
+            g["lr"] = self.lr_at(self.global_step)
+        self.optimizer.step()
+        self.zero_grad()
+
+    def zero_grad(self):
+        for p in self.model.parameters():
+            p.grad = None
+            g = getattr(p, "main_grad", None)
+            if g is not None and self.pstate.dense_bucket is None:
+                g.zero_()
+        if self.pstate.dense_bucket is not None:
+            self.pstate.dense_bucket.zero()
+            for p in self.model.expert_parameters():
+                g = getattr(p, "main_grad", None)
+                if g is not None:
+                    g.zero_()
+
+    def train(self, data_iter, steps: int | None = None, log=print):
+        steps = steps or self.cfg.total_steps
+        t0 = time.perf_counter()
+        for s in range(steps):
+            batch = next(data_iter)
+            loss = self.train_step(batch)
+            if self.rank == 0 and log and (s % max(1, self.cfg.log_interval) == 0 or s == steps - 1):
+                log(f"step {self.global_step} loss {loss:.4f} ({time.perf_counter() - t0:.1f}s)")
+        return self

@@ -11,7 +11,8 @@ def _ref(a, b):
 
 
 def _close(out, ref, tol=2e-2):
-    err = (out.float() - ref).abs().max().item()
+    out, ref = out.detach().float().cpu(), ref.detach().float().cpu()
+    err = (out - ref).abs().max().item()
     scale = ref.abs().max().item() + 1e-6
     assert err / scale < tol, f"relative error {err / scale:.3e}"
 

@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 
 
 def rel(a, b):
-    a, b = a.float(), b.float()
+    a, b = a.detach().float().cpu(), b.detach().float().cpu()
     return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
 
 
@@ -54,8 +54,8 @@ def test_qkv_norm_rope(hq, hkv, d, mode):
     (qr * gq.float().cpu()).sum().add_((kr * gk.float().cpu()).sum()).add_((vr * gv.float().cpu()).sum()).backward()
     assert rel(q.cpu(), qr) < 1e-2 and rel(k.cpu(), kr) < 1e-2 and rel(v.cpu(), vr) < 1e-2
     assert rel(qkv.grad.cpu(), qkv_r.grad) < 2e-2
-    assert rel(qw.grad.cpu(), qw_r.grad) < 2e-2
-    assert rel(kw.grad.cpu(), kw_r.grad) < 2e-2
+    assert rel(qw.main_grad.cpu(), qw_r.grad) < 2e-2
+    assert rel(kw.main_grad.cpu(), kw_r.grad) < 2e-2
 
 
 @pytest.mark.parametrize("e,k,renorm", [(64, 8, False), (128, 8, True), (16, 4, True)])
@@ -142,7 +142,7 @@ def test_moe_block_matches_reference(cfg):
     assert rel(y, yr) < 3e-2
     assert abs(aux.item() - auxr.item()) < 1e-4
     assert rel(x.grad, xr.grad) < 5e-2
-    assert rel(wg.grad, wgr.grad) < 5e-2
+    assert rel(wg.main_grad, wgr.grad) < 5e-2
     assert rel(p1.main_grad, p1r.grad) < 5e-2
     assert rel(p2.main_grad, p2r.grad) < 5e-2
 
@@ -166,7 +166,7 @@ def test_fused_adamw_matches_torch():
         topt.step()
     for p, r in zip(ps, ref):
         assert (p - r).abs().max().item() < 1e-5
-    assert (shadow.float() - ps[1].detach()).abs().max().item() < 1e-2
+    assert torch.equal(shadow, ps[1].detach().to(torch.bfloat16))
 
 
 def test_fused_linear_ce():
