@@ -516,6 +516,8 @@ static CUtensorMap head_map(const torch::Tensor& t) {
 static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t S) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q [T,Hq,D] bf16");
   TORCH_CHECK(k.sizes() == v.sizes() && k.is_contiguous() && v.is_contiguous(), "k/v layout");
+  PM_CHECK_CUDA(k); PM_CHECK_CUDA(v);
+  TORCH_CHECK(k.scalar_type() == torch::kBFloat16 && v.scalar_type() == torch::kBFloat16, "k/v bf16");
   TORCH_CHECK(k.size(0) == q.size(0) && k.size(2) == q.size(2), "k/v shape");
   TORCH_CHECK(q.size(1) % k.size(1) == 0, "Hq must be a multiple of Hkv");
   TORCH_CHECK(S % kTile == 0 && q.size(0) % S == 0, "seq_len must be a multiple of 128 and divide T");
@@ -560,6 +562,8 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
                                     torch::Tensor lse, torch::Tensor dout, int64_t S) {
   check_qkv(q, k, v, S);
   TORCH_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes() && o.sizes() == q.sizes(), "dout / o layout");
+  PM_CHECK_CUDA(o); PM_CHECK_CUDA(lse); PM_CHECK_CUDA(dout);
+  TORCH_CHECK(lse.scalar_type() == torch::kFloat32 && lse.numel() == q.size(0) * q.size(1), "lse [Hq, T] fp32");
   c10::cuda::CUDAGuard guard(q.device());
   const int T = (int)q.size(0), Hq = (int)q.size(1), Hkv = (int)k.size(1), D = (int)q.size(2);
   auto dq = torch::empty_like(q);

@@ -15,6 +15,12 @@
 
 #define PM_DEVICE __device__ __forceinline__
 
+// Every tensor handed to a kernel must live on the current CUDA device.
+#define PM_CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor (got ", (t).device(), ")")
+#define PM_CHECK_CUDA_OPT(t) \
+  do { if ((t).has_value()) TORCH_CHECK((t)->is_cuda(), #t " must be a CUDA tensor (got ", (t)->device(), ")"); } while (0)
+
+
 namespace pm {
 
 // Error word of this translation unit (each .cu file has its own copy; the

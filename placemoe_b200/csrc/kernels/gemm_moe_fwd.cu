@@ -1,0 +1,73 @@
+// tcgen05 GEMM entry points: expert-grouped forward / data-gradient GEMMs.
+// The kernel template, tile scheduler and epilogues are in gemm_sm100.cuh.
+#include "gemm_sm100.cuh"
+
+namespace pm {
+
+// Expert fc1 forward: h[rows, I] = scale[row] * silu(x W1_gate^T) * (x W1_up^T)
+// x: [rows, H] dispatched tokens, expert segments at group_offsets (multiples of 128).
+// w1: [E, 2I, H] (gate rows first, then up rows).  gu_out (optional): [rows, 2I].
+void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
+                    c10::optional<torch::Tensor> gu_out) {
+  check_bf16_2d(x, "x");
+  TORCH_CHECK(w1.dim() == 3 && w1.is_contiguous() && w1.scalar_type() == torch::kBFloat16, "w1 must be [E,2I,H] bf16");
+  const int64_t E = w1.size(0), I2 = w1.size(1), H = w1.size(2);
+  const int64_t I = I2 / 2;
+  TORCH_CHECK(x.size(1) == H, "x/w1 hidden mismatch");
+  TORCH_CHECK(I % 128 == 0, "moe intermediate size must be a multiple of 128");
+  TORCH_CHECK(E <= kMaxGroups, "too many experts");
+  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == E + 1, "offsets must be int32 [E+1]");
+  TORCH_CHECK(h.size(0) == x.size(0) && h.size(1) == I && h.stride(1) == 1, "h shape");
+  PM_CHECK_CUDA(w1); PM_CHECK_CUDA(offsets); PM_CHECK_CUDA(scale); PM_CHECK_CUDA(h); PM_CHECK_CUDA_OPT(gu_out);
+  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && scale.numel() >= x.size(0), "scale must be fp32 [rows]");
+  c10::cuda::CUDAGuard guard(x.device());
+  GemmArgs args = blank_args();
+  args.M = (int)x.size(0); args.N = (int)I2; args.K = (int)H; args.num_groups = (int)E;
+  args.group_offsets = offsets.data_ptr<int>();
+  args.D = h.data_ptr(); args.ldd = h.stride(0);
+  args.row_scale = scale.data_ptr<float>();
+  args.inter = (int)I;
+  if (gu_out.has_value()) {
+    check_bf16_2d(*gu_out, "gu_out");
+    args.aux_out = reinterpret_cast<__nv_bfloat16*>(gu_out->data_ptr());
+    args.ld_aux_out = gu_out->stride(0);
+  }
+  CUtensorMap ta = make_tmap_2d_bf16(x.data_ptr(), x.size(0), H, x.stride(0), 64, 128);
+  CUtensorMap tb = make_tmap_3d_bf16(w1.data_ptr(), E, I2, H, H, I2 * H, 64, 128);
+  const int ub = (int)((x.size(0) / BM) * (I / 128));
+  const int grid = std::max(1, std::min(ub, num_sms()));
+  launch<256, false, false, kGroupM, kSwiGLU, true>(ta, tb, args, grid);
+}
+
+// Expert GEMM with per-expert B, grouped over rows of A.
+//   b_mn = false: out[rows, N] = a[rows, K] . w[e]^T, w: [E, N, K]  (fc2 forward)
+//   b_mn = true : out[rows, N] = a[rows, K] . w[e],   w: [E, K, N]  (data gradients)
+void moe_grouped_gemm(torch::Tensor a, torch::Tensor w, torch::Tensor offsets, torch::Tensor out, bool b_mn) {
+  check_bf16_2d(a, "a");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(out.scalar_type() == torch::kBFloat16, "out must be bf16");
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == torch::kBFloat16, "w must be 3-D bf16");
+  const int64_t E = w.size(0);
+  const int64_t N = b_mn ? w.size(2) : w.size(1);
+  const int64_t K = b_mn ? w.size(1) : w.size(2);
+  TORCH_CHECK(a.size(1) == K && out.size(1) == N && out.size(0) == a.size(0), "shape mismatch");
+  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8");
+  TORCH_CHECK(E <= kMaxGroups && offsets.numel() == E + 1 && offsets.scalar_type() == torch::kInt32, "offsets");
+  PM_CHECK_CUDA(w); PM_CHECK_CUDA(offsets);
+  c10::cuda::CUDAGuard guard(a.device());
+  GemmArgs args = blank_args();
+  args.M = (int)a.size(0); args.N = (int)N; args.K = (int)K; args.num_groups = (int)E;
+  args.group_offsets = offsets.data_ptr<int>();
+  args.D = out.data_ptr(); args.ldd = out.stride(0);
+  CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), K, a.stride(0), 64, 128);
+  CUtensorMap tb = b_mn ? make_tmap_3d_bf16(w.data_ptr(), E, K, N, N, K * N, 64, 64)
+                        : make_tmap_3d_bf16(w.data_ptr(), E, N, K, K, K * N, 64, 256);
+  const int ub = (int)((a.size(0) / BM) * ((N + 255) / 256));
+  const int grid = std::max(1, std::min(ub, num_sms()));
+  if (b_mn) launch<256, false, true, kGroupM, kStoreBF16, false>(ta, tb, args, grid);
+  else launch<256, false, false, kGroupM, kStoreBF16, false>(ta, tb, args, grid);
+}
+
+}  // namespace pm
+
+PM_DEFINE_ERROR_QUERY(pm_error_gemm_moe_fwd)

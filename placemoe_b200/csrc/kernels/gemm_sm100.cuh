@@ -29,6 +29,7 @@
 // veomni/ops/kernels/moe/_kernels/kernel/group_gemm.py:79 (same_nk) and :265
 // (same_mn) and the EPGroupGemm autograd of
 // veomni/distributed/moe/moe_layer.py:147.
+#pragma once
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -402,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Host side
 // --------------------------------------------------------------------------
 
-static int num_sms() {
+static inline int num_sms() {
   static int n = 0;
   if (!n) {
     int dev;
@@ -426,7 +427,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-static void check_bf16_2d(const torch::Tensor& t, const char* name) {
+static inline void check_bf16_2d(const torch::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.scalar_type() == torch::kBFloat16, name, " must be bf16");
   TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
@@ -435,185 +436,10 @@ static void check_bf16_2d(const torch::Tensor& t, const char* name) {
   TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name, " must be 16-byte aligned");
 }
 
-static GemmArgs blank_args() {
+static inline GemmArgs blank_args() {
   GemmArgs a;
   memset(&a, 0, sizeof(a));
   return a;
 }
 
-// out[M, N] (bf16 or fp32) = A . B^T with the layouts described at the top.
-// accumulate: only for fp32 outputs (out += result).
-void dense_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate) {
-  check_bf16_2d(a, "a");
-  check_bf16_2d(b, "b");
-  TORCH_CHECK(out.is_cuda() && out.dim() == 2 && out.stride(1) == 1, "out must be a 2-D CUDA tensor");
-  const int64_t M = a_mn ? a.size(1) : a.size(0);
-  const int64_t K = a_mn ? a.size(0) : a.size(1);
-  const int64_t N = b_mn ? b.size(1) : b.size(0);
-  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
-  TORCH_CHECK(K == Kb, "contraction sizes differ: ", K, " vs ", Kb);
-  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "out has the wrong shape");
-  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8");
-  if (M == 0 || N == 0) return;
-  const bool f32 = out.scalar_type() == torch::kFloat32;
-  TORCH_CHECK(f32 || out.scalar_type() == torch::kBFloat16, "out must be bf16 or fp32");
-  TORCH_CHECK(!accumulate || f32, "accumulate requires an fp32 output");
-  c10::cuda::CUDAGuard guard(a.device());
-  if (K == 0) {
-    if (!accumulate) out.zero_();
-    return;
-  }
-  GemmArgs args = blank_args();
-  args.M = (int)M; args.N = (int)N; args.K = (int)K;
-  args.D = out.data_ptr(); args.ldd = out.stride(0); args.beta = accumulate ? 1.f : 0.f;
-
-  // BN = 64 for narrow outputs (router logits), 256 otherwise.
-  const bool narrow = N <= 64;
-  const int BN = narrow ? 64 : 256;
-  CUtensorMap ta = a_mn ? make_tmap_2d_bf16(a.data_ptr(), K, M, a.stride(0), 64, 64)
-                        : make_tmap_2d_bf16(a.data_ptr(), M, K, a.stride(0), 64, 128);
-  CUtensorMap tb = b_mn ? make_tmap_2d_bf16(b.data_ptr(), K, N, b.stride(0), 64, 64)
-                        : make_tmap_2d_bf16(b.data_ptr(), N, K, b.stride(0), 64, BN);
-  const int tiles = (int)(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
-  const int grid = std::min(tiles, num_sms());
-  if (narrow) {
-    TORCH_CHECK(!a_mn && !b_mn, "narrow GEMM supports the forward layout only");
-    if (f32) launch<64, false, false, kGroupNone, kStoreF32, false>(ta, tb, args, grid);
-    else launch<64, false, false, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
-    return;
-  }
-  if (!a_mn && !b_mn) {
-    if (f32) launch<256, false, false, kGroupNone, kStoreF32, false>(ta, tb, args, grid);
-    else launch<256, false, false, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
-  } else if (!a_mn && b_mn) {
-    TORCH_CHECK(!f32, "dgrad layout produces bf16");
-    launch<256, false, true, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
-  } else if (a_mn && b_mn) {
-    if (f32) launch<256, true, true, kGroupNone, kAccumF32, false>(ta, tb, args, grid);
-    else launch<256, true, true, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
-  } else {
-    TORCH_CHECK(false, "unsupported layout combination (a MN-major with b K-major)");
-  }
-}
-
-// Expert fc1 forward: h[rows, I] = scale[row] * silu(x W1_gate^T) * (x W1_up^T)
-// x: [rows, H] dispatched tokens, expert segments at group_offsets (multiples of 128).
-// w1: [E, 2I, H] (gate rows first, then up rows).  gu_out (optional): [rows, 2I].
-void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
-                    c10::optional<torch::Tensor> gu_out) {
-  check_bf16_2d(x, "x");
-  TORCH_CHECK(w1.dim() == 3 && w1.is_contiguous() && w1.scalar_type() == torch::kBFloat16, "w1 must be [E,2I,H] bf16");
-  const int64_t E = w1.size(0), I2 = w1.size(1), H = w1.size(2);
-  const int64_t I = I2 / 2;
-  TORCH_CHECK(x.size(1) == H, "x/w1 hidden mismatch");
-  TORCH_CHECK(I % 128 == 0, "moe intermediate size must be a multiple of 128");
-  TORCH_CHECK(E <= kMaxGroups, "too many experts");
-  TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == E + 1, "offsets must be int32 [E+1]");
-  TORCH_CHECK(h.size(0) == x.size(0) && h.size(1) == I && h.stride(1) == 1, "h shape");
-  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && scale.numel() >= x.size(0), "scale must be fp32 [rows]");
-  c10::cuda::CUDAGuard guard(x.device());
-  GemmArgs args = blank_args();
-  args.M = (int)x.size(0); args.N = (int)I2; args.K = (int)H; args.num_groups = (int)E;
-  args.group_offsets = offsets.data_ptr<int>();
-  args.D = h.data_ptr(); args.ldd = h.stride(0);
-  args.row_scale = scale.data_ptr<float>();
-  args.inter = (int)I;
-  if (gu_out.has_value()) {
-    check_bf16_2d(*gu_out, "gu_out");
-    args.aux_out = reinterpret_cast<__nv_bfloat16*>(gu_out->data_ptr());
-    args.ld_aux_out = gu_out->stride(0);
-  }
-  CUtensorMap ta = make_tmap_2d_bf16(x.data_ptr(), x.size(0), H, x.stride(0), 64, 128);
-  CUtensorMap tb = make_tmap_3d_bf16(w1.data_ptr(), E, I2, H, H, I2 * H, 64, 128);
-  const int ub = (int)((x.size(0) / BM) * (I / 128));
-  const int grid = std::max(1, std::min(ub, num_sms()));
-  launch<256, false, false, kGroupM, kSwiGLU, true>(ta, tb, args, grid);
-}
-
-// Expert GEMM with per-expert B, grouped over rows of A.
-//   b_mn = false: out[rows, N] = a[rows, K] . w[e]^T, w: [E, N, K]  (fc2 forward)
-//   b_mn = true : out[rows, N] = a[rows, K] . w[e],   w: [E, K, N]  (data gradients)
-void moe_grouped_gemm(torch::Tensor a, torch::Tensor w, torch::Tensor offsets, torch::Tensor out, bool b_mn) {
-  check_bf16_2d(a, "a");
-  check_bf16_2d(out, "out");
-  TORCH_CHECK(out.scalar_type() == torch::kBFloat16, "out must be bf16");
-  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == torch::kBFloat16, "w must be 3-D bf16");
-  const int64_t E = w.size(0);
-  const int64_t N = b_mn ? w.size(2) : w.size(1);
-  const int64_t K = b_mn ? w.size(1) : w.size(2);
-  TORCH_CHECK(a.size(1) == K && out.size(1) == N && out.size(0) == a.size(0), "shape mismatch");
-  TORCH_CHECK(N % 8 == 0, "N must be a multiple of 8");
-  TORCH_CHECK(E <= kMaxGroups && offsets.numel() == E + 1 && offsets.scalar_type() == torch::kInt32, "offsets");
-  c10::cuda::CUDAGuard guard(a.device());
-  GemmArgs args = blank_args();
-  args.M = (int)a.size(0); args.N = (int)N; args.K = (int)K; args.num_groups = (int)E;
-  args.group_offsets = offsets.data_ptr<int>();
-  args.D = out.data_ptr(); args.ldd = out.stride(0);
-  CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), K, a.stride(0), 64, 128);
-  CUtensorMap tb = b_mn ? make_tmap_3d_bf16(w.data_ptr(), E, K, N, N, K * N, 64, 64)
-                        : make_tmap_3d_bf16(w.data_ptr(), E, N, K, K, K * N, 64, 256);
-  const int ub = (int)((a.size(0) / BM) * ((N + 255) / 256));
-  const int grid = std::max(1, std::min(ub, num_sms()));
-  if (b_mn) launch<256, false, true, kGroupM, kStoreBF16, false>(ta, tb, args, grid);
-  else launch<256, false, false, kGroupM, kStoreBF16, false>(ta, tb, args, grid);
-}
-
-// Expert fc2 data gradient fused with the SwiGLU backward:
-//   dh_raw = dy[rows, H] . W2[e]  (W2: [E, H, I])
-//   dgu[rows, 2I] = d(gate|up) of h = scale * silu(g) * u, using the saved gu
-//   dscale[row] += sum_j silu(g) u dh_raw
-void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor offsets, torch::Tensor gu,
-                           torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale) {
-  check_bf16_2d(dy, "dy");
-  check_bf16_2d(gu, "gu");
-  check_bf16_2d(dgu, "dgu");
-  TORCH_CHECK(w2.dim() == 3 && w2.is_contiguous() && w2.scalar_type() == torch::kBFloat16, "w2 must be [E,H,I]");
-  const int64_t E = w2.size(0), H = w2.size(1), I = w2.size(2);
-  TORCH_CHECK(dy.size(1) == H && gu.size(1) == 2 * I && dgu.size(1) == 2 * I, "shape mismatch");
-  TORCH_CHECK(I % 128 == 0, "moe intermediate size must be a multiple of 128");
-  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && dscale.scalar_type() == torch::kFloat32, "fp32 scales");
-  c10::cuda::CUDAGuard guard(dy.device());
-  GemmArgs args = blank_args();
-  args.M = (int)dy.size(0); args.N = (int)I; args.K = (int)H; args.num_groups = (int)E;
-  args.group_offsets = offsets.data_ptr<int>();
-  args.row_scale = scale.data_ptr<float>();
-  args.aux = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()); args.ld_aux = gu.stride(0);
-  args.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()); args.ld_aux_out = dgu.stride(0);
-  args.row_grad = dscale.data_ptr<float>();
-  args.inter = (int)I;
-  CUtensorMap ta = make_tmap_2d_bf16(dy.data_ptr(), dy.size(0), H, dy.stride(0), 64, 128);
-  CUtensorMap tb = make_tmap_3d_bf16(w2.data_ptr(), E, H, I, I, H * I, 64, 64);
-  if (I % 256 == 0) {
-    const int ub = (int)((dy.size(0) / BM) * (I / 256));
-    launch<256, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())));
-  } else {
-    const int ub = (int)((dy.size(0) / BM) * (I / 128));
-    launch<128, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())));
-  }
-}
-
-// Expert weight gradient: dw[e] (+)= a[seg_e]^T . b[seg_e]
-//   a: [rows, M] (e.g. dY), b: [rows, N] (e.g. h); dw: [E, M, N] fp32.
-void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate) {
-  check_bf16_2d(a, "a");
-  check_bf16_2d(b, "b");
-  TORCH_CHECK(dw.dim() == 3 && dw.is_contiguous() && dw.scalar_type() == torch::kFloat32, "dw must be fp32 [E,M,N]");
-  const int64_t E = dw.size(0), M = dw.size(1), N = dw.size(2);
-  TORCH_CHECK(a.size(1) == M && b.size(1) == N && a.size(0) == b.size(0), "shape mismatch");
-  TORCH_CHECK(M % 128 == 0 && N % 8 == 0, "M must be a multiple of 128");
-  TORCH_CHECK(E <= kMaxGroups && offsets.numel() == E + 1, "offsets");
-  c10::cuda::CUDAGuard guard(a.device());
-  GemmArgs args = blank_args();
-  args.M = (int)M; args.N = (int)N; args.K = (int)a.size(0); args.num_groups = (int)E;
-  args.group_offsets = offsets.data_ptr<int>();
-  args.D = dw.data_ptr(); args.ldd = N; args.d_group_stride = M * N;
-  args.beta = accumulate ? 1.f : 0.f;
-  CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), M, a.stride(0), 64, 64);
-  CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), b.size(0), N, b.stride(0), 64, 64);
-  const int tiles = (int)(E * (M / BM) * ((N + 255) / 256));
-  launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()));
-}
-
 }  // namespace pm
-
-PM_DEFINE_ERROR_QUERY(pm_error_gemm)

@@ -104,6 +104,8 @@ void ce_fwd_bwd(torch::Tensor logits, torch::Tensor labels, int64_t ignore_index
   TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kBFloat16 && logits.stride(-1) == 1, "logits bf16");
   TORCH_CHECK(logits.stride(0) % 2 == 0, "row stride must be even");
   TORCH_CHECK(labels.scalar_type() == torch::kInt64 && labels.is_contiguous(), "labels int64");
+  PM_CHECK_CUDA(labels); PM_CHECK_CUDA(loss_sum); PM_CHECK_CUDA_OPT(row_loss);
+  TORCH_CHECK(labels.numel() == logits.size(0), "one label per row");
   const int n = (int)logits.size(0);
   const int V = (int)logits.size(1);
   if (n == 0) return;

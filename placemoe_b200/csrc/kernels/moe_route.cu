@@ -193,6 +193,8 @@ __global__ void __launch_bounds__(256) router_topk_bwd_kernel(const float* __res
 std::vector<torch::Tensor> router_topk_fwd(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t K,
                                            bool renorm) {
   TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == torch::kFloat32 && logits.is_contiguous(), "logits fp32");
+  PM_CHECK_CUDA_OPT(bias);
+  if (bias.has_value()) TORCH_CHECK(bias->scalar_type() == torch::kFloat32 && bias->numel() == logits.size(-1), "bias");
   const int E = (int)logits.size(-1);
   const int T = (int)(logits.numel() / E);
   TORCH_CHECK(E <= kMaxE && K <= 32 && K <= E, "router supports E <= 512, K <= 32");
@@ -218,6 +220,7 @@ torch::Tensor router_topk_bwd(torch::Tensor logits, c10::optional<torch::Tensor>
   const int T = (int)(logits.numel() / E);
   const int K = (int)idx.size(-1);
   TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous(), "dw fp32");
+  PM_CHECK_CUDA(logits); PM_CHECK_CUDA(idx); PM_CHECK_CUDA(dw); PM_CHECK_CUDA_OPT(bias); PM_CHECK_CUDA_OPT(aux);
   c10::cuda::CUDAGuard guard(logits.device());
   auto dl = torch::empty({T, E}, logits.options().dtype(torch::kBFloat16));
   if (T == 0) return dl;
@@ -348,6 +351,10 @@ std::vector<torch::Tensor> moe_plan(torch::Tensor idx, c10::optional<torch::Tens
                                     int64_t align) {
   TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == torch::kInt32 && idx.is_contiguous(), "idx int32");
   TORCH_CHECK(num_slots > 0 && num_slots <= 1024, "1..1024 slots");
+  PM_CHECK_CUDA_OPT(lut); PM_CHECK_CUDA_OPT(weights);
+  if (lut.has_value()) TORCH_CHECK(lut->scalar_type() == torch::kInt32 && lut->is_contiguous(), "lut int32");
+  if (weights.has_value())
+    TORCH_CHECK(weights->scalar_type() == torch::kFloat32 && weights->numel() == idx.numel(), "weights fp32");
   const int n = (int)idx.numel();
   const int K = (int)idx.size(-1);
   c10::cuda::CUDAGuard guard(idx.device());
@@ -448,6 +455,7 @@ void gather_rows(torch::Tensor src, torch::Tensor row_token, c10::optional<torch
   TORCH_CHECK(src.is_contiguous() && out.is_contiguous() && src.scalar_type() == torch::kBFloat16, "bf16 contiguous");
   const int H = (int)src.size(-1);
   TORCH_CHECK(H % 8 == 0 && out.size(-1) == H, "hidden");
+  PM_CHECK_CUDA(src); PM_CHECK_CUDA(row_token); PM_CHECK_CUDA(out); PM_CHECK_CUDA_OPT(end);
   const int cap = (int)out.size(0);
   TORCH_CHECK(row_token.numel() >= cap, "row_token too short");
   c10::cuda::CUDAGuard guard(src.device());
@@ -460,6 +468,7 @@ void gather_rows(torch::Tensor src, torch::Tensor row_token, c10::optional<torch
 
 void sum_rows(torch::Tensor src, torch::Tensor row_of, torch::Tensor out) {
   TORCH_CHECK(src.is_contiguous() && out.is_contiguous(), "contiguous");
+  PM_CHECK_CUDA(src); PM_CHECK_CUDA(row_of); PM_CHECK_CUDA(out);
   const int H = (int)src.size(-1);
   const int T = (int)out.size(0);
   const int K = (int)(row_of.numel() / std::max(T, 1));
@@ -472,6 +481,7 @@ void sum_rows(torch::Tensor src, torch::Tensor row_of, torch::Tensor out) {
 }
 
 torch::Tensor gather_scalar(torch::Tensor vals, torch::Tensor row_of) {
+  PM_CHECK_CUDA(vals); PM_CHECK_CUDA(row_of);
   const int n = (int)row_of.numel();
   c10::cuda::CUDAGuard guard(vals.device());
   auto out = torch::empty(row_of.sizes(), vals.options());

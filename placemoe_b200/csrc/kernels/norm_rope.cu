@@ -146,6 +146,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
   const int H = (int)x.size(-1);
   const int rows = (int)(x.numel() / H);
   TORCH_CHECK(w.numel() == H && w.is_contiguous(), "weight size");
+  PM_CHECK_CUDA(w);
   c10::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
@@ -170,6 +171,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == torch::kBFloat16, "dy/x contiguous bf16");
   TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous(), "dw must be fp32");
+  PM_CHECK_CUDA(dy); PM_CHECK_CUDA(x); PM_CHECK_CUDA(w); PM_CHECK_CUDA(rstd); PM_CHECK_CUDA(dw);
   const int H = (int)x.size(-1);
   const int rows = (int)(x.numel() / H);
   c10::cuda::CUDAGuard guard(x.device());
@@ -367,6 +369,9 @@ std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, to
   TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * D, "qkv width");
   TORCH_CHECK(D % 16 == 0, "head_dim must be a multiple of 16");
   TORCH_CHECK(pos.scalar_type() == torch::kInt32 && inv_freq.scalar_type() == torch::kFloat32, "pos int32, inv_freq fp32");
+  PM_CHECK_CUDA(pos); PM_CHECK_CUDA(inv_freq); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
+  TORCH_CHECK(!q_group || (qw.has_value() && qw->numel() == q_group), "q norm weight size");
+  TORCH_CHECK(!k_group || (kw.has_value() && kw->numel() == k_group), "k norm weight size");
   const int T = (int)(qkv.numel() / qkv.size(-1));
   TORCH_CHECK(pos.numel() == T, "positions");
   c10::cuda::CUDAGuard guard(qkv.device());
@@ -403,6 +408,9 @@ torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
                            c10::optional<torch::Tensor> dkw, int64_t Hq, int64_t Hkv, int64_t D, int64_t q_group,
                            int64_t k_group) {
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "grads must be contiguous");
+  PM_CHECK_CUDA(dq); PM_CHECK_CUDA(dk); PM_CHECK_CUDA(dv); PM_CHECK_CUDA(qkv); PM_CHECK_CUDA(pos);
+  PM_CHECK_CUDA(inv_freq); PM_CHECK_CUDA(rq); PM_CHECK_CUDA(rk); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
+  PM_CHECK_CUDA_OPT(dqw); PM_CHECK_CUDA_OPT(dkw);
   const int T = (int)(qkv.numel() / qkv.size(-1));
   c10::cuda::CUDAGuard guard(qkv.device());
   auto dqkv = torch::empty_like(qkv);

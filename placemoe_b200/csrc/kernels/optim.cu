@@ -159,6 +159,9 @@ std::vector<torch::Tensor> adamw_build_table(std::vector<torch::Tensor> params, 
     auto& p = params[i];
     TORCH_CHECK(p.is_cuda() && p.scalar_type() == torch::kFloat32 && p.is_contiguous(), "params must be fp32");
     TORCH_CHECK(grads[i].is_contiguous() && grads[i].numel() == p.numel(), "grad shape");
+    TORCH_CHECK(grads[i].is_cuda() && exp_avg[i].is_cuda() && exp_avg_sq[i].is_cuda(), "AdamW tensors must be CUDA");
+    TORCH_CHECK(!shadows[i].has_value() || (shadows[i]->is_cuda() && shadows[i]->numel() == p.numel() &&
+                                            shadows[i]->scalar_type() == torch::kBFloat16), "bf16 shadow");
     TORCH_CHECK(exp_avg[i].numel() == p.numel() && exp_avg_sq[i].numel() == p.numel(), "moment shape");
     TORCH_CHECK(grads[i].scalar_type() == torch::kFloat32 || grads[i].scalar_type() == torch::kBFloat16, "grad dtype");
     ts[i].p = p.data_ptr<float>();
@@ -186,6 +189,8 @@ std::vector<torch::Tensor> adamw_build_table(std::vector<torch::Tensor> params, 
 
 void adamw_step(torch::Tensor table, torch::Tensor meta, double lr, double beta1, double beta2, double eps, double wd,
                 int64_t step, c10::optional<torch::Tensor> grad_scale) {
+  PM_CHECK_CUDA(table);
+  PM_CHECK_CUDA_OPT(grad_scale);
   const int64_t nt = meta[0].item<int64_t>();
   const int nchunks = (int)meta[1].item<int64_t>();
   if (nchunks == 0) return;
@@ -206,7 +211,7 @@ std::vector<torch::Tensor> sq_norm_build_table(std::vector<torch::Tensor> grads,
   std::vector<NormTensor> ts(grads.size());
   std::vector<int2> chunks;
   for (size_t i = 0; i < grads.size(); ++i) {
-    TORCH_CHECK(grads[i].is_contiguous(), "grads must be contiguous");
+    TORCH_CHECK(grads[i].is_contiguous() && grads[i].is_cuda(), "grads must be contiguous CUDA tensors");
     ts[i].g = grads[i].data_ptr();
     ts[i].n = grads[i].numel();
     ts[i].weight = (float)weights[i];
@@ -227,6 +232,8 @@ std::vector<torch::Tensor> sq_norm_build_table(std::vector<torch::Tensor> grads,
 
 // out (fp32 scalar tensor) += sum_i weight_i * ||g_i||^2
 void sq_norm(torch::Tensor table, torch::Tensor meta, torch::Tensor out) {
+  PM_CHECK_CUDA(table);
+  PM_CHECK_CUDA(out);
   const int64_t nt = meta[0].item<int64_t>();
   const int nchunks = (int)meta[1].item<int64_t>();
   if (nchunks == 0) return;

@@ -5,7 +5,7 @@
 #include <vector>
 
 namespace pm {
-// gemm_sm100.cu
+// gemm_dense.cu, gemm_moe_fwd.cu, gemm_moe_bwd.cu (kernel template in gemm_sm100.cuh)
 void dense_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate);
 void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
                     c10::optional<torch::Tensor> gu_out);
@@ -60,7 +60,9 @@ int device_error(bool reset);
 }  // namespace pm
 
 // Per-translation-unit error words (see common.cuh).
-int pm_error_gemm(bool reset);
+int pm_error_gemm_dense(bool reset);
+int pm_error_gemm_moe_fwd(bool reset);
+int pm_error_gemm_moe_bwd(bool reset);
 int pm_error_norm(bool reset);
 int pm_error_route(bool reset);
 int pm_error_optim(bool reset);

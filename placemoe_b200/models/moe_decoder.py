@@ -96,7 +96,7 @@ class MoEBlock(nn.Module):
         self.down_proj = nn.Parameter(torch.empty(s, h, i))
         seed = layer_idx if cfg.router_bias_seed_per_layer else 0
         bias = zipf_router_bias(e, cfg.router_bias_zipf_s, cfg.router_bias_scale, seed)
-        self.register_buffer("router_bias", torch.from_numpy(bias), persistent=False)
+        self.register_buffer("router_bias", torch.tensor(bias, dtype=torch.float32), persistent=False)
         self.placement = None  # set by the placement runtime
         self.ep = None  # set by parallelize
         self.layer_key = f"model.layers.{layer_idx}.mlp.experts"
@@ -258,6 +258,7 @@ def build_model(cfg: MoEModelConfig, num_local_slots: int | None = None, device=
     """Construct directly on ``device`` (no CPU staging of multi-GB weights) and initialise."""
     with torch.device(device):
         model = MoEForCausalLM(cfg, num_local_slots)
+    model.to(device)  # buffers built from host data (router bias) follow the parameters
     model.init_weights(seed, expert_init)
     return model
 

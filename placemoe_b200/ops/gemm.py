@@ -1,4 +1,4 @@
-"""Dense GEMM ops on the tcgen05 kernel (``csrc/kernels/gemm_sm100.cu``).
+"""Dense GEMM ops on the tcgen05 kernel (``csrc/kernels/gemm_sm100.cuh``, ``gemm_dense.cu``).
 
 ``linear(x, w)`` computes ``x @ w.T`` in bf16 with fp32 accumulation; its
 backward issues the data gradient (``dy @ w``, B operand MN-major) and the

@@ -125,7 +125,8 @@ def test_moe_block_matches_reference(cfg):
     torch.manual_seed(4)
     t = 1024
     x = torch.randn(t, h, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    wg = (torch.randn(e, h, device="cuda") * 0.02).requires_grad_()
+    # bf16-representable router weights: reference and kernel see the same logits, no top-k flips
+    wg = (torch.randn(e, h, device="cuda") * 0.02).bfloat16().float().requires_grad_()
     bias = torch.randn(e, device="cuda") * 0.5
     p1 = (torch.randn(e, 2 * inter, h, device="cuda") * 0.02).requires_grad_()
     p2 = (torch.randn(e, h, inter, device="cuda") * 0.02).requires_grad_()
