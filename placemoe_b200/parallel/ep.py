@@ -154,7 +154,7 @@ class ExpertParallel:
         recv_slot = recv_meta[:, 1]
         partial = self._local_experts(blk, recv_x, recv_row, recv_slot, recv_w, sum(recv_rows))
         back = all_to_all(partial, recv_rows, send_rows, self.group)
-        y = torch.zeros(t, h, device=x.device, dtype=back.dtype).index_add(0, send_tok, back)
+        y = torch.zeros(t, h, device=x.device, dtype=torch.float32).index_add(0, send_tok, back.float())
         self.stats = {"sent_rows": sum(send_rows), "sent_assignments": sum(send_asg),
                       "dedup_ratio": sum(send_asg) / max(sum(send_rows), 1)}
         if self.capture_routes:
@@ -188,9 +188,11 @@ def _cuda_local_experts(blk, recv_x, recv_row, recv_slot, recv_w, nrows):
     offsets, counts, row_of, row_token, row_scale = kn.moe_plan(slot32, None, recv_w.detach().contiguous(), spr,
                                                                 cap, moe_ops.ALIGN)
     end = offsets[spr:]
-    # dispatched row -> received row (padding rows stay -1)
-    valid = row_token >= 0
-    row_src = torch.where(valid, recv_row.to(torch.int32)[row_token.clamp_min(0).long()], row_token)
+    # dispatched row -> received row.  Rows at or beyond offsets[spr] are not written by the
+    # plan (uninitialised), so they are masked by the device-side end before any indexing.
+    in_plan = torch.arange(cap, device=recv_x.device, dtype=torch.int32) < end
+    rt = torch.where(in_plan & (row_token >= 0), row_token, torch.full_like(row_token, -1))
+    row_src = torch.where(rt >= 0, recv_row.to(torch.int32)[rt.clamp_min(0).long()], rt)
     # received row -> its dispatched rows, padded to k entries
     first = torch.zeros(nrows + 1, dtype=torch.long, device=recv_x.device)
     first.index_add_(0, recv_row + 1, torch.ones_like(recv_row))
