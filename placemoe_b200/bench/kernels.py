@@ -1,0 +1,189 @@
+"""Kernel microbenchmarks with CUDA-event timing and roofline fractions.
+
+    python -m placemoe_b200.bench.kernels --op gemm --m 8192 --n 2048 --k 2048
+    python -m placemoe_b200.bench.kernels --op moe_fc1 --tokens 16384 --experts 64 --hidden 2048 --inter 1024
+    python -m placemoe_b200.bench.kernels --op attn --batch 2 --seq 4096 --heads 16 --kv-heads 16
+    python -m placemoe_b200.bench.kernels --op all
+
+Timing: warm-up launches, then ``--iters`` launches between two CUDA events
+on the launching stream with a synchronize on both sides; inputs are larger
+than the 126 MB L2 or an L2-flush write of 256 MB precedes every timed
+launch (``--flush``).  Fractions are against ``MEASURED_PEAKS.json``
+(bf16_tflops burst, hbm_gbs) when present, else 1.59 PFLOP/s and 6.65 TB/s.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"]), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def time_fn(fn, iters=20, warmup=5, flush=True):
+    buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda") if flush else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(iters):
+        if buf is not None:
+            buf.fill_(1.0)  # evict L2
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        total += s.elapsed_time(e)
+    return total / iters
+
+
+def report(name, ms, flops=0.0, nbytes=0.0):
+    tf, gbs, src = peaks()
+    row = {"op": name, "ms": round(ms, 4)}
+    if flops:
+        row["tflops"] = round(flops / ms / 1e9, 1)
+        row[f"frac_of_{src}_bf16"] = round(flops / ms / 1e9 / tf, 3)
+    if nbytes:
+        row["gbs"] = round(nbytes / ms / 1e6, 1)
+        row[f"frac_of_{src}_hbm"] = round(nbytes / ms / 1e6 / gbs, 3)
+    print(json.dumps(row), flush=True)
+    return row
+
+
+def bench_gemm(m, n, k, iters):
+    from placemoe_b200.ops.gemm import gemm_nn, gemm_nt, gemm_tn
+
+    a = torch.randn(m, k, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(n, k, device="cuda", dtype=torch.bfloat16)
+    out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    f = 2.0 * m * n * k
+    report(f"gemm_fwd[{m}x{n}x{k}]", time_fn(lambda: gemm_nt(a, b, out=out), iters), f)
+    w = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)
+    out2 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    report(f"gemm_dgrad[{m}x{n}x{k}]", time_fn(lambda: gemm_nn(a, w, out=out2), iters), f)
+    dy = torch.randn(k, m, device="cuda", dtype=torch.bfloat16)
+    x = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)
+    acc = torch.zeros(m, n, device="cuda", dtype=torch.float32)
+    report(f"gemm_wgrad_f32acc[{m}x{n}x{k}]", time_fn(lambda: gemm_tn(dy, x, out=acc, accumulate=True), iters), f)
+
+
+def _moe_inputs(tokens, experts, k, hidden, inter, skew=1.0):
+    from placemoe_b200.models.config import zipf_router_bias
+    from placemoe_b200.ops import kernels
+    from placemoe_b200.ops.moe import ALIGN, capacity_rows
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = torch.randn(tokens, experts, device="cuda", generator=g) + torch.from_numpy(
+        zipf_router_bias(experts, skew)).cuda()
+    idx, w, _, _ = kernels().router_topk_fwd(logits.contiguous(), None, k, False)
+    cap = capacity_rows(tokens, k, experts)
+    offsets, counts, row_of, row_token, row_scale = kernels().moe_plan(idx, None, w, experts, cap, ALIGN)
+    x = torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    xd = torch.empty(cap, hidden, device="cuda", dtype=torch.bfloat16)
+    kernels().gather_rows(x, row_token, offsets[experts:], xd)
+    w1 = (torch.randn(experts, 2 * inter, hidden, device="cuda") * 0.02).bfloat16()
+    w2 = (torch.randn(experts, hidden, inter, device="cuda") * 0.02).bfloat16()
+    return offsets, row_of, row_token, row_scale, xd, w1, w2, cap
+
+
+def bench_moe(tokens, experts, k, hidden, inter, iters, skew):
+    from placemoe_b200.ops import kernels
+
+    kn = kernels()
+    offsets, row_of, row_token, row_scale, xd, w1, w2, cap = _moe_inputs(tokens, experts, k, hidden, inter, skew)
+    rows = tokens * k
+    h = torch.empty(cap, inter, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(cap, 2 * inter, device="cuda", dtype=torch.bfloat16)
+    f1 = 2.0 * rows * 2 * inter * hidden
+    report(f"moe_fc1_swiglu[T{tokens} E{experts} k{k} H{hidden} I{inter}]",
+           time_fn(lambda: kn.moe_fc1_swiglu(xd, w1, offsets, row_scale, h, gu), iters), f1)
+    y = torch.empty(cap, hidden, device="cuda", dtype=torch.bfloat16)
+    f2 = 2.0 * rows * inter * hidden
+    report("moe_fc2", time_fn(lambda: kn.moe_grouped_gemm(h, w2, offsets, y, False), iters), f2)
+    dgu = torch.empty_like(gu)
+    dscale = torch.zeros(cap, device="cuda")
+    report("moe_fc2_dgrad_dswiglu",
+           time_fn(lambda: kn.moe_fc2_dgrad_dswiglu(y, w2, offsets, gu, row_scale, dgu, dscale), iters), f2)
+    dx = torch.empty_like(xd)
+    report("moe_fc1_dgrad", time_fn(lambda: kn.moe_grouped_gemm(dgu, w1, offsets, dx, True), iters), f1)
+    dw1 = torch.zeros(experts, 2 * inter, hidden, device="cuda")
+    report("moe_fc1_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(dgu, xd, offsets, dw1, True), iters), f1)
+    dw2 = torch.zeros(experts, hidden, inter, device="cuda")
+    report("moe_fc2_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(y, h, offsets, dw2, True), iters), f2)
+
+
+def bench_attn(batch, seq, heads, kv_heads, dim, iters):
+    from placemoe_b200.ops import kernels
+
+    t = batch * seq
+    q = torch.randn(t, heads, dim, device="cuda", dtype=torch.bfloat16)
+    kk = torch.randn(t, kv_heads, dim, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(t, kv_heads, dim, device="cuda", dtype=torch.bfloat16)
+    f = 4.0 * batch * seq * seq / 2 * heads * dim  # causal
+    o, lse = kernels().attn_fwd(q, kk, v, seq)
+    report(f"attn_fwd[B{batch} S{seq} H{heads}/{kv_heads} D{dim}]",
+           time_fn(lambda: kernels().attn_fwd(q, kk, v, seq), iters), f)
+    do = torch.randn_like(o)
+    report("attn_bwd", time_fn(lambda: kernels().attn_bwd(q, kk, v, o, lse, do, seq), iters), 2.5 * f)
+
+
+def bench_memory(tokens, hidden, iters):
+    from placemoe_b200.ops import kernels
+
+    x = torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(hidden, device="cuda")
+    report(f"rmsnorm_fwd[{tokens}x{hidden}]", time_fn(lambda: kernels().rmsnorm_fwd(x, w, 1e-6), iters),
+           nbytes=2 * x.numel() * 2)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--op", default="all", choices=("all", "gemm", "moe", "attn", "memory"))
+    ap.add_argument("--m", type=int, default=8192)
+    ap.add_argument("--n", type=int, default=2048)
+    ap.add_argument("--k", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--experts", type=int, default=64)
+    ap.add_argument("--topk", type=int, default=8)
+    ap.add_argument("--hidden", type=int, default=2048)
+    ap.add_argument("--inter", type=int, default=1024)
+    ap.add_argument("--skew", type=float, default=1.0)
+    ap.add_argument("--batch", type=int, default=2)
+    ap.add_argument("--seq", type=int, default=4096)
+    ap.add_argument("--heads", type=int, default=16)
+    ap.add_argument("--kv-heads", type=int, default=16)
+    ap.add_argument("--dim", type=int, default=128)
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args()
+    if a.op in ("all", "gemm"):
+        bench_gemm(a.m, a.n, a.k, a.iters)
+    if a.op in ("all", "moe"):
+        bench_moe(a.tokens, a.experts, a.topk, a.hidden, a.inter, a.iters, a.skew)
+    if a.op in ("all", "attn"):
+        bench_attn(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
+    if a.op in ("all", "memory"):
+        bench_memory(a.tokens, a.hidden, a.iters)
+    from placemoe_b200.ops import check_device_error
+
+    torch.cuda.synchronize()
+    check_device_error()
+
+
+if __name__ == "__main__":
+    main()
+
+
+__all__ = ["math"]

@@ -33,5 +33,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &pm::attn_bwd);
   // loss
   m.def("ce_fwd_bwd", &pm::ce_fwd_bwd);
+  // peer-to-peer data plane
+  m.def("p2p_put_rows", &pm::p2p_put_rows);
+  m.def("p2p_put_words", &pm::p2p_put_words);
+  m.def("p2p_allgather_words", &pm::p2p_allgather_words);
+  m.def("p2p_barrier", &pm::p2p_barrier);
+  m.def("p2p_reduce_f32", &pm::p2p_reduce_f32);
+  m.def("p2p_pull", &pm::p2p_pull);
   m.def("device_error", &pm::device_error, "read (and optionally clear) the kernels' error words");
 }

@@ -52,7 +52,11 @@ void dense_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, 
     TORCH_CHECK(!f32, "dgrad layout produces bf16");
     launch<256, false, true, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
   } else if (a_mn && b_mn) {
-    if (f32) launch<256, true, true, kGroupNone, kAccumF32, false>(ta, tb, args, grid);
+    if (f32) {
+      TORCH_CHECK(N % 4 == 0 && (out.stride(0) % 4) == 0, "fp32 weight-gradient output needs N % 4 == 0");
+      CUtensorMap td = make_tmap_f32_out(out.data_ptr(), 1, M, N, out.stride(0), 0, false);
+      launch<256, true, true, kGroupNone, kAccumF32, false>(ta, tb, args, grid, &td);
+    }
     else launch<256, true, true, kGroupNone, kStoreBF16, false>(ta, tb, args, grid);
   } else {
     TORCH_CHECK(false, "unsupported layout combination (a MN-major with b K-major)");

@@ -60,7 +60,8 @@ void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::T
   CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), M, a.stride(0), 64, 64);
   CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), b.size(0), N, b.stride(0), 64, 64);
   const int tiles = (int)(E * (M / BM) * ((N + 255) / 256));
-  launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()));
+  CUtensorMap td = make_tmap_f32_out(dw.data_ptr(), E, M, N, N, M * N, true);
+  launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()), &td);
 }
 
 }  // namespace pm

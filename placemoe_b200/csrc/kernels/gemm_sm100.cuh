@@ -45,7 +45,7 @@ enum Group : int { kGroupNone = 0, kGroupM = 1, kGroupK = 2 };
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
-constexpr int kMaxGroups = 1024;
+constexpr int kMaxGroups = 512;
 
 struct GemmArgs {
   int M, N, K;
@@ -64,14 +64,16 @@ struct GemmArgs {
   float beta;       // kAccumF32: D = acc + beta * D
 };
 
-template <int BN>
+template <int BN, int EPI = kStoreBF16>
 struct Cfg {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = BN * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int kStages = (BN == 256) ? 4 : 6;
+  // fp32-accumulating epilogues stage 32x32 fp32 boxes for TMA reduce-add: 4 warps x 2 buffers x 4 KB
+  static constexpr int kStagingBytes = EPI == kAccumF32 ? 4 * 2 * 4096 : 0;
+  static constexpr int kStages = EPI == kAccumF32 ? 3 : ((BN == 256) ? 4 : 6);
   static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kStagingBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 struct TileInfo {
@@ -157,8 +159,9 @@ __device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* src, float*
 
 template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs args) {
-  using C = Cfg<BN>;
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmD, GemmArgs args) {
+  using C = Cfg<BN, EPI>;
   constexpr int S = C::kStages;
   constexpr uint32_t kIdesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
 
@@ -167,7 +170,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* smA = smem;
   uint8_t* smB = smem + S * C::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
+  uint8_t* staging = smem + S * C::kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(staging + C::kStagingBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + S;
   uint64_t* tfull = bars + 2 * S;
@@ -285,6 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int r = q * 32 + lane;
     int acc = 0; uint32_t aph = 0;
+    int epi_buf = 0;  // kAccumF32: staging buffer toggle
     TileInfo ti;
     for (int t = blockIdx.x; decode_tile<BN, GROUP, SPLIT>(t, args, s_off, total, ti); t += gridDim.x) {
       if (*s_abort) break;
@@ -294,7 +299,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = ti.m0 + r;
       const bool empty_acc = ti.nkb == 0;
 
-      if (EPI == kStoreBF16 || EPI == kStoreF32 || EPI == kAccumF32) {
+      if (EPI == kAccumF32) {
+        // 32 rows (this warp's TMEM quadrant) x 32 columns per box: stage in swizzled smem, then
+        // one lane issues a TMA reduce-add (or a TMA store when beta == 0) into the fp32 output.
+        uint8_t* stg = staging + (warp - 2) * 2 * 4096;
+        const bool skip = empty_acc && args.beta == 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32 && !skip; ++c) {
+          const int col = ti.n0 + c * 32;
+          if (col >= args.N) break;
+          uint32_t rv[32];
+          if (!empty_acc) { tmem_ld32(taddr + c * 32, rv); tmem_ld_wait(); }
+          else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) rv[i] = 0u;
+          }
+          uint8_t* box = stg + (epi_buf & 1) * 4096;
+          if (lane == 0) bulk_wait_read_1();
+          __syncwarp();
+          uint8_t* rowp = box + lane * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(rowp + ((j ^ (lane & 7)) << 4)) =
+                make_uint4(rv[4 * j], rv[4 * j + 1], rv[4 * j + 2], rv[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int y0 = ti.m0 + q * 32;
+            if (GROUP == kGroupK) {
+              if (args.beta != 0.0f) tma_reduce_add_3d(&tmD, box, col, y0, ti.g);
+              else tma_store_3d(&tmD, box, col, y0, ti.g);
+            } else {
+              if (args.beta != 0.0f) tma_reduce_add_2d(&tmD, box, col, y0);
+              else tma_store_2d(&tmD, box, col, y0);
+            }
+            bulk_commit();
+          }
+          ++epi_buf;
+        }
+      } else if (EPI == kStoreBF16 || EPI == kStoreF32) {
         const bool row_ok = row < args.M;
         size_t base_off = (size_t)row * args.ldd;
         if (GROUP == kGroupK) base_off += (size_t)ti.g * args.d_group_stride;
@@ -316,16 +359,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_row32_bf16(reinterpret_cast<__nv_bfloat16*>(args.D) + base_off + col, v, valid);
           } else {
             float* dst = reinterpret_cast<float*>(args.D) + base_off + col;
-            if (EPI == kAccumF32 && empty_acc && args.beta == 1.0f) continue;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
               if (4 * i >= valid) break;
-              float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-              if (EPI == kAccumF32 && args.beta != 0.0f) {
-                float4 p = reinterpret_cast<float4*>(dst)[i];
-                o.x += args.beta * p.x; o.y += args.beta * p.y; o.z += args.beta * p.z; o.w += args.beta * p.w;
-              }
-              reinterpret_cast<float4*>(dst)[i] = o;
+              reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
             }
           }
         }
@@ -389,6 +426,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(&tempty[acc]);
       if (++acc == 2) { acc = 0; aph ^= 1; }
     }
+    // TMA reductions read shared memory and write global memory asynchronously: drain them
+    if (EPI == kAccumF32 && lane == 0) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -414,8 +453,9 @@ static inline int num_sms() {
 }
 
 template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT>
-static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid) {
-  using C = Cfg<BN>;
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
+                   const CUtensorMap* td = nullptr) {
+  using C = Cfg<BN, EPI>;
   auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, GROUP, EPI, SPLIT>;
   static bool configured = false;
   if (!configured) {
@@ -423,7 +463,10 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs&
     configured = true;
   }
   auto stream = at::cuda::getCurrentCUDAStream();
-  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, args);
+  CUtensorMap dummy;
+  memset(&dummy, 0, sizeof(dummy));
+  TORCH_CHECK(EPI != kAccumF32 || td != nullptr, "fp32-accumulating GEMM needs an output tensor map");
+  kern<<<grid, kThreads, C::kSmemBytes, stream>>>(ta, tb, td ? *td : dummy, args);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -3,7 +3,7 @@
 // rmsnorm_fwd/bwd: one warp per row, 16-byte vector accesses, fp32 math;
 //   backward accumulates d(weight) per CTA in registers/shared memory and
 //   adds it to the fp32 output with one atomic per element per CTA.
-// qkv_rope_fwd/bwd: one CTA per token splits the fused QKV projection into
+// qkv_rope_fwd/bwd: CTAs stride over tokens and split the fused QKV projection into
 //   q/k/v, applies RMSNorm to q and k (groups of `q_group`/`k_group`
 //   elements: head_dim for Qwen3-MoE per-head norms, the full width for
 //   OLMoE), then rotary embedding (rotate-half convention) from a fp32
@@ -220,145 +220,229 @@ struct QkvArgs {
   float* dkw;
 };
 
-// One CTA (256 threads) per token in the forward pass.
+// Layout used by both kernels: warp w handles heads w, w + 8, ... (q heads then k
+// heads, contiguous in the fused projection); lane l owns elements l + 32 c
+// (c < D / 32) of each of its heads, so the RoPE partner of element c is
+// c + D / 64 in the same lane.  Per-head norms reduce with warp shuffles; the
+// full-width norm adds one block reduction.  No shared-memory atomics.
+constexpr int kQkvWarps = 8;
+constexpr int kMaxHeadsPerWarp = 8;  // (Hq + Hkv) <= 64
+
+template <int D>
 __global__ void __launch_bounds__(256) qkv_rope_fwd_kernel(QkvArgs a) {
-  extern __shared__ float sm[];
-  const int t = blockIdx.x;
-  const int W = (a.Hq + 2 * a.Hkv) * a.D;
-  const int nq = a.Hq * a.D, nk = a.Hkv * a.D;
-  float* xs = sm;                // [nq + nk]
-  float* ss = sm + nq + nk;      // group sums
-  const int qg = a.q_group ? nq / a.q_group : 0;
-  const int kg = a.k_group ? nk / a.k_group : 0;
-  const __nv_bfloat16* row = a.qkv + (size_t)t * W;
-  for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) ss[i] = 0.f;
-  __syncthreads();
-  for (int i = threadIdx.x * 2; i < nq + nk; i += blockDim.x * 2) {
-    const __nv_bfloat162 p = *reinterpret_cast<const __nv_bfloat162*>(row + i);
-    const float x0 = __low2float(p), x1 = __high2float(p);
-    xs[i] = x0;
-    xs[i + 1] = x1;
-    if (i < nq) {
-      if (a.q_group) atomicAdd(&ss[i / a.q_group], x0 * x0 + x1 * x1);
-    } else if (a.k_group) {
-      atomicAdd(&ss[qg + (i - nq) / a.k_group], x0 * x0 + x1 * x1);
+  constexpr int C = D / 32;
+  constexpr int HC = C / 2;
+  __shared__ float red[2][kQkvWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NH = a.Hq + a.Hkv;
+  const int width = (a.Hq + 2 * a.Hkv) * D;
+  const int nq = a.Hq * D, nk = a.Hkv * D;
+  const bool full_q = a.q_group > D, full_k = a.k_group > D;
+  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
+    const __nv_bfloat16* row = a.qkv + (size_t)t * width;
+    float x[kMaxHeadsPerWarp][C];
+    float ssq = 0.f, ssk = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
+      const int h = warp + i * kQkvWarps;
+      float s = 0.f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        x[i][c] = h < NH ? __bfloat162float(row[h * D + lane + 32 * c]) : 0.f;
+        s += x[i][c] * x[i][c];
+      }
+      if (h < a.Hq) ssq += s; else if (h < NH) ssk += s;
     }
-  }
-  // v passes through
-  for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
-    *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + i) = *reinterpret_cast<const uint4*>(row + nq + nk + i);
-  __syncthreads();
-  for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) {
-    const int G = i < qg ? a.q_group : a.k_group;
-    const float r = rsqrtf(ss[i] / G + a.eps);
-    ss[i] = r;
-    if (i < qg) a.rq[(size_t)t * qg + i] = r;
-    else a.rk[(size_t)t * kg + (i - qg)] = r;
-  }
-  __syncthreads();
-  const float p = (float)a.pos[t];
-  const int half = a.D / 2;
-  const int pairs = (a.Hq + a.Hkv) * half;
-  for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-    const int h = idx / half, i = idx - h * half;
-    const bool isq = h < a.Hq;
-    const int e0 = h * a.D + i, e1 = e0 + half;  // positions in xs (q then k)
-    float x0 = xs[e0], x1 = xs[e1];
-    if (isq && a.q_group) {
-      x0 *= ss[e0 / a.q_group] * a.qw[e0 % a.q_group];
-      x1 *= ss[e1 / a.q_group] * a.qw[e1 % a.q_group];
-    } else if (!isq && a.k_group) {
-      const int k0 = e0 - nq, k1 = e1 - nq;
-      x0 *= ss[qg + k0 / a.k_group] * a.kw[k0 % a.k_group];
-      x1 *= ss[qg + k1 / a.k_group] * a.kw[k1 % a.k_group];
+    float rq_full = 1.f, rk_full = 1.f;
+    if (full_q || full_k) {
+      const float wq = warp_sum(ssq), wk = warp_sum(ssk);
+      __syncthreads();
+      if (lane == 0) { red[0][warp] = wq; red[1][warp] = wk; }
+      __syncthreads();
+      float tq = 0.f, tk = 0.f;
+#pragma unroll
+      for (int w = 0; w < kQkvWarps; ++w) { tq += red[0][w]; tk += red[1][w]; }
+      rq_full = rsqrtf(tq / (float)(a.q_group ? a.q_group : 1) + a.eps);
+      rk_full = rsqrtf(tk / (float)(a.k_group ? a.k_group : 1) + a.eps);
+      if (threadIdx.x == 0) {
+        if (full_q) a.rq[t] = rq_full;
+        if (full_k) a.rk[t] = rk_full;
+      }
     }
-    float sn, cs;
-    sincosf(p * a.inv_freq[i], &sn, &cs);
-    const float o0 = x0 * cs - x1 * sn;
-    const float o1 = x1 * cs + x0 * sn;
-    __nv_bfloat16* dst = isq ? a.q + (size_t)t * nq + e0 : a.k + (size_t)t * nk + (e0 - nq);
-    dst[0] = __float2bfloat16(o0);
-    dst[half] = __float2bfloat16(o1);
+    const float p = (float)a.pos[t];
+#pragma unroll
+    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
+      const int h = warp + i * kQkvWarps;
+      if (h >= NH) continue;
+      const bool isq = h < a.Hq;
+      const int hl = isq ? h : h - a.Hq;  // head index within q or k
+      const int G = isq ? a.q_group : a.k_group;
+      const float* wt = isq ? a.qw : a.kw;
+      float r = 1.f;
+      if (G == D) {
+        float s = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) s += x[i][c] * x[i][c];
+        r = rsqrtf(warp_sum(s) / (float)D + a.eps);
+        if (lane == 0) (isq ? a.rq : a.rk)[(size_t)t * (isq ? a.Hq : a.Hkv) + hl] = r;
+      } else if (G) {
+        r = isq ? rq_full : rk_full;
+      }
+      float y[C];
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int e = lane + 32 * c;
+        const float wv = G == D ? wt[e] : (G ? wt[hl * D + e] : 1.f);
+        y[c] = G ? x[i][c] * r * wv : x[i][c];
+      }
+      __nv_bfloat16* dst = isq ? a.q + ((size_t)t * a.Hq + hl) * D : a.k + ((size_t)t * a.Hkv + hl) * D;
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        const int e = lane + 32 * c;
+        float sn, cs;
+        sincosf(p * a.inv_freq[e], &sn, &cs);
+        dst[e] = __float2bfloat16(y[c] * cs - y[c + HC] * sn);
+        dst[e + D / 2] = __float2bfloat16(y[c + HC] * cs + y[c] * sn);
+      }
+    }
+    for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + i) = *reinterpret_cast<const uint4*>(row + nq + nk + i);
   }
 }
 
-// Backward: CTAs stride over tokens, d(weight) accumulated in shared memory.
+template <int D>
 __global__ void __launch_bounds__(256) qkv_rope_bwd_kernel(QkvArgs a) {
-  extern __shared__ float sm[];
-  const int W = (a.Hq + 2 * a.Hkv) * a.D;
-  const int nq = a.Hq * a.D, nk = a.Hkv * a.D;
-  const int qg = a.q_group ? nq / a.q_group : 0;
-  const int kg = a.k_group ? nk / a.k_group : 0;
-  float* g = sm;                         // [nq + nk] grad wrt normalized (pre-rope) values
-  float* xs = g + nq + nk;               // [nq + nk] inputs
-  float* dots = xs + nq + nk;            // [qg + kg]
-  float* sdq = dots + qg + kg;           // [q_group]
-  float* sdk = sdq + a.q_group;          // [k_group]
-  for (int i = threadIdx.x; i < a.q_group + a.k_group; i += blockDim.x) sdq[i] = 0.f;
-  const int half = a.D / 2;
-  const int pairs = (a.Hq + a.Hkv) * half;
+  constexpr int C = D / 32;
+  constexpr int HC = C / 2;
+  __shared__ float red[2][kQkvWarps];
+  __shared__ float sdw[2][kQkvWarps][D];  // per-head norm weights: per-warp partials
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NH = a.Hq + a.Hkv;
+  const int width = (a.Hq + 2 * a.Hkv) * D;
+  const int nq = a.Hq * D, nk = a.Hkv * D;
+  const bool full_q = a.q_group > D, full_k = a.k_group > D;
+  float dwacc[kMaxHeadsPerWarp][C];
+#pragma unroll
+  for (int i = 0; i < kMaxHeadsPerWarp; ++i)
+#pragma unroll
+    for (int c = 0; c < C; ++c) dwacc[i][c] = 0.f;
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-    __syncthreads();
-    const __nv_bfloat16* row = a.qkv + (size_t)t * W;
-    __nv_bfloat16* drow = a.dqkv + (size_t)t * W;
-    for (int i = threadIdx.x; i < qg + kg; i += blockDim.x) dots[i] = 0.f;
+    const __nv_bfloat16* row = a.qkv + (size_t)t * width;
+    __nv_bfloat16* drow = a.dqkv + (size_t)t * width;
     const float p = (float)a.pos[t];
-    for (int idx = threadIdx.x; idx < pairs; idx += blockDim.x) {
-      const int h = idx / half, i = idx - h * half;
+    float x[kMaxHeadsPerWarp][C], g[kMaxHeadsPerWarp][C];
+    float dotq = 0.f, dotk = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
+      const int h = warp + i * kQkvWarps;
+      if (h >= NH) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) { x[i][c] = 0.f; g[i][c] = 0.f; }
+        continue;
+      }
       const bool isq = h < a.Hq;
-      const int e0 = h * a.D + i, e1 = e0 + half;
-      const __nv_bfloat16* src = isq ? a.dq + (size_t)t * nq + e0 : a.dk + (size_t)t * nk + (e0 - nq);
-      const float d0 = __bfloat162float(src[0]), d1 = __bfloat162float(src[half]);
-      float sn, cs;
-      sincosf(p * a.inv_freq[i], &sn, &cs);
-      g[e0] = d0 * cs + d1 * sn;
-      g[e1] = -d0 * sn + d1 * cs;
-      xs[e0] = __bfloat162float(row[e0]);
-      xs[e1] = __bfloat162float(row[e1]);
+      const int hl = isq ? h : h - a.Hq;
+      const __nv_bfloat16* src = isq ? a.dq + ((size_t)t * a.Hq + hl) * D : a.dk + ((size_t)t * a.Hkv + hl) * D;
+#pragma unroll
+      for (int c = 0; c < HC; ++c) {
+        const int e = lane + 32 * c;
+        float sn, cs;
+        sincosf(p * a.inv_freq[e], &sn, &cs);
+        const float d0 = __bfloat162float(src[e]), d1 = __bfloat162float(src[e + D / 2]);
+        g[i][c] = d0 * cs + d1 * sn;
+        g[i][c + HC] = -d0 * sn + d1 * cs;
+      }
+      const int G = isq ? a.q_group : a.k_group;
+      const float* wt = isq ? a.qw : a.kw;
+      float dot = 0.f;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int e = lane + 32 * c;
+        x[i][c] = __bfloat162float(row[h * D + e]);
+        const float wv = G == D ? wt[e] : (G ? wt[hl * D + e] : 1.f);
+        dot += wv * g[i][c] * x[i][c];
+      }
+      if (G > D) { if (isq) dotq += dot; else dotk += dot; }
+    }
+    float tq = 0.f, tk = 0.f;
+    if (full_q || full_k) {
+      const float wq = warp_sum(dotq), wk = warp_sum(dotk);
+      __syncthreads();
+      if (lane == 0) { red[0][warp] = wq; red[1][warp] = wk; }
+      __syncthreads();
+#pragma unroll
+      for (int w = 0; w < kQkvWarps; ++w) { tq += red[0][w]; tk += red[1][w]; }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
+      const int h = warp + i * kQkvWarps;
+      if (h >= NH) continue;
+      const bool isq = h < a.Hq;
+      const int hl = isq ? h : h - a.Hq;
+      const int G = isq ? a.q_group : a.k_group;
+      const float* wt = isq ? a.qw : a.kw;
+      __nv_bfloat16* dst = drow + h * D;
+      if (!G) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) dst[lane + 32 * c] = __float2bfloat16(g[i][c]);
+        continue;
+      }
+      float r, dot;
+      if (G == D) {
+        r = (isq ? a.rq : a.rk)[(size_t)t * (isq ? a.Hq : a.Hkv) + hl];
+        float d = 0.f;
+#pragma unroll
+        for (int c = 0; c < C; ++c) d += wt[lane + 32 * c] * g[i][c] * x[i][c];
+        dot = warp_sum(d);
+      } else {
+        r = (isq ? a.rq : a.rk)[t];
+        dot = isq ? tq : tk;
+      }
+      const float coef = r * r * r * dot / (float)G;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int e = lane + 32 * c;
+        const float wv = G == D ? wt[e] : wt[hl * D + e];
+        dst[e] = __float2bfloat16(r * wv * g[i][c] - x[i][c] * coef);
+        dwacc[i][c] += g[i][c] * x[i][c] * r;
+      }
     }
     for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
       *reinterpret_cast<uint4*>(drow + nq + nk + i) = *reinterpret_cast<const uint4*>(a.dv + (size_t)t * nk + i);
-    __syncthreads();
-    // dot_g = sum_j w_j g_j x_j over each norm group; d(weight) partials
-    for (int e = threadIdx.x; e < nq + nk; e += blockDim.x) {
-      if (e < nq) {
-        if (!a.q_group) continue;
-        const int grp = e / a.q_group, j = e % a.q_group;
-        const float r = a.rq[(size_t)t * qg + grp];
-        atomicAdd(&dots[grp], a.qw[j] * g[e] * xs[e]);
-        atomicAdd(&sdq[j], g[e] * xs[e] * r);
-      } else {
-        if (!a.k_group) continue;
-        const int ke = e - nq;
-        const int grp = ke / a.k_group, j = ke % a.k_group;
-        const float r = a.rk[(size_t)t * kg + grp];
-        atomicAdd(&dots[qg + grp], a.kw[j] * g[e] * xs[e]);
-        atomicAdd(&sdk[j], g[e] * xs[e] * r);
-      }
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < nq + nk; e += blockDim.x) {
-      float out;
-      if (e < nq) {
-        if (a.q_group) {
-          const int grp = e / a.q_group, j = e % a.q_group;
-          const float r = a.rq[(size_t)t * qg + grp];
-          out = r * a.qw[j] * g[e] - xs[e] * r * r * r * dots[grp] / a.q_group;
-        } else out = g[e];
-      } else {
-        const int ke = e - nq;
-        if (a.k_group) {
-          const int grp = ke / a.k_group, j = ke % a.k_group;
-          const float r = a.rk[(size_t)t * kg + grp];
-          out = r * a.kw[j] * g[e] - xs[e] * r * r * r * dots[qg + grp] / a.k_group;
-        } else out = g[e];
-      }
-      drow[e] = __float2bfloat16(out);
+  }
+  // weight gradients: full-width norms own one element per (head, lane, c) -> direct atomics;
+  // per-head norms reduce over the warp's heads, then over the 8 warps in shared memory.
+  float hq[C], hk[C];
+#pragma unroll
+  for (int c = 0; c < C; ++c) { hq[c] = 0.f; hk[c] = 0.f; }
+#pragma unroll
+  for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
+    const int h = warp + i * kQkvWarps;
+    if (h >= NH) continue;
+    const bool isq = h < a.Hq;
+    const int hl = isq ? h : h - a.Hq;
+    const int G = isq ? a.q_group : a.k_group;
+    if (!G) continue;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int e = lane + 32 * c;
+      if (G == D) { if (isq) hq[c] += dwacc[i][c]; else hk[c] += dwacc[i][c]; }
+      else atomicAdd(&(isq ? a.dqw : a.dkw)[hl * D + e], dwacc[i][c]);
     }
   }
-  __syncthreads();
-  for (int i = threadIdx.x; i < a.q_group; i += blockDim.x) atomicAdd(&a.dqw[i], sdq[i]);
-  for (int i = threadIdx.x; i < a.k_group; i += blockDim.x) atomicAdd(&a.dkw[i], sdk[i]);
+  if (a.q_group == D || a.k_group == D) {
+#pragma unroll
+    for (int c = 0; c < C; ++c) { sdw[0][warp][lane + 32 * c] = hq[c]; sdw[1][warp][lane + 32 * c] = hk[c]; }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 2 * D; e += blockDim.x) {
+      const int which = e / D, j = e % D;
+      float s = 0.f;
+#pragma unroll
+      for (int w = 0; w < kQkvWarps; ++w) s += sdw[which][w][j];
+      if (which == 0 && a.q_group == D) atomicAdd(&a.dqw[j], s);
+      if (which == 1 && a.k_group == D) atomicAdd(&a.dkw[j], s);
+    }
+  }
 }
 
 // Returns q [T,Hq,D], k [T,Hkv,D], v [T,Hkv,D], rstd_q, rstd_k.
@@ -367,7 +451,7 @@ std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, to
                                         int64_t Hkv, int64_t D, int64_t q_group, int64_t k_group, double eps) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == torch::kBFloat16 && qkv.is_contiguous(), "qkv contiguous bf16");
   TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * D, "qkv width");
-  TORCH_CHECK(D % 16 == 0, "head_dim must be a multiple of 16");
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   TORCH_CHECK(pos.scalar_type() == torch::kInt32 && inv_freq.scalar_type() == torch::kFloat32, "pos int32, inv_freq fp32");
   PM_CHECK_CUDA(pos); PM_CHECK_CUDA(inv_freq); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
   TORCH_CHECK(!q_group || (qw.has_value() && qw->numel() == q_group), "q norm weight size");
@@ -393,10 +477,13 @@ std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, to
   a.kw = k_group ? kw->data_ptr<float>() : nullptr;
   a.q = (__nv_bfloat16*)q.data_ptr(); a.k = (__nv_bfloat16*)k.data_ptr(); a.v = (__nv_bfloat16*)v.data_ptr();
   a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
-  const size_t smem = (size_t)((Hq + Hkv) * D + qg + kg) * sizeof(float);
-  auto kern = qkv_rope_fwd_kernel;
-  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  kern<<<T, 256, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  TORCH_CHECK(Hq + Hkv <= kQkvWarps * kMaxHeadsPerWarp, "at most 64 q+k heads");
+  TORCH_CHECK(!q_group || q_group == D || q_group == Hq * D, "q norm group: head_dim or full width");
+  TORCH_CHECK(!k_group || k_group == D || k_group == Hkv * D, "k norm group: head_dim or full width");
+  const int grid = std::min(T, sm_count() * 8);
+  if (D == 128) qkv_rope_fwd_kernel<128><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  else if (D == 64) qkv_rope_fwd_kernel<64><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  else TORCH_CHECK(false, "head_dim must be 64 or 128");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {q, k, v, rq, rk};
 }
@@ -428,11 +515,11 @@ torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
   a.dv = (const __nv_bfloat16*)dv.data_ptr(); a.dqkv = (__nv_bfloat16*)dqkv.data_ptr();
   a.dqw = q_group ? dqw->data_ptr<float>() : nullptr;
   a.dkw = k_group ? dkw->data_ptr<float>() : nullptr;
-  const size_t smem = (size_t)(2 * (Hq + Hkv) * D + qg + kg + q_group + k_group) * sizeof(float);
-  auto kern = qkv_rope_bwd_kernel;
-  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  TORCH_CHECK(Hq + Hkv <= kQkvWarps * kMaxHeadsPerWarp, "at most 64 q+k heads");
   const int grid = std::min(T, sm_count() * 4);
-  kern<<<grid, 256, smem, at::cuda::getCurrentCUDAStream()>>>(a);
+  if (D == 128) qkv_rope_bwd_kernel<128><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  else if (D == 64) qkv_rope_bwd_kernel<64><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  else TORCH_CHECK(false, "head_dim must be 64 or 128");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dqkv;
 }

@@ -110,13 +110,30 @@ __global__ void __launch_bounds__(256) sq_norm_kernel(const NormTensor* __restri
     float part = 0.f;
     if (t.g_bf16) {
       const __nv_bfloat16* g = reinterpret_cast<const __nv_bfloat16*>(t.g);
-      for (long long i = beg + threadIdx.x; i < end; i += blockDim.x) {
+      const bool vec_ok = (reinterpret_cast<uintptr_t>(g + beg) & 15) == 0;
+      const long long vend = vec_ok ? beg + ((end - beg) & ~7LL) : beg;
+      for (long long i = beg + threadIdx.x * 8; i < vend; i += blockDim.x * 8) {
+        const uint4 q = *reinterpret_cast<const uint4*>(g + i);
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float a = bf16_lo(u[j]), b = bf16_hi(u[j]);
+          part += a * a + b * b;
+        }
+      }
+      for (long long i = vend + threadIdx.x; i < end; i += blockDim.x) {
         const float x = __bfloat162float(g[i]);
         part += x * x;
       }
     } else {
       const float* g = reinterpret_cast<const float*>(t.g);
-      for (long long i = beg + threadIdx.x; i < end; i += blockDim.x) part += g[i] * g[i];
+      const bool vec_ok = (reinterpret_cast<uintptr_t>(g + beg) & 15) == 0;
+      const long long vend = vec_ok ? beg + ((end - beg) & ~3LL) : beg;
+      for (long long i = beg + threadIdx.x * 4; i < vend; i += blockDim.x * 4) {
+        const float4 v = *reinterpret_cast<const float4*>(g + i);
+        part += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      }
+      for (long long i = vend + threadIdx.x; i < end; i += blockDim.x) part += g[i] * g[i];
     }
     acc += part * t.weight;
   }
@@ -240,7 +257,7 @@ void sq_norm(torch::Tensor table, torch::Tensor meta, torch::Tensor out) {
   c10::cuda::CUDAGuard guard(table.device());
   const NormTensor* tp = reinterpret_cast<const NormTensor*>(table.data_ptr());
   const int2* cp = reinterpret_cast<const int2*>(reinterpret_cast<const uint8_t*>(table.data_ptr()) + nt * sizeof(NormTensor));
-  const int grid = std::min(nchunks, sms_opt() * 4);
+  const int grid = std::min(nchunks, sms_opt() * 8);
   sq_norm_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(tp, cp, nchunks, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

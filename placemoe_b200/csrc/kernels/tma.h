@@ -80,4 +80,24 @@ inline CUtensorMap make_tmap_3d_bf16(const void* base, uint64_t batch, uint64_t 
   return m;
 }
 
+// fp32 output [rows, cols] (2-D) or [batch, rows, cols] (3-D) for TMA store / reduce-add,
+// box = 32 x 32 (x 1) elements, 128-byte swizzle.
+inline CUtensorMap make_tmap_f32_out(void* base, uint64_t batch, uint64_t rows, uint64_t cols, uint64_t ld,
+                                     uint64_t batch_stride, bool three_d) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
+  if ((ld * 4) % 16 != 0 || (three_d && (batch_stride * 4) % 16 != 0))
+    throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  CUtensorMap m;
+  const cuuint32_t rank = three_d ? 3 : 2;
+  cuuint64_t dims[3] = {cols, rows, batch};
+  cuuint64_t strides[2] = {ld * 4, batch_stride * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, base, dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled(f32 out) failed: " + std::to_string((int)r));
+  return m;
+}
+
 }  // namespace pm

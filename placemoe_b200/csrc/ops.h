@@ -56,6 +56,17 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
 void ce_fwd_bwd(torch::Tensor logits, torch::Tensor labels, int64_t ignore_index, double grad_scale,
                 torch::Tensor loss_sum, c10::optional<torch::Tensor> row_loss);
 
+// p2p.cu
+void p2p_put_rows(torch::Tensor src, c10::optional<torch::Tensor> src_row, torch::Tensor dst_rank, torch::Tensor dst_row,
+                  c10::optional<torch::Tensor> n_dev, int64_t n_host, torch::Tensor peers, int64_t region_off,
+                  int64_t ld);
+void p2p_put_words(torch::Tensor vals, torch::Tensor dst_rank, torch::Tensor dst_idx, c10::optional<torch::Tensor> n_dev,
+                   int64_t n_host, torch::Tensor peers, int64_t region_off);
+void p2p_allgather_words(torch::Tensor vals, torch::Tensor peers, int64_t region_off, int64_t my_rank);
+void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s);
+void p2p_reduce_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor ranks, int64_t region_off);
+void p2p_pull(torch::Tensor dst, torch::Tensor peers, int64_t src_rank, int64_t region_off);
+
 int device_error(bool reset);
 }  // namespace pm
 
@@ -68,3 +79,4 @@ int pm_error_route(bool reset);
 int pm_error_optim(bool reset);
 int pm_error_loss(bool reset);
 int pm_error_attn(bool reset);
+int pm_error_p2p(bool reset);
