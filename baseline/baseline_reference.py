@@ -1,23 +1,177 @@
-"""Reference arm of bench.py: the unmodified reference (installed into baseline/_ref) on the same metric/config.
+"""Reference arm of bench.py: the unmodified reference (installed in baseline/_ref) on the same metric.
 
-Prints one JSON line with "impl": "reference".  Until the harness that drives
-the reference's own trainer on the synthetic OLMoE-shaped configuration is in
-place, it reports the arm as unavailable with the reason.
+Drives the reference through its public API and stock code path, in the
+order its BaseTrainer uses: ``init_parallel_state`` (FSDP2 data parallel +
+expert parallel = world size), ``configure_hiermoe`` (defaults),
+``build_foundation_model`` (meta init) -> ``build_parallelize_model`` (FSDP2,
+mixed precision, gradient checkpointing as in its trainer default) ->
+``build_optimizer`` (fused AdamW) and, per step, forward/backward of every
+micro-batch, ``veomni_clip_grad_norm`` and ``optimizer.step``.
+
+Model: the reference has no expert-parallel OLMoE implementation, so its
+Qwen3-MoE implementation is configured at the OLMoE-1B-7B shape (16 layers,
+hidden 2048, 16 MHA heads x 128, 64 experts top-8, moe_intermediate 1024,
+vocab 50304); MoE kernels ``fused_triton`` (its default), attention through
+PyTorch SDPA, other ops eager (liger_kernel is not installed here).  The
+reference exposes no router-bias hook, so its routing is not skewed.
+
+Timing and output follow bench.py: W warm-up steps, K device-timed steps
+(CUDA events, max over ranks), then K end-to-end steps with pinned-host
+inputs and a loss read per step.
 """
 
 from __future__ import annotations
 
 import json
 import os
+import sys
+import tempfile
+import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(HERE, "_ref")
 
 
+def _unavailable(reason: str) -> int:
+    print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+    return 0
+
+
+def _config_dir(vocab=50304, hidden=2048, layers=16, heads=16, kv=16, hd=128, experts=64, k=8, inter=1024):
+    d = tempfile.mkdtemp(prefix="ref_olmoe_shape_")
+    cfg = {
+        "architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe", "vocab_size": vocab,
+        "hidden_size": hidden, "intermediate_size": inter, "moe_intermediate_size": inter,
+        "num_hidden_layers": layers, "num_attention_heads": heads, "num_key_value_heads": kv, "head_dim": hd,
+        "num_experts": experts, "num_experts_per_tok": k, "norm_topk_prob": False, "decoder_sparse_step": 1,
+        "mlp_only_layers": [], "rope_theta": 10000.0, "rms_norm_eps": 1e-5, "max_position_embeddings": 4096,
+        "tie_word_embeddings": False, "router_aux_loss_coef": 0.01, "output_router_logits": True,
+        "attention_bias": False, "attention_dropout": 0.0, "hidden_act": "silu", "initializer_range": 0.02,
+        "torch_dtype": "bfloat16", "use_cache": False,
+    }
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(cfg, f)
+    return d
+
+
 def main(args) -> int:
     if not os.path.isdir(os.path.join(REF, "veomni")):
-        print(json.dumps({"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}))
-        return 0
-    print(json.dumps({"impl": "reference",
-                      "unavailable": "reference harness for the OLMoE-shaped synthetic run is not implemented yet"}))
+        return _unavailable("reference not installed in baseline/_ref")
+    if args.model != "olmoe_1b_7b":
+        return _unavailable(f"reference arm is defined for olmoe_1b_7b only (got {args.model})")
+    sys.path.insert(0, REF)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if not dist.is_initialized():
+        if world == 1:
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", str(29600 + os.getpid() % 1000))
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    try:
+        from veomni.arguments.arguments_types import HierMoEConfig, MixedPrecisionConfig, OpsImplementationConfig
+        from veomni.distributed.clip_grad_norm import veomni_clip_grad_norm
+        from veomni.distributed.moe.hiermoe.state import configure_hiermoe
+        from veomni.distributed.parallel_state import get_parallel_state, init_parallel_state
+        from veomni.distributed.torch_parallelize import build_parallelize_model
+        from veomni.models import build_foundation_model
+        from veomni.optim import build_optimizer
+    except Exception as e:  # missing optional deps etc.
+        return _unavailable(f"reference import failed: {type(e).__name__}: {e}")
+
+    init_parallel_state(dp_size=world, dp_shard_size=world, extra_parallel_sizes=(world,),
+                        extra_parallel_names=("ep",), dp_mode="fsdp2")
+    ps = get_parallel_state()
+    configure_hiermoe(HierMoEConfig(), ep_group=ps.ep_group if getattr(ps, "ep_enabled", False) else None,
+                      ep_fsdp_size=ps.ep_fsdp_size if getattr(ps, "ep_enabled", False) else 1,
+                      activation_checkpointing_enabled=True, fsdp_offload_enabled=False,
+                      gradient_bytes_per_element=4)
+    ops = OpsImplementationConfig(attn_implementation="sdpa", moe_implementation="fused_triton",
+                                  cross_entropy_loss_implementation="eager", rms_norm_implementation="eager",
+                                  swiglu_mlp_implementation="eager", rotary_pos_emb_implementation="eager")
+    cfg_dir = _config_dir()
+    model = build_foundation_model(config_path=cfg_dir, weights_path=None, torch_dtype="float32", init_device="meta",
+                                   ops_implementation=ops)
+    model = build_parallelize_model(model, init_device="meta", weights_path=None, enable_reshard_after_forward=True,
+                                    mixed_precision=MixedPrecisionConfig(enable=True),
+                                    enable_gradient_checkpointing=True,
+                                    basic_modules=list(getattr(model, "_no_split_modules", None) or []),
+                                    enable_forward_prefetch=True)
+    model.train()
+    opt = build_optimizer(model, lr=3e-4, weight_decay=0.1, fused=True)
+
+    seq, bpg, mb = args.seq, args.batch_per_gpu, args.micro_batch
+    g = torch.Generator().manual_seed(rank)
+    pool = [torch.randint(0, 50304, (bpg, seq), generator=g).pin_memory() for _ in range(2)]
+    dev = [p.cuda() for p in pool]
+
+    def step(ids, read_loss):
+        losses = []
+        for i in range(0, bpg, mb):
+            x = ids[i:i + mb].cuda(non_blocking=True)
+            out = model(input_ids=x, labels=x, use_cache=False)
+            loss = out.loss
+            (loss / max(1, bpg // mb)).backward()
+            losses.append(loss.detach())
+        veomni_clip_grad_norm(model, 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+        loss = torch.stack(losses).mean()
+        return float(loss.item()) if read_loss else loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(pool[0], True)
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(dev[i % 2], False)
+    e.record()
+    barrier()
+    ms = s.elapsed_time(e) / args.steps
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    last = None
+    for i in range(args.steps):
+        last = step(pool[i % 2], True)
+    e2.record()
+    barrier()
+    ms_e2e = s2.elapsed_time(e2) / args.steps
+    t = torch.tensor([ms, ms_e2e], device="cuda")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e2e = t.tolist()
+    tokens = bpg * seq * world
+    if rank == 0:
+        print(json.dumps({
+            "impl": "reference", "metric": "MoE train tokens/s", "value": round(tokens / (ms / 1e3), 1),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic uniform token ids (seeded), random-init weights",
+            "config": {"model": "reference Qwen3-MoE implementation at the olmoe_1b_7b shape (16L, H2048, 64E top8, "
+                                "I1024, V50304); no router bias", "global_batch": bpg * world, "seq_len": seq,
+                       "micro_batch": mb, "parallelism": f"fsdp{world}+ep{world}",
+                       "ops": "moe fused_triton, attention sdpa, gradient checkpointing on"},
+            "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": pool[0].numel() * 8, "d2h_bytes_per_step": 4, "last_loss": last},
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+    dist.destroy_process_group()
     return 0
+
+
+__all__ = ["main", "time"]

@@ -46,6 +46,7 @@ def parse():
     p.add_argument("--redundant-slots", type=int, default=0)
     p.add_argument("--artifact", default="")
     p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
+    p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
     return p.parse_args()
 
 
@@ -134,7 +135,8 @@ def main():
     mcfg = get_preset(args.model, **overrides)
     cfg = TrainConfig(model=args.model, seq_len=args.seq, batch_per_rank=args.batch_per_gpu,
                       micro_batch_size=args.micro_batch, redundant_slots_per_rank=args.redundant_slots,
-                      placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1)
+                      placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1,
+                      ep_transport=args.ep_transport)
     trainer = Trainer(cfg, mcfg)
     pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank)
     dev_batches = [b.to("cuda") for b in pool.batches]
@@ -206,6 +208,7 @@ def main():
                 "seq_len": args.seq,
                 "micro_batch": args.micro_batch,
                 "parallelism": f"dp{world}+ep{world}",
+                "ep_transport": args.ep_transport if world > 1 else "none",
                 "router_bias": f"{mcfg.router_bias_scale} * log Zipf(s={mcfg.router_bias_zipf_s})",
                 "l2": "working set >> 126 MB L2 (no explicit flush)",
                 "baseline_metric": BASELINE_METRIC,

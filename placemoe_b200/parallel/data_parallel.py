@@ -116,9 +116,11 @@ def expert_topology(num_experts: int, ep_size: int, redundant_slots_per_rank: in
 
 
 def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = None, group=None, device=None,
-                      capture_routes: bool = False) -> ParallelState:
+                      capture_routes: bool = False, transport: str = "auto") -> ParallelState:
     """Attach EP placement + dispatch to every MoE block and back dense grads with one bucket.
 
+    ``transport``: "auto" / "nccl" (all-to-all with exchanged split sizes) or "p2p" (peer-memory
+    kernels, CUDA only).
     The model must already hold the local expert slots (built with
     ``num_local_slots = topology.slots_per_rank`` and filled through
     :func:`placement.slice_expert_weights` or an expert_init callback).
@@ -132,7 +134,17 @@ def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = 
         raise ValueError("expert parallel size must equal the process-group size")
     keys = [blk.layer_key for blk in model.moe_blocks()]
     placements = build_placements(plans, topology, rank, keys)
-    ep = ExpertParallel(group, capture_routes=capture_routes) if world > 1 else None
+    ep = None
+    if world > 1:
+        dev0 = device or next(model.parameters()).device
+        # "auto" uses the all-to-all transport until the peer-memory path measures faster end to end
+        use_p2p = transport == "p2p"
+        if use_p2p:
+            from .p2p_ep import P2PExpertParallel
+
+            ep = P2PExpertParallel(group, capture_routes=capture_routes)
+        else:
+            ep = ExpertParallel(group, capture_routes=capture_routes)
     for blk in model.moe_blocks():
         if blk.num_local_slots != topology.slots_per_rank:
             raise ValueError(f"{blk.layer_key} holds {blk.num_local_slots} slots, topology needs "

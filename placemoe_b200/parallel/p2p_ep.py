@@ -41,6 +41,32 @@ from ..ops import moe as moe_ops
 BARRIER_TIMEOUT_S = 30.0
 
 
+class PhaseTimer:
+    """Optional CUDA-event marks at phase boundaries (set ``p2p_ep.TIMER = PhaseTimer()``)."""
+
+    def __init__(self):
+        self.marks: list[tuple[str, torch.cuda.Event]] = []
+
+    def mark(self, name: str) -> None:
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.marks.append((name, e))
+
+    def phases(self) -> dict[str, float]:
+        out: dict[str, float] = {}
+        for (_, a), (name, b) in zip(self.marks, self.marks[1:]):
+            out[name] = out.get(name, 0.0) + a.elapsed_time(b)
+        return out
+
+
+TIMER: PhaseTimer | None = None
+
+
+def _mark(name: str) -> None:
+    if TIMER is not None:
+        TIMER.mark(name)
+
+
 def _align(n: int, a: int = 256) -> int:
     return (n + a - 1) // a * a
 
@@ -104,12 +130,15 @@ class _P2PMoE(torch.autograd.Function):
         t, h = x.shape
         k = dest.shape[1]
         dev = x.device
+        _mark("start")
         onehot, pos_in_d, asg_pos, asg_to = _dispatch_tables(dest, W)
         rows_to = onehot.sum(0)
         # ---- 3) counts all-gather
         row = torch.stack([rows_to, asg_to], 1).to(torch.int32).contiguous()  # [W, 2]
+        _mark("fwd.tables")
         kn.p2p_allgather_words(row, arena.peers, arena.layout["counts"], r)
         arena.barrier()
+        _mark("fwd.counts_exchange")
         C = arena.view("counts", (W, W, 2), torch.int32).clone()  # [src, dst, (rows, asg)]
         # ---- 4) where my rows / assignments land at each destination
         excl = torch.cumsum(C, 0) - C  # prefix over sources
@@ -134,7 +163,9 @@ class _P2PMoE(torch.autograd.Function):
             kn.p2p_put_words(meta[:, :, c].contiguous().reshape(-1), d32.reshape(-1).contiguous(),
                              (dst_asg * 4 + c).reshape(-1).to(torch.int32).contiguous(), None, t * k, arena.peers,
                              arena.layout["recv_meta"])
+        _mark("fwd.offsets_and_puts")
         arena.barrier()
+        _mark("fwd.dispatch_barrier")
         # ---- 6) receiver side
         n_rows = C[:, r, 0].sum()  # device scalars
         n_asg = C[:, r, 1].sum()
@@ -153,6 +184,7 @@ class _P2PMoE(torch.autograd.Function):
         src_a = torch.searchsorted(torch.cumsum(asg_from, 0), a_idx, right=True).clamp_max(W - 1)
         loc["asg_src_rank"] = torch.where(valid, src_a, torch.full_like(src_a, -1)).to(torch.int32).contiguous()
         loc["asg_src_idx"] = torch.where(valid, rmeta[:, 3], torch.full_like(rmeta[:, 3], -1)).contiguous()
+        _mark("fwd.local_plan")
         xd = torch.empty(loc["cap"], h, device=dev, dtype=torch.bfloat16)
         kn.gather_rows(recv_x, loc["row_src"], loc["end"], xd)
         w1, w2 = blk.compute_weights()
@@ -162,19 +194,23 @@ class _P2PMoE(torch.autograd.Function):
         kn.moe_fc1_swiglu(xd, w1, loc["offsets"], loc["row_scale"], hbuf, gu)
         yd = torch.empty(loc["cap"], h, device=dev, dtype=torch.bfloat16)
         kn.moe_grouped_gemm(hbuf, w2, loc["offsets"], yd, False)
+        _mark("fwd.expert_gemms")
         partial = torch.empty(R_cap, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(yd, loc["table"], partial)
         # ---- 7) partial sums back to the sources
         back_dst_rank, back_dst_row = _return_targets(C, r, R_cap, dev)
         kn.p2p_put_rows(partial, None, back_dst_rank, back_dst_row, n_rows.to(torch.int32).reshape(1), R_cap,
                         arena.peers, arena.layout["back_rows"], h)
+        _mark("fwd.combine_puts")
         arena.barrier()
+        _mark("fwd.combine_barrier")
         # ---- 8) sum per token
         send_base = torch.cumsum(C[r, :, 0], 0) - C[r, :, 0]  # my send-order base per destination
         back_pos = torch.where(onehot > 0, send_base[None, :] + pos_in_d, torch.full_like(pos_in_d, -1)).to(torch.int32)
         back = arena.view("back_rows", (R_cap, h), torch.bfloat16)
         y = torch.empty(t, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(back, back_pos.contiguous(), y)
+        _mark("fwd.token_sum")
         ctx.save_for_backward(xd, hbuf, gu, w1, w2, dst_row, back_pos, d32, dst_asg.to(torch.int32), C)
         ctx.loc = loc
         ctx.blk, ctx.arena, ctx.shape = blk, arena, (t, h, k)

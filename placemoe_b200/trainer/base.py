@@ -55,6 +55,7 @@ class TrainConfig:
     redundant_slots_per_rank: int = 0
     placemoe_artifact: str = ""  # schema-v2 artifact loaded at startup
     capture_routes: bool = False
+    ep_transport: str = "auto"  # "auto" | "p2p" | "nccl"
     gradient_checkpointing: bool = False
     device: str = "cuda"
     log_interval: int = 10
@@ -100,7 +101,7 @@ class Trainer:
         self.model.gradient_checkpointing = cfg.gradient_checkpointing
         self.model.train()
         self.pstate = parallelize_model(self.model, plans=plans, topology=topology, device=self.device,
-                                        capture_routes=cfg.capture_routes)
+                                        capture_routes=cfg.capture_routes, transport=cfg.ep_transport)
         self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                     weight_decay=cfg.weight_decay)
         self._norm_table = None
