@@ -15,6 +15,12 @@ vocab 50304); MoE kernels ``fused_triton`` (its default), attention through
 PyTorch SDPA, other ops eager (liger_kernel is not installed here).  The
 reference exposes no router-bias hook, so its routing is not skewed.
 
+On one GPU the reference's parallelizer skips FSDP, which is where its
+mixed-precision policy lives: with the policy switched on it only upcasts the
+model to fp32, which its fused MoE kernels reject.  The one-GPU arm therefore
+builds the model in bf16 with the policy off (bf16 parameters and AdamW
+states) and initialises on cuda (meta init is rejected without FSDP).
+
 Timing and output follow bench.py: W warm-up steps, K device-timed steps
 (CUDA events, max over ranks), then K end-to-end steps with pinned-host
 inputs and a loss read per step.
@@ -98,10 +104,17 @@ def main(args) -> int:
                                   cross_entropy_loss_implementation="eager", rms_norm_implementation="eager",
                                   swiglu_mlp_implementation="eager", rotary_pos_emb_implementation="eager")
     cfg_dir = _config_dir()
-    model = build_foundation_model(config_path=cfg_dir, weights_path=None, torch_dtype="float32", init_device="meta",
-                                   ops_implementation=ops)
-    model = build_parallelize_model(model, init_device="meta", weights_path=None, enable_reshard_after_forward=True,
-                                    mixed_precision=MixedPrecisionConfig(enable=True),
+    # its parallelizer accepts meta init only when FSDP is on (world size > 1)
+    init_device = "meta" if world > 1 else "cuda"
+    # Without FSDP its mixed-precision switch only upcasts the model to fp32, which its fused
+    # MoE kernels reject (bf16/fp16 only); on one GPU the model is therefore built in bf16 with
+    # the switch off (bf16 parameters and optimizer states).
+    mp_on = world > 1
+    model = build_foundation_model(config_path=cfg_dir, weights_path=None,
+                                   torch_dtype="float32" if mp_on else "bfloat16",
+                                   init_device=init_device, ops_implementation=ops)
+    model = build_parallelize_model(model, init_device=init_device, weights_path=None, enable_reshard_after_forward=True,
+                                    mixed_precision=MixedPrecisionConfig(enable=mp_on),
                                     enable_gradient_checkpointing=True,
                                     basic_modules=list(getattr(model, "_no_split_modules", None) or []),
                                     enable_forward_prefetch=True)
@@ -163,6 +176,8 @@ def main(args) -> int:
             "dtype": "bf16", "data": "synthetic uniform token ids (seeded), random-init weights",
             "config": {"model": "reference Qwen3-MoE implementation at the olmoe_1b_7b shape (16L, H2048, 64E top8, "
                                 "I1024, V50304); no router bias", "global_batch": bpg * world, "seq_len": seq,
+                       "precision": "fsdp2 mixed precision (fp32 masters, bf16 compute)" if mp_on
+                       else "bf16 parameters and optimizer states (no FSDP on one GPU)",
                        "micro_batch": mb, "parallelism": f"fsdp{world}+ep{world}",
                        "ops": "moe fused_triton, attention sdpa, gradient checkpointing on"},
             "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",

@@ -71,6 +71,9 @@ def bench_gemm(m, n, k, iters):
     out = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     f = 2.0 * m * n * k
     report(f"gemm_fwd[{m}x{n}x{k}]", time_fn(lambda: gemm_nt(a, b, out=out), iters), f)
+    # the same product through cuBLAS (torch.matmul), for a same-box comparison
+    bt = b.t()
+    report(f"cublas_fwd[{m}x{n}x{k}]", time_fn(lambda: torch.matmul(a, bt, out=out), iters), f)
     w = torch.randn(k, n, device="cuda", dtype=torch.bfloat16)
     out2 = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
     report(f"gemm_dgrad[{m}x{n}x{k}]", time_fn(lambda: gemm_nn(a, w, out=out2), iters), f)
@@ -80,17 +83,17 @@ def bench_gemm(m, n, k, iters):
     report(f"gemm_wgrad_f32acc[{m}x{n}x{k}]", time_fn(lambda: gemm_tn(dy, x, out=acc, accumulate=True), iters), f)
 
 
-def _moe_inputs(tokens, experts, k, hidden, inter, skew=1.0):
+def _moe_inputs(tokens, experts, k, hidden, inter, skew=1.0, align=128):
     from placemoe_b200.models.config import zipf_router_bias
     from placemoe_b200.ops import kernels
-    from placemoe_b200.ops.moe import ALIGN, capacity_rows
+    from placemoe_b200.ops.moe import capacity_rows
 
     g = torch.Generator(device="cuda").manual_seed(0)
     logits = torch.randn(tokens, experts, device="cuda", generator=g) + torch.from_numpy(
         zipf_router_bias(experts, skew)).cuda()
     idx, w, _, _ = kernels().router_topk_fwd(logits.contiguous(), None, k, False)
-    cap = capacity_rows(tokens, k, experts)
-    offsets, counts, row_of, row_token, row_scale = kernels().moe_plan(idx, None, w, experts, cap, ALIGN)
+    cap = capacity_rows(tokens, k, experts, align)
+    offsets, counts, row_of, row_token, row_scale = kernels().moe_plan(idx, None, w, experts, cap, align)
     x = torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16)
     xd = torch.empty(cap, hidden, device="cuda", dtype=torch.bfloat16)
     kernels().gather_rows(x, row_token, offsets[experts:], xd)
@@ -99,26 +102,27 @@ def _moe_inputs(tokens, experts, k, hidden, inter, skew=1.0):
     return offsets, row_of, row_token, row_scale, xd, w1, w2, cap
 
 
-def bench_moe(tokens, experts, k, hidden, inter, iters, skew):
+def bench_moe(tokens, experts, k, hidden, inter, iters, skew, align=128):
     from placemoe_b200.ops import kernels
 
     kn = kernels()
-    offsets, row_of, row_token, row_scale, xd, w1, w2, cap = _moe_inputs(tokens, experts, k, hidden, inter, skew)
+    offsets, row_of, row_token, row_scale, xd, w1, w2, cap = _moe_inputs(tokens, experts, k, hidden, inter, skew,
+                                                                         align)
     rows = tokens * k
     h = torch.empty(cap, inter, device="cuda", dtype=torch.bfloat16)
     gu = torch.empty(cap, 2 * inter, device="cuda", dtype=torch.bfloat16)
     f1 = 2.0 * rows * 2 * inter * hidden
-    report(f"moe_fc1_swiglu[T{tokens} E{experts} k{k} H{hidden} I{inter}]",
-           time_fn(lambda: kn.moe_fc1_swiglu(xd, w1, offsets, row_scale, h, gu), iters), f1)
+    report(f"moe_fc1_swiglu[T{tokens} E{experts} k{k} H{hidden} I{inter} align{align}]",
+           time_fn(lambda: kn.moe_fc1_swiglu(xd, w1, offsets, row_scale, h, gu, align), iters), f1)
     y = torch.empty(cap, hidden, device="cuda", dtype=torch.bfloat16)
     f2 = 2.0 * rows * inter * hidden
-    report("moe_fc2", time_fn(lambda: kn.moe_grouped_gemm(h, w2, offsets, y, False), iters), f2)
+    report("moe_fc2", time_fn(lambda: kn.moe_grouped_gemm(h, w2, offsets, y, False, align), iters), f2)
     dgu = torch.empty_like(gu)
     dscale = torch.zeros(cap, device="cuda")
     report("moe_fc2_dgrad_dswiglu",
-           time_fn(lambda: kn.moe_fc2_dgrad_dswiglu(y, w2, offsets, gu, row_scale, dgu, dscale), iters), f2)
+           time_fn(lambda: kn.moe_fc2_dgrad_dswiglu(y, w2, offsets, gu, row_scale, dgu, dscale, align), iters), f2)
     dx = torch.empty_like(xd)
-    report("moe_fc1_dgrad", time_fn(lambda: kn.moe_grouped_gemm(dgu, w1, offsets, dx, True), iters), f1)
+    report("moe_fc1_dgrad", time_fn(lambda: kn.moe_grouped_gemm(dgu, w1, offsets, dx, True, align), iters), f1)
     dw1 = torch.zeros(experts, 2 * inter, hidden, device="cuda")
     report("moe_fc1_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(dgu, xd, offsets, dw1, True), iters), f1)
     dw2 = torch.zeros(experts, hidden, inter, device="cuda")
@@ -167,11 +171,16 @@ def main():
     ap.add_argument("--kv-heads", type=int, default=16)
     ap.add_argument("--dim", type=int, default=128)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--align", type=int, default=0, help="MoE segment alignment (0: both 128 and 256)")
     a = ap.parse_args()
     if a.op in ("all", "gemm"):
         bench_gemm(a.m, a.n, a.k, a.iters)
+        if a.op == "all":
+            bench_gemm(16384, 4096, 4096, a.iters)
+            bench_gemm(8192, 8192, 8192, a.iters)
     if a.op in ("all", "moe"):
-        bench_moe(a.tokens, a.experts, a.topk, a.hidden, a.inter, a.iters, a.skew)
+        for al in (128, 256) if a.align == 0 else (a.align,):
+            bench_moe(a.tokens, a.experts, a.topk, a.hidden, a.inter, a.iters, a.skew, al)
     if a.op in ("all", "attn"):
         bench_attn(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
     if a.op in ("all", "memory"):

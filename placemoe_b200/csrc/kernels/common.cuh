@@ -115,6 +115,12 @@ PM_DEVICE void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64
       : "memory");
 }
 
+// Prefetch `bytes` (multiple of 16, 16-byte aligned) of global memory into L2.
+PM_DEVICE void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(src)), "r"(bytes)
+               : "memory");
+}
+
 // 2^x on the SFU (ex2.approx, flush-to-zero).
 PM_DEVICE float fast_exp2(float x) {
   float y;
@@ -180,6 +186,8 @@ PM_DEVICE void tma_reduce_add_3d(const void* tmap, const void* smem_src, int x, 
 PM_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // at most one committed group may still be reading shared memory
 PM_DEVICE void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+// no committed group is still reading shared memory
+PM_DEVICE void bulk_wait_read_0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // every committed group has completed
 PM_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
@@ -265,6 +273,83 @@ PM_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::
 
 PM_DEVICE void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ------------------------------------------- CTA pairs (tcgen05 cta_group::2)
+// Two CTAs of a cluster share one MMA: the even CTA issues it, each CTA holds
+// half of A (rows) and half of B (columns) in its own shared memory, and each
+// CTA's TMEM receives its own rows of the accumulator.
+PM_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+PM_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the variable at `smem_addr` in cluster CTA `rank`.
+PM_DEVICE uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier given by a shared::cluster address (possibly in the peer CTA).
+PM_DEVICE void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+
+// Tensor loads into this CTA's shared memory whose completion is counted on the
+// pair leader's mbarrier (`bar_cluster_addr` from mapa_shared(..., 0)).
+PM_DEVICE void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
+PM_DEVICE void tma_load_3d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
+// Executed by one warp in EACH CTA of the pair: same TMEM columns in both.
+PM_DEVICE void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
+               "r"(ncols)
+               : "memory");
+}
+PM_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+PM_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA, issued by the leader CTA only: D (both CTAs' TMEM) (+)= A (both halves) * B (both halves).
+PM_DEVICE void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at the same shared offset in every CTA of `cta_mask`
+// when the leader's previously issued pair MMAs complete.
+PM_DEVICE void umma_commit_pair(uint64_t* bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
+}
+
 // ------------------------------------------------------ UMMA descriptors
 // Shared-memory matrix descriptor (sm_100 layout):
 //   [0,14) start address >> 4, [16,30) leading byte offset >> 4,
@@ -297,8 +382,9 @@ PM_DEVICE uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-PM_DEVICE float silu_f(float x) { return x / (1.0f + __expf(-x)); }
-PM_DEVICE float sigmoid_f(float x) { return 1.0f / (1.0f + __expf(-x)); }
+// Approximate division (reciprocal on the SFU): activations feed bf16 results.
+PM_DEVICE float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+PM_DEVICE float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 PM_DEVICE float warp_sum(float v) {
 #pragma unroll

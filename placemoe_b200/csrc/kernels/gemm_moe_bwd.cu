@@ -9,7 +9,8 @@ namespace pm {
 //   dgu[rows, 2I] = d(gate|up) of h = scale * silu(g) * u, using the saved gu
 //   dscale[row] += sum_j silu(g) u dh_raw
 void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor offsets, torch::Tensor gu,
-                           torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale) {
+                           torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale, int64_t align) {
+  TORCH_CHECK(align == 128 || align == 256, "segment alignment must be 128 or 256");
   check_bf16_2d(dy, "dy");
   check_bf16_2d(gu, "gu");
   check_bf16_2d(dgu, "dgu");
@@ -24,6 +25,7 @@ void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor off
   GemmArgs args = blank_args();
   args.M = (int)dy.size(0); args.N = (int)I; args.K = (int)H; args.num_groups = (int)E;
   args.group_offsets = offsets.data_ptr<int>();
+  args.raster = 1;  // an expert's weights (<= tens of MB) stay in L2 while its rows stream once
   args.row_scale = scale.data_ptr<float>();
   args.aux = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()); args.ld_aux = gu.stride(0);
   args.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()); args.ld_aux_out = dgu.stride(0);
@@ -31,12 +33,25 @@ void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor off
   args.inter = (int)I;
   CUtensorMap ta = make_tmap_2d_bf16(dy.data_ptr(), dy.size(0), H, dy.stride(0), 64, 128);
   CUtensorMap tb = make_tmap_3d_bf16(w2.data_ptr(), E, H, I, I, H * I, 64, 64);
-  if (I % 256 == 0) {
+  // saved activations in, d(gate|up) out: 32 x 32 epilogue boxes
+  CUtensorMap tg = make_tmap_bf16_epi(gu.data_ptr(), gu.size(0), 2 * I, gu.stride(0));
+  CUtensorMap tdg = make_tmap_bf16_epi(dgu.data_ptr(), dgu.size(0), 2 * I, dgu.stride(0));
+  if (align == 256) {
+    if (I % 256 == 0) {
+      const int ub = (int)((dy.size(0) / 256) * (I / 256));
+      launch<256, false, true, kGroupM, kDSwiGLU, false, true>(ta, tb, args, std::max(1, std::min(ub, num_pairs())),
+                                                               &tg, &tdg);
+    } else {
+      const int ub = (int)((dy.size(0) / 256) * (I / 128));
+      launch<128, false, true, kGroupM, kDSwiGLU, false, true>(ta, tb, args, std::max(1, std::min(ub, num_pairs())),
+                                                               &tg, &tdg);
+    }
+  } else if (I % 256 == 0) {
     const int ub = (int)((dy.size(0) / BM) * (I / 256));
-    launch<256, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())));
+    launch<256, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())), &tg, &tdg);
   } else {
     const int ub = (int)((dy.size(0) / BM) * (I / 128));
-    launch<128, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())));
+    launch<128, false, true, kGroupM, kDSwiGLU, false>(ta, tb, args, std::max(1, std::min(ub, num_sms())), &tg, &tdg);
   }
 }
 
@@ -59,8 +74,13 @@ void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::T
   args.beta = accumulate ? 1.f : 0.f;
   CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), M, a.stride(0), 64, 64);
   CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), b.size(0), N, b.stride(0), 64, 64);
-  const int tiles = (int)(E * (M / BM) * ((N + 255) / 256));
   CUtensorMap td = make_tmap_f32_out(dw.data_ptr(), E, M, N, N, M * N, true);
+  if (M % 256 == 0) {  // CTA pairs over 256 output rows
+    const int tiles = (int)(E * (M / 256) * ((N + 255) / 256));
+    launch<256, true, true, kGroupK, kAccumF32, false, true>(ta, tb, args, std::min(tiles, num_pairs()), &td);
+    return;
+  }
+  const int tiles = (int)(E * (M / BM) * ((N + 255) / 256));
   launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()), &td);
 }
 

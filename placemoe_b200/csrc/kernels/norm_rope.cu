@@ -203,7 +203,8 @@ struct QkvArgs {
   float eps;
   const __nv_bfloat16* qkv;  // [T, (Hq + 2 Hkv) D]
   const int* pos;            // [T]
-  const float* inv_freq;     // [D/2]
+  const float2* rope;        // [rope_len, D/2]: (cos, sin) of pos * inv_freq
+  int rope_len;
   const float* qw;           // [q_group] or null
   const float* kw;           // [k_group] or null
   __nv_bfloat16* q;          // [T, Hq, D]
@@ -220,242 +221,385 @@ struct QkvArgs {
   float* dkw;
 };
 
-// Layout used by both kernels: warp w handles heads w, w + 8, ... (q heads then k
-// heads, contiguous in the fused projection); lane l owns elements l + 32 c
-// (c < D / 32) of each of its heads, so the RoPE partner of element c is
-// c + D / 64 in the same lane.  Per-head norms reduce with warp shuffles; the
-// full-width norm adds one block reduction.  No shared-memory atomics.
-constexpr int kQkvWarps = 8;
-constexpr int kMaxHeadsPerWarp = 8;  // (Hq + Hkv) <= 64
+// One block of 256 threads per token (grid-stride).  Thread j owns 16-byte
+// chunks j, j + 256, ... of the q region and of the k region (8 consecutive
+// elements each), so every global access is a 16-byte vector.  A head spans
+// D / 8 consecutive threads; the RoPE partner of a chunk (offset +-D/2 in its
+// head) lives in lane ^ (D / 16).  Per-head norms reduce over the head's lanes
+// with shuffles, full-width norms with one block reduction per token.  The
+// rotation angles come from a (cos, sin) table indexed by position.
+constexpr int kQkvThreads = 256;
 
+PM_DEVICE void load8(const __nv_bfloat16* p, float (&v)[8]) {
+  const uint4 q = *reinterpret_cast<const uint4*>(p);
+  v[0] = bf16_lo(q.x); v[1] = bf16_hi(q.x); v[2] = bf16_lo(q.y); v[3] = bf16_hi(q.y);
+  v[4] = bf16_lo(q.z); v[5] = bf16_hi(q.z); v[6] = bf16_lo(q.w); v[7] = bf16_hi(q.w);
+}
+
+PM_DEVICE void store8(__nv_bfloat16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]),
+                                            pack_bf16(v[6], v[7]));
+}
+
+PM_DEVICE void load8f(const float* p, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+PM_DEVICE void load_rope(const float2* tab, float (&c)[8], float (&s)[8]) {
+  const float4* t4 = reinterpret_cast<const float4*>(tab);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 v = t4[i];
+    c[2 * i] = v.x; s[2 * i] = v.y; c[2 * i + 1] = v.z; s[2 * i + 1] = v.w;
+  }
+}
+
+template <int HL>
+PM_DEVICE float head_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < HL; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum of two values over the block (all threads call it; returns the totals).
+PM_DEVICE float2 block_sum2(float a, float b, float (*red)[kQkvThreads / 32]) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  __syncthreads();
+  if (lane == 0) { red[0][warp] = a; red[1][warp] = b; }
+  __syncthreads();
+  float ta = 0.f, tb = 0.f;
+#pragma unroll
+  for (int w = 0; w < kQkvThreads / 32; ++w) { ta += red[0][w]; tb += red[1][w]; }
+  return make_float2(ta, tb);
+}
+
+// Normalise, rotate and store one chunk (forward).
 template <int D>
-__global__ void __launch_bounds__(256) qkv_rope_fwd_kernel(QkvArgs a) {
-  constexpr int C = D / 32;
-  constexpr int HC = C / 2;
-  __shared__ float red[2][kQkvWarps];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NH = a.Hq + a.Hkv;
-  const int width = (a.Hq + 2 * a.Hkv) * D;
+PM_DEVICE void qkv_fwd_chunk(const float (&x)[8], float ssq, int c, int nch, int G, const float* wt, float rfull,
+                             float* rsave, int H, int t, __nv_bfloat16* dst, const float (&cs)[8],
+                             const float (&sn)[8], int o, bool first_half, float eps, int lane) {
+  constexpr int HL = D / 8;
+  constexpr int PX = D / 16;
+  float r = 1.f;
+  if (G == D) {
+    r = rsqrtf(head_sum<HL>(ssq) / (float)D + eps);
+    if (c < nch && (lane % HL) == 0) rsave[(size_t)t * H + (8 * c) / D] = r;
+  } else if (G) {
+    r = rfull;
+  }
+  float w8[8];
+  if (G == D) load8f(wt + o, w8);
+  else if (G && c < nch) load8f(wt + 8 * c, w8);
+  else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) w8[e] = 1.f;
+  }
+  float y[8], out[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) y[e] = G ? x[e] * r * w8[e] : x[e];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float py = __shfl_xor_sync(0xffffffffu, y[e], PX);
+    out[e] = first_half ? y[e] * cs[e] - py * sn[e] : y[e] * cs[e] + py * sn[e];
+  }
+  if (c < nch) store8(dst + 8 * c, out);
+}
+
+template <int D, int MQ, int MK>
+__global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
+  __shared__ float red[2][kQkvThreads / 32];
+  const int j = threadIdx.x, lane = j & 31;
   const int nq = a.Hq * D, nk = a.Hkv * D;
+  const int nqc = nq / 8, nkc = nk / 8;
+  const int width = nq + 2 * nk;
+  const int o = (8 * j) % D;  // offset of this thread's chunks inside their heads
+  const bool first_half = o < D / 2;
+  const int ai = o % (D / 2);  // rotation-angle index of the chunk's first element
   const bool full_q = a.q_group > D, full_k = a.k_group > D;
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
     const __nv_bfloat16* row = a.qkv + (size_t)t * width;
-    float x[kMaxHeadsPerWarp][C];
-    float ssq = 0.f, ssk = 0.f;
+    int p = a.pos[t];
+    if (p < 0 || p >= a.rope_len) {
+      if (j == 0) set_error(kErrBounds);
+      p = 0;
+    }
+    float cs[8], sn[8];
+    load_rope(a.rope + (size_t)p * (D / 2) + ai, cs, sn);
+    float xq[MQ][8], xk[MK][8], sq[MQ], sk[MK];
+    float tq = 0.f, tk = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
-      const int h = warp + i * kQkvWarps;
-      float s = 0.f;
+    for (int i = 0; i < MQ; ++i) {
+      const int c = j + kQkvThreads * i;
+      if (c < nqc) load8(row + 8 * c, xq[i]);
+      else {
 #pragma unroll
-      for (int c = 0; c < C; ++c) {
-        x[i][c] = h < NH ? __bfloat162float(row[h * D + lane + 32 * c]) : 0.f;
-        s += x[i][c] * x[i][c];
+        for (int e = 0; e < 8; ++e) xq[i][e] = 0.f;
       }
-      if (h < a.Hq) ssq += s; else if (h < NH) ssk += s;
+      sq[i] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sq[i] += xq[i][e] * xq[i][e];
+      tq += sq[i];
+    }
+#pragma unroll
+    for (int i = 0; i < MK; ++i) {
+      const int c = j + kQkvThreads * i;
+      if (c < nkc) load8(row + nq + 8 * c, xk[i]);
+      else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xk[i][e] = 0.f;
+      }
+      sk[i] = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sk[i] += xk[i][e] * xk[i][e];
+      tk += sk[i];
     }
     float rq_full = 1.f, rk_full = 1.f;
     if (full_q || full_k) {
-      const float wq = warp_sum(ssq), wk = warp_sum(ssk);
-      __syncthreads();
-      if (lane == 0) { red[0][warp] = wq; red[1][warp] = wk; }
-      __syncthreads();
-      float tq = 0.f, tk = 0.f;
-#pragma unroll
-      for (int w = 0; w < kQkvWarps; ++w) { tq += red[0][w]; tk += red[1][w]; }
-      rq_full = rsqrtf(tq / (float)(a.q_group ? a.q_group : 1) + a.eps);
-      rk_full = rsqrtf(tk / (float)(a.k_group ? a.k_group : 1) + a.eps);
-      if (threadIdx.x == 0) {
+      const float2 tot = block_sum2(tq, tk, red);
+      rq_full = rsqrtf(tot.x / (float)(a.q_group ? a.q_group : 1) + a.eps);
+      rk_full = rsqrtf(tot.y / (float)(a.k_group ? a.k_group : 1) + a.eps);
+      if (j == 0) {
         if (full_q) a.rq[t] = rq_full;
         if (full_k) a.rk[t] = rk_full;
       }
     }
-    const float p = (float)a.pos[t];
 #pragma unroll
-    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
-      const int h = warp + i * kQkvWarps;
-      if (h >= NH) continue;
-      const bool isq = h < a.Hq;
-      const int hl = isq ? h : h - a.Hq;  // head index within q or k
-      const int G = isq ? a.q_group : a.k_group;
-      const float* wt = isq ? a.qw : a.kw;
-      float r = 1.f;
-      if (G == D) {
-        float s = 0.f;
+    for (int i = 0; i < MQ; ++i)
+      qkv_fwd_chunk<D>(xq[i], sq[i], j + kQkvThreads * i, nqc, a.q_group, a.qw, rq_full, a.rq, a.Hq, t,
+                       a.q + (size_t)t * nq, cs, sn, o, first_half, a.eps, lane);
 #pragma unroll
-        for (int c = 0; c < C; ++c) s += x[i][c] * x[i][c];
-        r = rsqrtf(warp_sum(s) / (float)D + a.eps);
-        if (lane == 0) (isq ? a.rq : a.rk)[(size_t)t * (isq ? a.Hq : a.Hkv) + hl] = r;
-      } else if (G) {
-        r = isq ? rq_full : rk_full;
-      }
-      float y[C];
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const int e = lane + 32 * c;
-        const float wv = G == D ? wt[e] : (G ? wt[hl * D + e] : 1.f);
-        y[c] = G ? x[i][c] * r * wv : x[i][c];
-      }
-      __nv_bfloat16* dst = isq ? a.q + ((size_t)t * a.Hq + hl) * D : a.k + ((size_t)t * a.Hkv + hl) * D;
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const int e = lane + 32 * c;
-        float sn, cs;
-        sincosf(p * a.inv_freq[e], &sn, &cs);
-        dst[e] = __float2bfloat16(y[c] * cs - y[c + HC] * sn);
-        dst[e + D / 2] = __float2bfloat16(y[c + HC] * cs + y[c] * sn);
-      }
-    }
-    for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
-      *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + i) = *reinterpret_cast<const uint4*>(row + nq + nk + i);
+    for (int i = 0; i < MK; ++i)
+      qkv_fwd_chunk<D>(xk[i], sk[i], j + kQkvThreads * i, nkc, a.k_group, a.kw, rk_full, a.rk, a.Hkv, t,
+                       a.k + (size_t)t * nk, cs, sn, o, first_half, a.eps, lane);
+    for (int c = j; c < nkc; c += kQkvThreads)
+      *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + 8 * c) = *reinterpret_cast<const uint4*>(row + nq + nk + 8 * c);
   }
 }
 
+// Backward, phase 1 of a chunk: load, undo the rotation (g = R^T d), return the norm dot partial.
 template <int D>
-__global__ void __launch_bounds__(256) qkv_rope_bwd_kernel(QkvArgs a) {
-  constexpr int C = D / 32;
-  constexpr int HC = C / 2;
-  __shared__ float red[2][kQkvWarps];
-  __shared__ float sdw[2][kQkvWarps][D];  // per-head norm weights: per-warp partials
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int NH = a.Hq + a.Hkv;
-  const int width = (a.Hq + 2 * a.Hkv) * D;
+PM_DEVICE float qkv_bwd_load(const __nv_bfloat16* dsrc, const __nv_bfloat16* xsrc, int c, int nch, int G,
+                             const float* wt, float (&x)[8], float (&g)[8], const float (&cs)[8],
+                             const float (&sn)[8], int o, bool first_half) {
+  constexpr int PX = D / 16;
+  float d[8];
+  if (c < nch) {
+    load8(dsrc + 8 * c, d);
+    load8(xsrc + 8 * c, x);
+  } else {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) { d[e] = 0.f; x[e] = 0.f; }
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    const float pd = __shfl_xor_sync(0xffffffffu, d[e], PX);
+    g[e] = first_half ? d[e] * cs[e] + pd * sn[e] : d[e] * cs[e] - pd * sn[e];
+  }
+  float dot = 0.f;
+  if (G && c < nch) {
+    float w8[8];
+    if (G == D) load8f(wt + o, w8);
+    else load8f(wt + 8 * c, w8);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dot += w8[e] * g[e] * x[e];
+  }
+  return dot;
+}
+
+// Backward, phase 2 of a chunk: input gradient through the norm, weight-gradient partials.
+template <int D>
+PM_DEVICE void qkv_bwd_store(const float (&x)[8], const float (&g)[8], float dot_part, float dot_full, int c, int nch,
+                             int G, const float* wt, const float* rsave, int H, int t, __nv_bfloat16* dst,
+                             float (&dwa)[8], int o) {
+  constexpr int HL = D / 8;
+  float dx[8];
+  if (!G) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dx[e] = g[e];
+  } else {
+    float r, dot;
+    if (G == D) {
+      dot = head_sum<HL>(dot_part);
+      r = c < nch ? rsave[(size_t)t * H + (8 * c) / D] : 0.f;
+    } else {
+      dot = dot_full;
+      r = rsave[t];
+    }
+    float w8[8];
+    if (G == D) load8f(wt + o, w8);
+    else if (c < nch) load8f(wt + 8 * c, w8);
+    else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) w8[e] = 0.f;
+    }
+    const float coef = r * r * r * dot / (float)G;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      dx[e] = r * w8[e] * g[e] - x[e] * coef;
+      dwa[e] += g[e] * x[e] * r;
+    }
+  }
+  if (c < nch) store8(dst + 8 * c, dx);
+}
+
+// Norm-weight gradient flush: full-width norms own distinct weights per chunk; per-head
+// norms share weights o..o+7 across heads (summed over lanes, then warps in shared memory).
+template <int D, int M>
+PM_DEVICE void qkv_dw_flush(const float (&dwa)[M][8], int nch, int G, float* dw, float (*sdw_part)[D], int o) {
+  constexpr int HL = D / 8;
+  const int j = threadIdx.x, lane = j & 31, warp = j >> 5;
+  if (!G || dw == nullptr) return;
+  if (G > D) {
+#pragma unroll
+    for (int i = 0; i < M; ++i) {
+      const int c = j + kQkvThreads * i;
+      if (c < nch)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(&dw[8 * c + e], dwa[i][e]);
+    }
+    return;
+  }
+  float v[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    v[e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < M; ++i) v[e] += dwa[i][e];
+#pragma unroll
+    for (int off = HL; off < 32; off <<= 1) v[e] += __shfl_xor_sync(0xffffffffu, v[e], off);
+  }
+  if (lane < HL) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sdw_part[warp][o + e] = v[e];
+  }
+}
+
+template <int D, int MQ, int MK>
+__global__ void __launch_bounds__(kQkvThreads) qkv_rope_bwd_kernel(QkvArgs a) {
+  constexpr int NW = kQkvThreads / 32;
+  __shared__ float red[2][NW];
+  __shared__ float sdw[2][NW][D];  // per-head norm weights: per-warp partials
+  const int j = threadIdx.x;
   const int nq = a.Hq * D, nk = a.Hkv * D;
+  const int nqc = nq / 8, nkc = nk / 8;
+  const int width = nq + 2 * nk;
+  const int o = (8 * j) % D;
+  const bool first_half = o < D / 2;
+  const int ai = o % (D / 2);
   const bool full_q = a.q_group > D, full_k = a.k_group > D;
-  float dwacc[kMaxHeadsPerWarp][C];
+  float dwq[MQ][8], dwk[MK][8];
 #pragma unroll
-  for (int i = 0; i < kMaxHeadsPerWarp; ++i)
+  for (int e = 0; e < 8; ++e) {
 #pragma unroll
-    for (int c = 0; c < C; ++c) dwacc[i][c] = 0.f;
+    for (int i = 0; i < MQ; ++i) dwq[i][e] = 0.f;
+#pragma unroll
+    for (int i = 0; i < MK; ++i) dwk[i][e] = 0.f;
+  }
   for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
     const __nv_bfloat16* row = a.qkv + (size_t)t * width;
     __nv_bfloat16* drow = a.dqkv + (size_t)t * width;
-    const float p = (float)a.pos[t];
-    float x[kMaxHeadsPerWarp][C], g[kMaxHeadsPerWarp][C];
-    float dotq = 0.f, dotk = 0.f;
+    int p = a.pos[t];
+    if (p < 0 || p >= a.rope_len) {
+      if (j == 0) set_error(kErrBounds);
+      p = 0;
+    }
+    float cs[8], sn[8];
+    load_rope(a.rope + (size_t)p * (D / 2) + ai, cs, sn);
+    float xq[MQ][8], gq[MQ][8], xk[MK][8], gk[MK][8], dq_h[MQ], dk_h[MK];
+    float pq = 0.f, pk = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
-      const int h = warp + i * kQkvWarps;
-      if (h >= NH) {
+    for (int i = 0; i < MQ; ++i) {
+      dq_h[i] = qkv_bwd_load<D>(a.dq + (size_t)t * nq, row, j + kQkvThreads * i, nqc, a.q_group, a.qw, xq[i], gq[i],
+                                cs, sn, o, first_half);
+      pq += dq_h[i];
+    }
 #pragma unroll
-        for (int c = 0; c < C; ++c) { x[i][c] = 0.f; g[i][c] = 0.f; }
-        continue;
-      }
-      const bool isq = h < a.Hq;
-      const int hl = isq ? h : h - a.Hq;
-      const __nv_bfloat16* src = isq ? a.dq + ((size_t)t * a.Hq + hl) * D : a.dk + ((size_t)t * a.Hkv + hl) * D;
-#pragma unroll
-      for (int c = 0; c < HC; ++c) {
-        const int e = lane + 32 * c;
-        float sn, cs;
-        sincosf(p * a.inv_freq[e], &sn, &cs);
-        const float d0 = __bfloat162float(src[e]), d1 = __bfloat162float(src[e + D / 2]);
-        g[i][c] = d0 * cs + d1 * sn;
-        g[i][c + HC] = -d0 * sn + d1 * cs;
-      }
-      const int G = isq ? a.q_group : a.k_group;
-      const float* wt = isq ? a.qw : a.kw;
-      float dot = 0.f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const int e = lane + 32 * c;
-        x[i][c] = __bfloat162float(row[h * D + e]);
-        const float wv = G == D ? wt[e] : (G ? wt[hl * D + e] : 1.f);
-        dot += wv * g[i][c] * x[i][c];
-      }
-      if (G > D) { if (isq) dotq += dot; else dotk += dot; }
+    for (int i = 0; i < MK; ++i) {
+      dk_h[i] = qkv_bwd_load<D>(a.dk + (size_t)t * nk, row + nq, j + kQkvThreads * i, nkc, a.k_group, a.kw, xk[i],
+                                gk[i], cs, sn, o, first_half);
+      pk += dk_h[i];
     }
     float tq = 0.f, tk = 0.f;
     if (full_q || full_k) {
-      const float wq = warp_sum(dotq), wk = warp_sum(dotk);
-      __syncthreads();
-      if (lane == 0) { red[0][warp] = wq; red[1][warp] = wk; }
-      __syncthreads();
-#pragma unroll
-      for (int w = 0; w < kQkvWarps; ++w) { tq += red[0][w]; tk += red[1][w]; }
+      const float2 tot = block_sum2(pq, pk, red);
+      tq = tot.x;
+      tk = tot.y;
     }
 #pragma unroll
-    for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
-      const int h = warp + i * kQkvWarps;
-      if (h >= NH) continue;
-      const bool isq = h < a.Hq;
-      const int hl = isq ? h : h - a.Hq;
-      const int G = isq ? a.q_group : a.k_group;
-      const float* wt = isq ? a.qw : a.kw;
-      __nv_bfloat16* dst = drow + h * D;
-      if (!G) {
+    for (int i = 0; i < MQ; ++i)
+      qkv_bwd_store<D>(xq[i], gq[i], dq_h[i], tq, j + kQkvThreads * i, nqc, a.q_group, a.qw, a.rq, a.Hq, t, drow,
+                       dwq[i], o);
 #pragma unroll
-        for (int c = 0; c < C; ++c) dst[lane + 32 * c] = __float2bfloat16(g[i][c]);
-        continue;
-      }
-      float r, dot;
-      if (G == D) {
-        r = (isq ? a.rq : a.rk)[(size_t)t * (isq ? a.Hq : a.Hkv) + hl];
-        float d = 0.f;
-#pragma unroll
-        for (int c = 0; c < C; ++c) d += wt[lane + 32 * c] * g[i][c] * x[i][c];
-        dot = warp_sum(d);
-      } else {
-        r = (isq ? a.rq : a.rk)[t];
-        dot = isq ? tq : tk;
-      }
-      const float coef = r * r * r * dot / (float)G;
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const int e = lane + 32 * c;
-        const float wv = G == D ? wt[e] : wt[hl * D + e];
-        dst[e] = __float2bfloat16(r * wv * g[i][c] - x[i][c] * coef);
-        dwacc[i][c] += g[i][c] * x[i][c] * r;
-      }
-    }
-    for (int i = threadIdx.x * 8; i < nk; i += blockDim.x * 8)
-      *reinterpret_cast<uint4*>(drow + nq + nk + i) = *reinterpret_cast<const uint4*>(a.dv + (size_t)t * nk + i);
+    for (int i = 0; i < MK; ++i)
+      qkv_bwd_store<D>(xk[i], gk[i], dk_h[i], tk, j + kQkvThreads * i, nkc, a.k_group, a.kw, a.rk, a.Hkv, t,
+                       drow + nq, dwk[i], o);
+    for (int c = j; c < nkc; c += kQkvThreads)
+      *reinterpret_cast<uint4*>(drow + nq + nk + 8 * c) = *reinterpret_cast<const uint4*>(a.dv + (size_t)t * nk + 8 * c);
   }
-  // weight gradients: full-width norms own one element per (head, lane, c) -> direct atomics;
-  // per-head norms reduce over the warp's heads, then over the 8 warps in shared memory.
-  float hq[C], hk[C];
+  qkv_dw_flush<D, MQ>(dwq, nqc, a.q_group, a.dqw, sdw[0], o);
+  qkv_dw_flush<D, MK>(dwk, nkc, a.k_group, a.dkw, sdw[1], o);
+  __syncthreads();
 #pragma unroll
-  for (int c = 0; c < C; ++c) { hq[c] = 0.f; hk[c] = 0.f; }
-#pragma unroll
-  for (int i = 0; i < kMaxHeadsPerWarp; ++i) {
-    const int h = warp + i * kQkvWarps;
-    if (h >= NH) continue;
-    const bool isq = h < a.Hq;
-    const int hl = isq ? h : h - a.Hq;
-    const int G = isq ? a.q_group : a.k_group;
-    if (!G) continue;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int e = lane + 32 * c;
-      if (G == D) { if (isq) hq[c] += dwacc[i][c]; else hk[c] += dwacc[i][c]; }
-      else atomicAdd(&(isq ? a.dqw : a.dkw)[hl * D + e], dwacc[i][c]);
-    }
-  }
-  if (a.q_group == D || a.k_group == D) {
-#pragma unroll
-    for (int c = 0; c < C; ++c) { sdw[0][warp][lane + 32 * c] = hq[c]; sdw[1][warp][lane + 32 * c] = hk[c]; }
-    __syncthreads();
-    for (int e = threadIdx.x; e < 2 * D; e += blockDim.x) {
-      const int which = e / D, j = e % D;
+  for (int part = 0; part < 2; ++part) {
+    const int G = part ? a.k_group : a.q_group;
+    float* dw = part ? a.dkw : a.dqw;
+    if (G != D || dw == nullptr) continue;
+    for (int e = threadIdx.x; e < D; e += kQkvThreads) {
       float s = 0.f;
 #pragma unroll
-      for (int w = 0; w < kQkvWarps; ++w) s += sdw[which][w][j];
-      if (which == 0 && a.q_group == D) atomicAdd(&a.dqw[j], s);
-      if (which == 1 && a.k_group == D) atomicAdd(&a.dkw[j], s);
+      for (int w = 0; w < NW; ++w) s += sdw[part][w][e];
+      atomicAdd(&dw[e], s);
     }
   }
 }
 
+#define PM_QKV_DISPATCH(KERNEL, D_, MQ_, MK_, GRID, ARGS)                                              \
+  do {                                                                                                 \
+    auto st = at::cuda::getCurrentCUDAStream();                                                        \
+    if (D_ == 128) {                                                                                   \
+      if (MQ_ == 1 && MK_ == 1) KERNEL<128, 1, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);                 \
+      else if (MQ_ == 2 && MK_ == 1) KERNEL<128, 2, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);            \
+      else if (MQ_ <= 4 && MK_ == 1) KERNEL<128, 4, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);            \
+      else KERNEL<128, 4, 2><<<GRID, kQkvThreads, 0, st>>>(ARGS);                                      \
+    } else {                                                                                           \
+      if (MQ_ == 1 && MK_ == 1) KERNEL<64, 1, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);                  \
+      else if (MQ_ == 2 && MK_ == 1) KERNEL<64, 2, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);             \
+      else if (MQ_ <= 4 && MK_ == 1) KERNEL<64, 4, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);             \
+      else KERNEL<64, 4, 2><<<GRID, kQkvThreads, 0, st>>>(ARGS);                                       \
+    }                                                                                                  \
+  } while (0)
+
+static void qkv_chunk_counts(int64_t Hq, int64_t Hkv, int64_t D, int& mq, int& mk) {
+  const int64_t nqc = Hq * D / 8, nkc = Hkv * D / 8;
+  TORCH_CHECK(nqc <= 4 * kQkvThreads, "q width must be at most ", 32 * kQkvThreads, " elements");
+  TORCH_CHECK(nkc <= 2 * kQkvThreads, "k width must be at most ", 16 * kQkvThreads, " elements");
+  mq = nqc <= kQkvThreads ? 1 : (nqc <= 2 * kQkvThreads ? 2 : 4);
+  mk = nkc <= kQkvThreads ? 1 : 2;
+}
+
+static void check_rope_table(const torch::Tensor& rope, int64_t D) {
+  TORCH_CHECK(rope.is_cuda() && rope.scalar_type() == torch::kFloat32 && rope.is_contiguous(), "rope table fp32");
+  TORCH_CHECK(rope.dim() == 3 && rope.size(1) == D / 2 && rope.size(2) == 2, "rope table must be [L, D/2, 2]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(rope.data_ptr()) & 15) == 0, "rope table must be 16-byte aligned");
+}
+
 // Returns q [T,Hq,D], k [T,Hkv,D], v [T,Hkv,D], rstd_q, rstd_k.
-std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor rope,
                                         c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw, int64_t Hq,
                                         int64_t Hkv, int64_t D, int64_t q_group, int64_t k_group, double eps) {
   TORCH_CHECK(qkv.is_cuda() && qkv.scalar_type() == torch::kBFloat16 && qkv.is_contiguous(), "qkv contiguous bf16");
   TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * D, "qkv width");
   TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
-  TORCH_CHECK(pos.scalar_type() == torch::kInt32 && inv_freq.scalar_type() == torch::kFloat32, "pos int32, inv_freq fp32");
-  PM_CHECK_CUDA(pos); PM_CHECK_CUDA(inv_freq); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
+  TORCH_CHECK(pos.scalar_type() == torch::kInt32, "pos must be int32");
+  PM_CHECK_CUDA(pos); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
+  check_rope_table(rope, D);
   TORCH_CHECK(!q_group || (qw.has_value() && qw->numel() == q_group), "q norm weight size");
   TORCH_CHECK(!k_group || (kw.has_value() && kw->numel() == k_group), "k norm weight size");
+  TORCH_CHECK(!q_group || q_group == D || q_group == Hq * D, "q norm group: head_dim or full width");
+  TORCH_CHECK(!k_group || k_group == D || k_group == Hkv * D, "k norm group: head_dim or full width");
   const int T = (int)(qkv.numel() / qkv.size(-1));
   TORCH_CHECK(pos.numel() == T, "positions");
   c10::cuda::CUDAGuard guard(qkv.device());
@@ -472,42 +616,41 @@ std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, to
   memset(&a, 0, sizeof(a));
   a.T = T; a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.D = (int)D; a.q_group = (int)q_group; a.k_group = (int)k_group;
   a.eps = (float)eps;
-  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>(); a.inv_freq = inv_freq.data_ptr<float>();
+  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>();
+  a.rope = reinterpret_cast<const float2*>(rope.data_ptr<float>()); a.rope_len = (int)rope.size(0);
   a.qw = q_group ? qw->data_ptr<float>() : nullptr;
   a.kw = k_group ? kw->data_ptr<float>() : nullptr;
   a.q = (__nv_bfloat16*)q.data_ptr(); a.k = (__nv_bfloat16*)k.data_ptr(); a.v = (__nv_bfloat16*)v.data_ptr();
   a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
-  TORCH_CHECK(Hq + Hkv <= kQkvWarps * kMaxHeadsPerWarp, "at most 64 q+k heads");
-  TORCH_CHECK(!q_group || q_group == D || q_group == Hq * D, "q norm group: head_dim or full width");
-  TORCH_CHECK(!k_group || k_group == D || k_group == Hkv * D, "k norm group: head_dim or full width");
+  int mq, mk;
+  qkv_chunk_counts(Hq, Hkv, D, mq, mk);
   const int grid = std::min(T, sm_count() * 8);
-  if (D == 128) qkv_rope_fwd_kernel<128><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  else if (D == 64) qkv_rope_fwd_kernel<64><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  else TORCH_CHECK(false, "head_dim must be 64 or 128");
+  PM_QKV_DISPATCH(qkv_rope_fwd_kernel, D, mq, mk, grid, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {q, k, v, rq, rk};
 }
 
 // Returns dqkv; accumulates d(q_norm weight), d(k_norm weight) into dqw/dkw (fp32).
 torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv, torch::Tensor pos,
-                           torch::Tensor inv_freq, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
+                           torch::Tensor rope, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
                            torch::Tensor rq, torch::Tensor rk, c10::optional<torch::Tensor> dqw,
                            c10::optional<torch::Tensor> dkw, int64_t Hq, int64_t Hkv, int64_t D, int64_t q_group,
                            int64_t k_group) {
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "grads must be contiguous");
   PM_CHECK_CUDA(dq); PM_CHECK_CUDA(dk); PM_CHECK_CUDA(dv); PM_CHECK_CUDA(qkv); PM_CHECK_CUDA(pos);
-  PM_CHECK_CUDA(inv_freq); PM_CHECK_CUDA(rq); PM_CHECK_CUDA(rk); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
+  PM_CHECK_CUDA(rq); PM_CHECK_CUDA(rk); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
   PM_CHECK_CUDA_OPT(dqw); PM_CHECK_CUDA_OPT(dkw);
+  check_rope_table(rope, D);
+  TORCH_CHECK(D == 64 || D == 128, "head_dim must be 64 or 128");
   const int T = (int)(qkv.numel() / qkv.size(-1));
   c10::cuda::CUDAGuard guard(qkv.device());
   auto dqkv = torch::empty_like(qkv);
   if (T == 0) return dqkv;
-  const int qg = q_group ? (int)(Hq * D / q_group) : 0;
-  const int kg = k_group ? (int)(Hkv * D / k_group) : 0;
   QkvArgs a;
   memset(&a, 0, sizeof(a));
   a.T = T; a.Hq = (int)Hq; a.Hkv = (int)Hkv; a.D = (int)D; a.q_group = (int)q_group; a.k_group = (int)k_group;
-  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>(); a.inv_freq = inv_freq.data_ptr<float>();
+  a.qkv = (const __nv_bfloat16*)qkv.data_ptr(); a.pos = pos.data_ptr<int>();
+  a.rope = reinterpret_cast<const float2*>(rope.data_ptr<float>()); a.rope_len = (int)rope.size(0);
   a.qw = q_group ? qw->data_ptr<float>() : nullptr;
   a.kw = k_group ? kw->data_ptr<float>() : nullptr;
   a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
@@ -515,11 +658,10 @@ torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
   a.dv = (const __nv_bfloat16*)dv.data_ptr(); a.dqkv = (__nv_bfloat16*)dqkv.data_ptr();
   a.dqw = q_group ? dqw->data_ptr<float>() : nullptr;
   a.dkw = k_group ? dkw->data_ptr<float>() : nullptr;
-  TORCH_CHECK(Hq + Hkv <= kQkvWarps * kMaxHeadsPerWarp, "at most 64 q+k heads");
+  int mq, mk;
+  qkv_chunk_counts(Hq, Hkv, D, mq, mk);
   const int grid = std::min(T, sm_count() * 4);
-  if (D == 128) qkv_rope_bwd_kernel<128><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  else if (D == 64) qkv_rope_bwd_kernel<64><<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(a);
-  else TORCH_CHECK(false, "head_dim must be 64 or 128");
+  PM_QKV_DISPATCH(qkv_rope_bwd_kernel, D, mq, mk, grid, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dqkv;
 }

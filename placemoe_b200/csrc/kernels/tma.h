@@ -45,9 +45,10 @@ inline EncodeTiledFn encode_tiled_fn() {
 }
 
 // Row-major bf16 matrix [rows, cols] with leading dimension `ld` (elements);
-// box = {box_cols, box_rows}, 128-byte swizzle.
+// box = {box_cols, box_rows}, 128-byte swizzle (64-byte for 32-column boxes).
 inline CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols,
                                      uint32_t box_rows) {
+  const CUtensorMapSwizzle swz = box_cols * 2 == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base must be 16-byte aligned");
   if ((ld * 2) % 16 != 0) throw std::runtime_error("TMA row stride must be a multiple of 16 bytes");
   CUtensorMap m;
@@ -56,7 +57,7 @@ inline CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t c
   cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
-                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled(2d) failed: " + std::to_string((int)r));
   return m;
@@ -98,6 +99,11 @@ inline CUtensorMap make_tmap_f32_out(void* base, uint64_t batch, uint64_t rows, 
                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled(f32 out) failed: " + std::to_string((int)r));
   return m;
+}
+
+// bf16 epilogue boxes: 32 rows x 32 columns, 64-byte swizzle.
+inline CUtensorMap make_tmap_bf16_epi(const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+  return make_tmap_2d_bf16(base, rows, cols, ld, 32, 32);
 }
 
 }  // namespace pm

@@ -8,20 +8,21 @@ namespace pm {
 // gemm_dense.cu, gemm_moe_fwd.cu, gemm_moe_bwd.cu (kernel template in gemm_sm100.cuh)
 void dense_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate);
 void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
-                    c10::optional<torch::Tensor> gu_out);
-void moe_grouped_gemm(torch::Tensor a, torch::Tensor w, torch::Tensor offsets, torch::Tensor out, bool b_mn);
+                    c10::optional<torch::Tensor> gu_out, int64_t align);
+void moe_grouped_gemm(torch::Tensor a, torch::Tensor w, torch::Tensor offsets, torch::Tensor out, bool b_mn,
+                      int64_t align);
 void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor offsets, torch::Tensor gu,
-                           torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale);
+                           torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale, int64_t align);
 void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate);
 
 // norm_rope.cu
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw);
-std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor inv_freq,
+std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor rope,
                                         c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw, int64_t Hq,
                                         int64_t Hkv, int64_t D, int64_t q_group, int64_t k_group, double eps);
 torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv, torch::Tensor qkv, torch::Tensor pos,
-                           torch::Tensor inv_freq, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
+                           torch::Tensor rope, c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw,
                            torch::Tensor rq, torch::Tensor rk, c10::optional<torch::Tensor> dqw,
                            c10::optional<torch::Tensor> dkw, int64_t Hq, int64_t Hkv, int64_t D, int64_t q_group,
                            int64_t k_group);

@@ -70,7 +70,8 @@ class Attention(nn.Module):
         # x: [T, H] (T = batch * seq_len, packed by sequence)
         qkv = mp_ops.linear(x, self.qkv_proj)
         q, k, v = norm_ops.qkv_norm_rope(qkv, self.q_norm, self.k_norm, pos, self.inv_freq, self.hq, self.hkv,
-                                         self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps)
+                                         self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps,
+                                         max_pos=seq_len)
         o = attn_ops.causal_attention(q, k, v, seq_len)  # [T, Hq, D]
         o = o.reshape(o.shape[0], -1)
         return mp_ops.linear(o, self.o_proj)

@@ -29,12 +29,22 @@ import torch.nn.functional as F
 
 from ._ext import kernels
 
-ALIGN = 128
+ALIGN = 128  # expert segment alignment for single-CTA GEMM tiles
+PAIR_ALIGN = 256  # alignment for CTA-pair (cta_group::2) tiles of 256 rows
+# Average rows per expert slot from which 256-row segments pay: pair tiles move a third
+# fewer operand bytes per SM, and the extra padding (~64 rows per slot on average) is
+# small against segments of this length.
+PAIR_MIN_ROWS = 768
 
 
-def capacity_rows(num_tokens: int, top_k: int, num_slots: int) -> int:
+def segment_align(assignments: int, num_slots: int) -> int:
+    """Segment alignment of a dispatch plan with ``assignments`` rows over ``num_slots`` slots."""
+    return PAIR_ALIGN if assignments >= PAIR_MIN_ROWS * max(num_slots, 1) else ALIGN
+
+
+def capacity_rows(num_tokens: int, top_k: int, num_slots: int, align: int = ALIGN) -> int:
     """Upper bound of dispatched rows: every assignment plus per-slot padding."""
-    return num_tokens * top_k + num_slots * (ALIGN - 1) + ALIGN
+    return num_tokens * top_k + num_slots * (align - 1) + align
 
 
 @dataclass
@@ -101,27 +111,58 @@ def _accum_main_grad(param: torch.Tensor) -> torch.Tensor:
     return g
 
 
+def wgrad_target(param: torch.Tensor) -> tuple[torch.Tensor, bool]:
+    """(main_grad buffer, accumulate) for a weight-gradient GEMM.
+
+    After ``mark_grads_stale`` the buffer holds last step's values: the first
+    GEMM of the step overwrites it (an fp32 store instead of a read-modify-
+    write, and no zero fill) and later micro-batches accumulate.
+    """
+    g = _accum_main_grad(param)
+    if getattr(param, "_main_grad_stale", False):
+        param._main_grad_stale = False
+        return g, False
+    return g, True
+
+
+def mark_grads_stale(params) -> None:
+    """Start a new accumulation without zeroing: the next weight-gradient GEMM overwrites."""
+    for p in params:
+        if getattr(p, "main_grad", None) is not None:
+            p._main_grad_stale = True
+
+
+def settle_stale_grads(params) -> None:
+    """Zero the buffers that no GEMM overwrote since ``mark_grads_stale`` (unused parameters)."""
+    for p in params:
+        if getattr(p, "_main_grad_stale", False):
+            p.main_grad.zero_()
+            p._main_grad_stale = False
+
+
 class ExpertFFN(torch.autograd.Function):
     """Grouped SwiGLU expert FFN over dispatched rows.
 
-    Inputs: xd [rows, H] bf16 (expert-contiguous, 128-aligned segments),
-    scale [rows] fp32 routing weights, w1 [S, 2I, H] / w2 [S, H, I] bf16 compute
-    copies, offsets [S+1] int32.  Weight gradients are accumulated into the
-    fp32 ``main_grad`` of ``p1`` / ``p2`` (the master parameters).
+    Inputs: xd [rows, H] bf16 (expert-contiguous segments aligned to ``align``
+    rows: 128, or 256 for CTA-pair tiles), scale [rows] fp32 routing weights,
+    w1 [S, 2I, H] / w2 [S, H, I] bf16 compute copies, offsets [S+1] int32.
+    Weight gradients are accumulated into the fp32 ``main_grad`` of ``p1`` /
+    ``p2`` (the master parameters).
     """
 
     @staticmethod
-    def forward(ctx, xd, scale, w1, w2, offsets, p1, p2):
+    def forward(ctx, xd, scale, w1, w2, offsets, p1, p2, align=ALIGN):
         kn = kernels()
         rows = xd.shape[0]
         inter = w1.shape[1] // 2
         h = torch.empty(rows, inter, device=xd.device, dtype=torch.bfloat16)
         gu = torch.empty(rows, 2 * inter, device=xd.device, dtype=torch.bfloat16)
-        kn.moe_fc1_swiglu(xd, w1, offsets, scale, h, gu)
+        kn.moe_fc1_swiglu(xd, w1, offsets, scale, h, gu, align)
         y = torch.empty(rows, w2.shape[1], device=xd.device, dtype=torch.bfloat16)
-        kn.moe_grouped_gemm(h, w2, offsets, y, False)
+        kn.moe_grouped_gemm(h, w2, offsets, y, False, align)
         ctx.save_for_backward(xd, scale, w1, w2, offsets, h, gu)
         ctx.params = (p1, p2)
+        ctx.align = align
         return y
 
     @staticmethod
@@ -133,14 +174,14 @@ class ExpertFFN(torch.autograd.Function):
         rows = xd.shape[0]
         dgu = torch.empty_like(gu)
         dscale = torch.zeros(rows, device=xd.device, dtype=torch.float32)
-        kn.moe_fc2_dgrad_dswiglu(dy, w2, offsets, gu, scale, dgu, dscale)
+        kn.moe_fc2_dgrad_dswiglu(dy, w2, offsets, gu, scale, dgu, dscale, ctx.align)
         dx = torch.empty_like(xd)
-        kn.moe_grouped_gemm(dgu, w1, offsets, dx, True)
+        kn.moe_grouped_gemm(dgu, w1, offsets, dx, True, ctx.align)
         if p2 is not None and p2.requires_grad:
-            kn.moe_wgrad(dy, h, offsets, _accum_main_grad(p2), True)
+            kn.moe_wgrad(dy, h, offsets, *wgrad_target(p2))
         if p1 is not None and p1.requires_grad:
-            kn.moe_wgrad(dgu, xd, offsets, _accum_main_grad(p1), True)
-        return dx, dscale, None, None, None, None, None
+            kn.moe_wgrad(dgu, xd, offsets, *wgrad_target(p1))
+        return dx, dscale, None, None, None, None, None, None
 
 
 class _GatherRows(torch.autograd.Function):
@@ -246,12 +287,13 @@ def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=N
     aux = None
     if aux_coef:
         aux = _AuxLoss.apply(w, ps, cnt, t, k, float(aux_coef), holder)
-    cap = capacity_rows(t, k, num_slots)
-    offsets, counts, row_of, row_token, row_scale = kn.moe_plan(idx, lut, w.detach(), num_slots, cap, ALIGN)
+    align = segment_align(t * k, num_slots)
+    cap = capacity_rows(t, k, num_slots, align)
+    offsets, counts, row_of, row_token, row_scale = kn.moe_plan(idx, lut, w.detach(), num_slots, cap, align)
     end = offsets[num_slots:]
     scale = _ScaleGather.apply(w, row_scale, row_of)
     xd = _GatherRows.apply(x, row_token, end, row_of, cap)
-    yd = ExpertFFN.apply(xd, scale, w1_bf16, w2_bf16, offsets, p1, p2)
+    yd = ExpertFFN.apply(xd, scale, w1_bf16, w2_bf16, offsets, p1, p2, align)
     y = _SumRows.apply(yd, row_of, row_token, end, t)
     return y, aux, idx
 

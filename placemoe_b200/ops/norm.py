@@ -77,14 +77,29 @@ def qkv_rope_reference(qkv, pos, inv_freq, qw, kw, hq, hkv, d, q_group, k_group,
     return q.to(qkv.dtype), k.to(qkv.dtype), v.reshape(t, hkv, d).to(qkv.dtype)
 
 
+_ROPE_TABLES: dict = {}
+
+
+def rope_table(inv_freq: torch.Tensor, length: int) -> torch.Tensor:
+    """(cos, sin) of p * inv_freq for positions p < length: [length, D/2, 2] fp32 (cached)."""
+    key = (inv_freq.data_ptr(), inv_freq.device, inv_freq.numel())
+    tab = _ROPE_TABLES.get(key)
+    if tab is None or tab.shape[0] < length:
+        n = max(length, tab.shape[0] * 2 if tab is not None else 0)
+        ang = torch.arange(n, device=inv_freq.device, dtype=torch.float64)[:, None] * inv_freq.double()[None, :]
+        tab = torch.stack([torch.cos(ang), torch.sin(ang)], -1).float().contiguous()
+        _ROPE_TABLES[key] = tab
+    return tab
+
+
 class _QkvRope(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, qkv, qw, kw, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
+    def forward(ctx, qkv, qw, kw, pos, rope, hq, hkv, d, q_group, k_group, eps):
         qkv = qkv.contiguous()
         qwd = qw.detach() if qw is not None else None
         kwd = kw.detach() if kw is not None else None
-        q, k, v, rq, rk = kernels().qkv_rope_fwd(qkv, pos, inv_freq, qwd, kwd, hq, hkv, d, q_group, k_group, eps)
-        ctx.save_for_backward(qkv, pos, inv_freq, rq, rk)
+        q, k, v, rq, rk = kernels().qkv_rope_fwd(qkv, pos, rope, qwd, kwd, hq, hkv, d, q_group, k_group, eps)
+        ctx.save_for_backward(qkv, pos, rope, rq, rk)
         ctx.masters = (qw, kw)
         ctx.cfg = (hq, hkv, d, q_group, k_group)
         return q, k, v
@@ -93,7 +108,7 @@ class _QkvRope(torch.autograd.Function):
     def backward(ctx, dq, dk, dv):
         from .mp import main_grad
 
-        qkv, pos, inv_freq, rq, rk = ctx.saved_tensors
+        qkv, pos, rope, rq, rk = ctx.saved_tensors
         hq, hkv, d, q_group, k_group = ctx.cfg
         qw, kw = ctx.masters
 
@@ -104,24 +119,28 @@ class _QkvRope(torch.autograd.Function):
 
         bf = torch.bfloat16
         dqkv = kernels().qkv_rope_bwd(
-            dq.contiguous().to(bf), dk.contiguous().to(bf), dv.contiguous().to(bf), qkv, pos, inv_freq,
+            dq.contiguous().to(bf), dk.contiguous().to(bf), dv.contiguous().to(bf), qkv, pos, rope,
             qw.detach() if qw is not None else None, kw.detach() if kw is not None else None, rq, rk,
             acc(qw), acc(kw), hq, hkv, d, q_group, k_group,
         )
         return dqkv, None, None, None, None, None, None, None, None, None, None
 
 
-def qkv_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, hq, hkv, d, q_group, k_group, eps):
+def qkv_norm_rope(qkv, q_norm_w, k_norm_w, pos, inv_freq, hq, hkv, d, q_group, k_group, eps, max_pos=None):
     """Split a fused QKV projection [T, (hq+2hkv)*d] into rotated, normalised q, k and v.
 
     ``q_group``/``k_group`` are the RMSNorm group sizes (``d`` for per-head
     norms, the full width for OLMoE-style norms, 0 for none).  On CUDA the
-    norm weights are fp32 masters whose gradients accumulate into ``main_grad``.
+    norm weights are fp32 masters whose gradients accumulate into ``main_grad``
+    and the rotation reads a (cos, sin) table covering positions < ``max_pos``
+    (default: the number of tokens); a position outside it raises the device
+    error flag.
     """
     if not qkv.is_cuda:
         return qkv_rope_reference(qkv, pos, inv_freq, q_norm_w, k_norm_w, hq, hkv, d, q_group, k_group, eps)
     for w in (q_norm_w, k_norm_w):
         if w is not None and w.dtype != torch.float32:
             raise TypeError("QK-norm weights must be fp32 masters on the CUDA path")
-    return _QkvRope.apply(qkv.to(torch.bfloat16), q_norm_w, k_norm_w, pos.to(torch.int32), inv_freq, hq, hkv, d,
+    rope = rope_table(inv_freq, int(max_pos) if max_pos else qkv.shape[0])
+    return _QkvRope.apply(qkv.to(torch.bfloat16), q_norm_w, k_norm_w, pos.to(torch.int32), rope, hq, hkv, d,
                           q_group, k_group, eps)

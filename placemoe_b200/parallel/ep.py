@@ -183,10 +183,11 @@ def _cuda_local_experts(blk, recv_x, recv_row, recv_slot, recv_w, nrows):
     n = recv_slot.shape[0]
     spr = blk.num_local_slots
     k = blk.cfg.num_experts_per_tok
-    cap = moe_ops.capacity_rows(n, 1, spr)
+    align = moe_ops.segment_align(n, spr)
+    cap = moe_ops.capacity_rows(n, 1, spr, align)
     slot32 = recv_slot.to(torch.int32).reshape(n, 1).contiguous()
     offsets, counts, row_of, row_token, row_scale = kn.moe_plan(slot32, None, recv_w.detach().contiguous(), spr,
-                                                                cap, moe_ops.ALIGN)
+                                                                cap, align)
     end = offsets[spr:]
     # dispatched row -> received row.  Rows at or beyond offsets[spr] are not written by the
     # plan (uninitialised), so they are masked by the device-side end before any indexing.
@@ -203,5 +204,5 @@ def _cuda_local_experts(blk, recv_x, recv_row, recv_slot, recv_w, nrows):
     scale = moe_ops._ScaleGather.apply(recv_w, row_scale, row_of)
     w1, w2 = blk.compute_weights()
     xd = moe_ops._GatherRows.apply(recv_x.contiguous(), row_src.contiguous(), end, table, cap)
-    yd = moe_ops.ExpertFFN.apply(xd, scale, w1, w2, offsets, blk.gate_up_proj, blk.down_proj)
+    yd = moe_ops.ExpertFFN.apply(xd, scale, w1, w2, offsets, blk.gate_up_proj, blk.down_proj, align)
     return moe_ops._SumRows.apply(yd, table, row_src.contiguous(), end, nrows)

@@ -177,7 +177,7 @@ class _P2PMoE(torch.autograd.Function):
         slots = torch.where(valid, rmeta[:, 1], torch.full_like(rmeta[:, 1], -1)).contiguous()
         rrow = torch.where(valid, rmeta[:, 0], torch.full_like(rmeta[:, 0], -1)).contiguous()
         rw = torch.where(valid, rmeta[:, 2].view(torch.float32), torch.zeros_like(rmeta[:, 2].view(torch.float32)))
-        loc = _local_plan(blk, rrow, slots, rw.contiguous(), R_cap, k)
+        loc = _local_plan(blk, rrow, slots, rw.contiguous(), R_cap, k, arena.tokens * k)
         # return address of every received assignment's routing-weight gradient
         asg_from = C[:, r, 1]
         a_idx = torch.arange(A_cap, device=dev)
@@ -191,9 +191,9 @@ class _P2PMoE(torch.autograd.Function):
         inter = w1.shape[1] // 2
         hbuf = torch.empty(loc["cap"], inter, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(loc["cap"], 2 * inter, device=dev, dtype=torch.bfloat16)
-        kn.moe_fc1_swiglu(xd, w1, loc["offsets"], loc["row_scale"], hbuf, gu)
+        kn.moe_fc1_swiglu(xd, w1, loc["offsets"], loc["row_scale"], hbuf, gu, loc["align"])
         yd = torch.empty(loc["cap"], h, device=dev, dtype=torch.bfloat16)
-        kn.moe_grouped_gemm(hbuf, w2, loc["offsets"], yd, False)
+        kn.moe_grouped_gemm(hbuf, w2, loc["offsets"], yd, False, loc["align"])
         _mark("fwd.expert_gemms")
         partial = torch.empty(R_cap, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(yd, loc["table"], partial)
@@ -225,6 +225,7 @@ class _P2PMoE(torch.autograd.Function):
         W, r = arena.world, arena.rank
         dev = dy.device
         R_cap = W * arena.tokens
+        _mark("start")
         dy = dy.contiguous().to(torch.bfloat16)
         # combine backward: dy rows to the destinations (same positions as the forward dispatch)
         tok = torch.arange(t, device=dev, dtype=torch.int32)
@@ -232,19 +233,22 @@ class _P2PMoE(torch.autograd.Function):
         ranks = torch.arange(W, device=dev, dtype=torch.int32)[None, :].expand(t, W).reshape(-1).contiguous()
         kn.p2p_put_rows(dy, src_rows, ranks, dst_row.reshape(-1).contiguous(), None, t * W, arena.peers,
                         arena.layout["recv_rows"], h)
+        _mark("bwd.dy_puts")
         arena.barrier()
+        _mark("bwd.dy_barrier")
         recv_dy = arena.view("recv_rows", (R_cap, h), torch.bfloat16)
         dyd = torch.empty(loc["cap"], h, device=dev, dtype=torch.bfloat16)
         kn.gather_rows(recv_dy, loc["row_src"], loc["end"], dyd)
         dgu = torch.empty_like(gu)
         dscale = torch.zeros(loc["cap"], device=dev, dtype=torch.float32)
-        kn.moe_fc2_dgrad_dswiglu(dyd, w2, loc["offsets"], gu, loc["row_scale"], dgu, dscale)
+        kn.moe_fc2_dgrad_dswiglu(dyd, w2, loc["offsets"], gu, loc["row_scale"], dgu, dscale, loc["align"])
         dxd = torch.empty_like(xd)
-        kn.moe_grouped_gemm(dgu, w1, loc["offsets"], dxd, True)
+        kn.moe_grouped_gemm(dgu, w1, loc["offsets"], dxd, True, loc["align"])
         if blk.down_proj.requires_grad:
-            kn.moe_wgrad(dyd, hbuf, loc["offsets"], moe_ops._accum_main_grad(blk.down_proj), True)
+            kn.moe_wgrad(dyd, hbuf, loc["offsets"], *moe_ops.wgrad_target(blk.down_proj))
         if blk.gate_up_proj.requires_grad:
-            kn.moe_wgrad(dgu, xd, loc["offsets"], moe_ops._accum_main_grad(blk.gate_up_proj), True)
+            kn.moe_wgrad(dgu, xd, loc["offsets"], *moe_ops.wgrad_target(blk.gate_up_proj))
+        _mark("bwd.expert_gemms")
         # dispatch backward: per received row, sum over its assignments -> back to the source
         dpart = torch.empty(R_cap, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(dxd, loc["table"], dpart)
@@ -257,11 +261,14 @@ class _P2PMoE(torch.autograd.Function):
         n_asg = C[:, r, 1].sum().to(torch.int32).reshape(1)
         kn.p2p_put_words(dw_asg.contiguous().view(torch.int32), loc["asg_src_rank"], loc["asg_src_idx"], n_asg,
                          dw_asg.numel(), arena.peers, arena.layout["back_words"])
+        _mark("bwd.back_puts")
         arena.barrier()
+        _mark("bwd.back_barrier")
         back = arena.view("back_rows", (R_cap, h), torch.bfloat16)
         dx = torch.empty(t, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(back, back_pos, dx)
         dw = arena.view("back_words", (R_cap * k,), torch.float32)[: t * k].clone().view(t, k)
+        _mark("bwd.token_sum")
         return dx, dw, None, None, None, None
 
 
@@ -279,13 +286,15 @@ def _return_targets(C: torch.Tensor, r: int, R_cap: int, dev):
             torch.where(valid, pos, torch.full_like(pos, -1)).to(torch.int32).contiguous())
 
 
-def _local_plan(blk, rrow, slots, rw, R_cap, k):
+def _local_plan(blk, rrow, slots, rw, R_cap, k, expected_asg):
     """Expert plan over received assignments (invalid ones carry slot -1)."""
     kn = moe_ops.kernels()
     A = slots.shape[0]
     spr = blk.num_local_slots
-    cap = moe_ops.capacity_rows(A, 1, spr)
-    offsets, counts, row_of, row_token, row_scale = kn.moe_plan(slots.view(A, 1), None, rw, spr, cap, moe_ops.ALIGN)
+    # alignment from the expected (balanced) share of assignments, not the capacity A
+    align = moe_ops.segment_align(expected_asg, spr)
+    cap = moe_ops.capacity_rows(A, 1, spr, align)
+    offsets, counts, row_of, row_token, row_scale = kn.moe_plan(slots.view(A, 1), None, rw, spr, cap, align)
     end = offsets[spr:]
     dev = slots.device
     in_plan = torch.arange(cap, device=dev, dtype=torch.int32) < end
@@ -302,7 +311,7 @@ def _local_plan(blk, rrow, slots, rw, R_cap, k):
     table[rr, pos] = torch.where(valid, row_of, torch.full_like(row_of, -1))
     table = table[:R_cap].contiguous()
     return {"cap": cap, "offsets": offsets, "end": end, "row_of": row_of, "row_src": row_src,
-            "row_scale": row_scale, "table": table}
+            "row_scale": row_scale, "table": table, "align": align}
 
 
 class P2PExpertParallel:

@@ -30,6 +30,7 @@ import torch.distributed as dist
 
 from ..models.config import MoEModelConfig, get_preset
 from ..models.moe_decoder import build_model
+from ..ops import moe as moe_ops
 from ..ops import mp as mp_ops
 from ..ops.optim import FusedAdamW
 from ..parallel.data_parallel import (expert_init_from_full, expert_topology, parallelize_model,
@@ -173,6 +174,7 @@ class Trainer:
         cfg = self.cfg
         # gradients of micro-batches were accumulated; average them
         nmb = max(1, cfg.batch_per_rank // max(1, cfg.micro_batch_size))
+        moe_ops.settle_stale_grads(self.model.expert_parameters())
         if self.world > 1:
             sync_replica_gradients(self.model, self.pstate.placements)
             if self.pstate.dense_bucket is not None:
@@ -220,17 +222,16 @@ class Trainer:
         self.zero_grad()
 
     def zero_grad(self):
+        expert = {id(p) for p in self.model.expert_parameters()}
         for p in self.model.parameters():
             p.grad = None
             g = getattr(p, "main_grad", None)
-            if g is not None and self.pstate.dense_bucket is None:
+            if g is not None and self.pstate.dense_bucket is None and id(p) not in expert:
                 g.zero_()
         if self.pstate.dense_bucket is not None:
             self.pstate.dense_bucket.zero()
-            for p in self.model.expert_parameters():
-                g = getattr(p, "main_grad", None)
-                if g is not None:
-                    g.zero_()
+        # expert gradients (the bulk) are overwritten by the step's first weight-gradient GEMM
+        moe_ops.mark_grads_stale(self.model.expert_parameters())
 
     def train(self, data_iter, steps: int | None = None, log=print):
         steps = steps or self.cfg.total_steps

@@ -76,15 +76,17 @@ def _segments(counts, align=128):
     return offs
 
 
+@pytest.mark.parametrize("align", [128, 256])
 @pytest.mark.parametrize("E,H,I", [(4, 256, 256), (8, 512, 384), (16, 2048, 1024)])
-def test_grouped_fc1_fc2_and_backward(E, H, I):
+def test_grouped_fc1_fc2_and_backward(E, H, I, align):
+    """align 256 runs the CTA-pair (cta_group::2) kernels."""
     from placemoe_b200.ops import kernels, check_device_error
 
     torch.manual_seed(3)
     counts = [int(c) for c in torch.randint(0, 300, (E,))]
     counts[0] = 0
-    offs = _segments(counts)
-    rows = offs[-1] + 128  # capacity larger than used rows
+    offs = _segments(counts, align)
+    rows = offs[-1] + align  # capacity larger than used rows
     x = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
     scale = torch.zeros(rows, device="cuda", dtype=torch.float32)
     for e in range(E):
@@ -96,17 +98,17 @@ def test_grouped_fc1_fc2_and_backward(E, H, I):
     k = kernels()
     h = torch.zeros(rows, I, device="cuda", dtype=torch.bfloat16)
     gu = torch.zeros(rows, 2 * I, device="cuda", dtype=torch.bfloat16)
-    k.moe_fc1_swiglu(x, w1, off_t, scale, h, gu)
+    k.moe_fc1_swiglu(x, w1, off_t, scale, h, gu, align)
     y = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
-    k.moe_grouped_gemm(h, w2, off_t, y, False)
+    k.moe_grouped_gemm(h, w2, off_t, y, False, align)
     dy = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
     for e in range(E):
         dy[offs[e]: offs[e] + counts[e]] = torch.randn(counts[e], H, device="cuda", dtype=torch.bfloat16)
     dgu = torch.zeros(rows, 2 * I, device="cuda", dtype=torch.bfloat16)
     dscale = torch.zeros(rows, device="cuda", dtype=torch.float32)
-    k.moe_fc2_dgrad_dswiglu(dy, w2, off_t, gu, scale, dgu, dscale)
+    k.moe_fc2_dgrad_dswiglu(dy, w2, off_t, gu, scale, dgu, dscale, align)
     dx = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
-    k.moe_grouped_gemm(dgu, w1, off_t, dx, True)
+    k.moe_grouped_gemm(dgu, w1, off_t, dx, True, align)
     dw1 = torch.zeros(E, 2 * I, H, device="cuda", dtype=torch.float32)
     dw2 = torch.zeros(E, H, I, device="cuda", dtype=torch.float32)
     k.moe_wgrad(dgu, x, off_t, dw1, False)

@@ -31,7 +31,8 @@ def test_rmsnorm_fwd_bwd():
     assert rel(w.grad, wr.grad) < 1e-2
 
 
-@pytest.mark.parametrize("hq,hkv,d,mode", [(16, 16, 128, "full"), (32, 4, 128, "per_head"), (8, 2, 64, "per_head")])
+@pytest.mark.parametrize("hq,hkv,d,mode", [(16, 16, 128, "full"), (32, 4, 128, "per_head"), (8, 2, 64, "per_head"),
+                                         (64, 32, 128, "per_head"), (24, 8, 64, "full")])
 def test_qkv_norm_rope(hq, hkv, d, mode):
     from placemoe_b200.ops.norm import qkv_norm_rope, rope_inv_freq
 
@@ -217,3 +218,19 @@ def test_attention_fwd_bwd(b, s, hq, hkv, d):
     torch.cuda.synchronize()
     check_device_error()
     assert math.isfinite(o.float().sum().item())
+
+
+def test_sq_norm_matches_torch():
+    from placemoe_b200.ops import kernels
+
+    torch.manual_seed(6)
+    gs = [torch.randn(n, device="cuda") for n in (1000, 65536 * 3 + 17, 7)]
+    gs.append(torch.randn(12345, device="cuda").bfloat16())
+    gs.append(torch.randn(20000, device="cuda").bfloat16()[1:])  # unaligned start
+    gs[-1] = gs[-1].contiguous()
+    weights = [1.0, 0.5, 2.0, 1.0, 0.25]
+    table, meta = kernels().sq_norm_build_table(gs, weights)
+    out = torch.zeros(1, device="cuda")
+    kernels().sq_norm(table, meta, out)
+    ref = sum(w * g.double().pow(2).sum() for g, w in zip(gs, weights))
+    assert abs(out.item() - ref.item()) / ref.item() < 1e-5
