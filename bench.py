@@ -47,6 +47,8 @@ def parse():
     p.add_argument("--artifact", default="")
     p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
     p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
+    p.add_argument("--recompute-expert-rows", action="store_true",
+                   help="re-gather dispatched expert inputs in the backward instead of keeping them (memory)")
     return p.parse_args()
 
 
@@ -136,7 +138,7 @@ def main():
     cfg = TrainConfig(model=args.model, seq_len=args.seq, batch_per_rank=args.batch_per_gpu,
                       micro_batch_size=args.micro_batch, redundant_slots_per_rank=args.redundant_slots,
                       placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1,
-                      ep_transport=args.ep_transport)
+                      ep_transport=args.ep_transport, recompute_expert_rows=args.recompute_expert_rows)
     trainer = Trainer(cfg, mcfg)
     pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank)
     dev_batches = [b.to("cuda") for b in pool.batches]
@@ -219,6 +221,7 @@ def main():
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": pool.bytes_per_batch,
                     "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e, 3), "last_loss": last},
             "gpu_launches": launches,
+            "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 2**30, 1),
             "model_tflops_per_gpu": round(flops / (ms / 1e3) / world / 1e12, 1),
         }
         print(json.dumps(line), flush=True)

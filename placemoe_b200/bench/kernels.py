@@ -113,7 +113,7 @@ def bench_moe(tokens, experts, k, hidden, inter, iters, skew, align=128):
     gu = torch.empty(cap, 2 * inter, device="cuda", dtype=torch.bfloat16)
     f1 = 2.0 * rows * 2 * inter * hidden
     report(f"moe_fc1_swiglu[T{tokens} E{experts} k{k} H{hidden} I{inter} align{align}]",
-           time_fn(lambda: kn.moe_fc1_swiglu(xd, w1, offsets, row_scale, h, gu, align), iters), f1)
+           time_fn(lambda: kn.moe_fc1_swiglu(xd, w1, offsets, row_scale, h, gu, align, None), iters), f1)
     y = torch.empty(cap, hidden, device="cuda", dtype=torch.bfloat16)
     f2 = 2.0 * rows * inter * hidden
     report("moe_fc2", time_fn(lambda: kn.moe_grouped_gemm(h, w2, offsets, y, False, align), iters), f2)
@@ -124,9 +124,15 @@ def bench_moe(tokens, experts, k, hidden, inter, iters, skew, align=128):
     dx = torch.empty_like(xd)
     report("moe_fc1_dgrad", time_fn(lambda: kn.moe_grouped_gemm(dgu, w1, offsets, dx, True, align), iters), f1)
     dw1 = torch.zeros(experts, 2 * inter, hidden, device="cuda")
-    report("moe_fc1_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(dgu, xd, offsets, dw1, True), iters), f1)
+    report("moe_fc1_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(dgu, xd, offsets, dw1, True, None), iters), f1)
     dw2 = torch.zeros(experts, hidden, inter, device="cuda")
-    report("moe_fc2_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(y, h, offsets, dw2, True), iters), f2)
+    report("moe_fc2_wgrad_f32acc", time_fn(lambda: kn.moe_wgrad(y, h, offsets, dw2, True, None), iters), f2)
+    # the same fc1 GEMMs reading token rows through TMA row gathers (no dispatched copy)
+    xt = torch.randn(tokens, hidden, device="cuda", dtype=torch.bfloat16)
+    report("moe_fc1_swiglu_gathered",
+           time_fn(lambda: kn.moe_fc1_swiglu(xt, w1, offsets, row_scale, h, gu, align, row_token), iters), f1)
+    report("moe_fc1_wgrad_f32acc_gathered",
+           time_fn(lambda: kn.moe_wgrad(dgu, xt, offsets, dw1, True, row_token), iters), f1)
 
 
 def bench_attn(batch, seq, heads, kv_heads, dim, iters):

@@ -317,6 +317,24 @@ PM_DEVICE void tma_load_3d_pair(void* smem_dst, const void* tmap, uint32_t bar_c
       : "memory");
 }
 
+// Row gathers: four rows (indices r.x..r.w) of `box_cols` columns starting at
+// column x, written as four consecutive 128-byte rows at smem_dst.  The tensor
+// map's box is one row high.
+PM_DEVICE void tma_gather4(void* smem_dst, const void* tmap, uint64_t* bar, int x, int4 r) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+      : "memory");
+}
+PM_DEVICE void tma_gather4_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int x, int4 r) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(r.x), "r"(r.y), "r"(r.z), "r"(r.w)
+      : "memory");
+}
+
 // Executed by one warp in EACH CTA of the pair: same TMEM columns in both.
 PM_DEVICE void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),

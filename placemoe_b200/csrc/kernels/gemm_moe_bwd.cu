@@ -57,12 +57,21 @@ void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor off
 
 // Expert weight gradient: dw[e] (+)= a[seg_e]^T . b[seg_e]
 //   a: [rows, M] (e.g. dY), b: [rows, N] (e.g. h); dw: [E, M, N] fp32.
-void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate) {
+//   gather_idx (optional, int32 [rows]): row r of b is b[gather_idx[r]] (TMA row gathers).
+void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate,
+               c10::optional<torch::Tensor> gather_idx) {
+  const bool gather = gather_idx.has_value();
+  if (gather) {
+    TORCH_CHECK(gather_idx->is_cuda() && gather_idx->scalar_type() == torch::kInt32 && gather_idx->is_contiguous(),
+                "gather_idx must be a contiguous int32 CUDA tensor");
+    TORCH_CHECK(gather_idx->numel() == a.size(0), "gather_idx must have one entry per row of a");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(gather_idx->data_ptr()) & 15) == 0, "gather_idx must be 16-byte aligned");
+  }
   check_bf16_2d(a, "a");
   check_bf16_2d(b, "b");
   TORCH_CHECK(dw.dim() == 3 && dw.is_contiguous() && dw.scalar_type() == torch::kFloat32, "dw must be fp32 [E,M,N]");
   const int64_t E = dw.size(0), M = dw.size(1), N = dw.size(2);
-  TORCH_CHECK(a.size(1) == M && b.size(1) == N && a.size(0) == b.size(0), "shape mismatch");
+  TORCH_CHECK(a.size(1) == M && b.size(1) == N && (gather || a.size(0) == b.size(0)), "shape mismatch");
   TORCH_CHECK(M % 128 == 0 && N % 8 == 0, "M must be a multiple of 128");
   TORCH_CHECK(E <= kMaxGroups && offsets.numel() == E + 1 && offsets.scalar_type() == torch::kInt32, "offsets");
   PM_CHECK_CUDA(dw); PM_CHECK_CUDA(offsets);
@@ -72,16 +81,19 @@ void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::T
   args.group_offsets = offsets.data_ptr<int>();
   args.D = dw.data_ptr(); args.ldd = N; args.d_group_stride = M * N;
   args.beta = accumulate ? 1.f : 0.f;
+  if (gather) args.gather_idx = gather_idx->data_ptr<int>();
   CUtensorMap ta = make_tmap_2d_bf16(a.data_ptr(), a.size(0), M, a.stride(0), 64, 64);
-  CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), b.size(0), N, b.stride(0), 64, 64);
+  CUtensorMap tb = make_tmap_2d_bf16(b.data_ptr(), b.size(0), N, b.stride(0), 64, gather ? 1 : 64);
   CUtensorMap td = make_tmap_f32_out(dw.data_ptr(), E, M, N, N, M * N, true);
   if (M % 256 == 0) {  // CTA pairs over 256 output rows
     const int tiles = (int)(E * (M / 256) * ((N + 255) / 256));
-    launch<256, true, true, kGroupK, kAccumF32, false, true>(ta, tb, args, std::min(tiles, num_pairs()), &td);
+    if (gather) launch<256, true, true, kGroupK, kAccumF32, false, true, true>(ta, tb, args, std::min(tiles, num_pairs()), &td);
+    else launch<256, true, true, kGroupK, kAccumF32, false, true>(ta, tb, args, std::min(tiles, num_pairs()), &td);
     return;
   }
   const int tiles = (int)(E * (M / BM) * ((N + 255) / 256));
-  launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()), &td);
+  if (gather) launch<256, true, true, kGroupK, kAccumF32, false, false, true>(ta, tb, args, std::min(tiles, num_sms()), &td);
+  else launch<256, true, true, kGroupK, kAccumF32, false>(ta, tb, args, std::min(tiles, num_sms()), &td);
 }
 
 }  // namespace pm

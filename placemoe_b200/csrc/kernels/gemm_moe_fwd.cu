@@ -8,9 +8,18 @@ namespace pm {
 // x: [rows, H] dispatched tokens, expert segments at group_offsets (multiples of 128).
 // w1: [E, 2I, H] (gate rows first, then up rows).  gu_out (optional): [rows, 2I].
 // align: the segment alignment of `offsets` (128, or 256 to run on CTA pairs).
+// gather_idx (optional, int32 [rows]): A row r is x[gather_idx[r]] (fetched by TMA row
+// gathers; < 0 marks padding) instead of x[r].
 void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
-                    c10::optional<torch::Tensor> gu_out, int64_t align) {
+                    c10::optional<torch::Tensor> gu_out, int64_t align, c10::optional<torch::Tensor> gather_idx) {
   TORCH_CHECK(align == 128 || align == 256, "segment alignment must be 128 or 256");
+  const bool gather = gather_idx.has_value();
+  if (gather) {
+    TORCH_CHECK(gather_idx->is_cuda() && gather_idx->scalar_type() == torch::kInt32 && gather_idx->is_contiguous(),
+                "gather_idx must be a contiguous int32 CUDA tensor");
+    TORCH_CHECK((reinterpret_cast<uintptr_t>(gather_idx->data_ptr()) & 15) == 0, "gather_idx must be 16-byte aligned");
+  }
+  const int64_t rows = gather ? gather_idx->numel() : x.size(0);
   check_bf16_2d(x, "x");
   TORCH_CHECK(w1.dim() == 3 && w1.is_contiguous() && w1.scalar_type() == torch::kBFloat16, "w1 must be [E,2I,H] bf16");
   const int64_t E = w1.size(0), I2 = w1.size(1), H = w1.size(2);
@@ -19,12 +28,13 @@ void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, to
   TORCH_CHECK(I % 128 == 0, "moe intermediate size must be a multiple of 128");
   TORCH_CHECK(E <= kMaxGroups, "too many experts");
   TORCH_CHECK(offsets.scalar_type() == torch::kInt32 && offsets.numel() == E + 1, "offsets must be int32 [E+1]");
-  TORCH_CHECK(h.size(0) == x.size(0) && h.size(1) == I && h.stride(1) == 1, "h shape");
+  TORCH_CHECK(h.size(0) == rows && h.size(1) == I && h.stride(1) == 1, "h shape");
   PM_CHECK_CUDA(w1); PM_CHECK_CUDA(offsets); PM_CHECK_CUDA(scale); PM_CHECK_CUDA(h); PM_CHECK_CUDA_OPT(gu_out);
-  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && scale.numel() >= x.size(0), "scale must be fp32 [rows]");
+  TORCH_CHECK(scale.scalar_type() == torch::kFloat32 && scale.numel() >= rows, "scale must be fp32 [rows]");
   c10::cuda::CUDAGuard guard(x.device());
   GemmArgs args = blank_args();
-  args.M = (int)x.size(0); args.N = (int)I2; args.K = (int)H; args.num_groups = (int)E;
+  args.M = (int)rows; args.N = (int)I2; args.K = (int)H; args.num_groups = (int)E;
+  if (gather) args.gather_idx = gather_idx->data_ptr<int>();
   args.group_offsets = offsets.data_ptr<int>();
   args.raster = 1;  // an expert's weights (<= tens of MB) stay in L2 while its rows stream once
   args.D = h.data_ptr(); args.ldd = h.stride(0);
@@ -35,7 +45,7 @@ void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, to
     args.aux_out = reinterpret_cast<__nv_bfloat16*>(gu_out->data_ptr());
     args.ld_aux_out = gu_out->stride(0);
   }
-  CUtensorMap ta = make_tmap_2d_bf16(x.data_ptr(), x.size(0), H, x.stride(0), 64, 128);
+  CUtensorMap ta = make_tmap_2d_bf16(x.data_ptr(), x.size(0), H, x.stride(0), 64, gather ? 1 : 128);
   CUtensorMap tb = make_tmap_3d_bf16(w1.data_ptr(), E, I2, H, H, I2 * H, 64, 128);
   check_bf16_2d(h, "h");
   CUtensorMap th = make_tmap_bf16_epi(h.data_ptr(), h.size(0), I, h.stride(0));
@@ -43,14 +53,14 @@ void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, to
   if (gu_out.has_value()) tg = make_tmap_bf16_epi(gu_out->data_ptr(), gu_out->size(0), I2, gu_out->stride(0));
   const CUtensorMap* tgp = gu_out.has_value() ? &tg : nullptr;
   if (align == 256) {
-    const int ub = (int)((x.size(0) / 256) * (I / 128));
-    launch<256, false, false, kGroupM, kSwiGLU, true, true>(ta, tb, args, std::max(1, std::min(ub, num_pairs())), &th,
-                                                            tgp);
+    const int grid = std::max(1, std::min((int)((rows / 256) * (I / 128)), num_pairs()));
+    if (gather) launch<256, false, false, kGroupM, kSwiGLU, true, true, true>(ta, tb, args, grid, &th, tgp);
+    else launch<256, false, false, kGroupM, kSwiGLU, true, true>(ta, tb, args, grid, &th, tgp);
     return;
   }
-  const int ub = (int)((x.size(0) / BM) * (I / 128));
-  const int grid = std::max(1, std::min(ub, num_sms()));
-  launch<256, false, false, kGroupM, kSwiGLU, true>(ta, tb, args, grid, &th, tgp);
+  const int grid = std::max(1, std::min((int)((rows / BM) * (I / 128)), num_sms()));
+  if (gather) launch<256, false, false, kGroupM, kSwiGLU, true, false, true>(ta, tb, args, grid, &th, tgp);
+  else launch<256, false, false, kGroupM, kSwiGLU, true>(ta, tb, args, grid, &th, tgp);
 }
 
 // Expert GEMM with per-expert B, grouped over rows of A.

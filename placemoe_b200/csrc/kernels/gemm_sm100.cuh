@@ -70,6 +70,7 @@ struct GemmArgs {
   float* row_grad;  // dSwiGLU: d(routing weight), atomically accumulated
   int inter;        // I: column offset of the "up" half
   float beta;       // kAccumF32: D = acc + beta * D
+  const int* gather_idx;  // GATHER: source row of every A row (kGroupM) / B row (kGroupK); < 0 = padding
   int raster;       // 0: consecutive tiles walk M (B reused from L2); 1: walk N (A reused from L2)
 };
 
@@ -158,6 +159,14 @@ __device__ __forceinline__ int total_tiles(const GemmArgs& a, const int* s_off) 
   return ((a.M + TM - 1) / TM) * n_tiles;
 }
 
+// Four gather indices (16-byte aligned); padding rows (< 0) read row 0, whose
+// values are multiplied by zero routing weights / zero gradients downstream.
+__device__ __forceinline__ int4 load_rows4(const int* p) {
+  int4 r = *reinterpret_cast<const int4*>(p);
+  r.x = max(r.x, 0); r.y = max(r.y, 0); r.z = max(r.z, 0); r.w = max(r.w, 0);
+  return r;
+}
+
 // Store 32 fp32 values as bf16 at dst (16-byte aligned), masking columns >= limit.
 __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, const float* v, int valid) {
   uint32_t p[16];
@@ -186,7 +195,7 @@ __device__ __forceinline__ void load_row32_bf16(const __nv_bfloat16* src, float*
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT, bool PAIR = false>
+template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT, bool PAIR = false, bool GATHER = false>
 __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmD, const __grid_constant__ CUtensorMap tmE,
@@ -261,25 +270,58 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
+    // Lane 0 waits for free stages and issues the tiled loads.  With GATHER the
+    // whole warp also issues row gathers: expert rows of A (kGroupM, lane l
+    // fetches rows 4l..4l+3 of the CTA's 128) or token rows of B (kGroupK, lane
+    // l fetches rows 4 (l % 16).. of the k-block into 64-column atom l / 16).
+    static_assert(!GATHER || (GROUP == kGroupM && !A_MN) || (GROUP == kGroupK && B_MN && BNc % 128 == 0),
+                  "gathered operand layout");
+    if (lane == 0 || GATHER) {
       int s = 0; uint32_t ph = 0;
       int issued_mask = 0; uint32_t issued_par = 0;
       // paired: every copy completes on the leader's full barrier
       const uint32_t full0 = PAIR ? mapa_shared(smem_u32(&full[0]), 0) : 0u;
       TileInfo ti;
       for (int t = first_tile; decode_tile<BN, GROUP, SPLIT, TM>(t, args, s_off, total, ti, crank); t += tile_step) {
-        if (*s_abort) break;
+        int stop = *s_abort;
+        if (GATHER) stop = __shfl_sync(0xffffffffu, stop, 0);  // the warp leaves together
+        if (stop) break;
         // this CTA's B columns: the gate or up half (SPLIT), else its half of the tile
         const int nb = SPLIT ? (PAIR ? (crank ? args.inter + ti.n0 : ti.n0) : ti.n0) : ti.n0 + crank * BNc;
+        int4 arow = make_int4(0, 0, 0, 0);
+        if (GATHER && GROUP == kGroupM) arow = load_rows4(args.gather_idx + ti.m0 + 4 * lane);
         for (int kb = 0; kb < ti.nkb; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1)) { *s_abort = 1; break; }
-          if (!PAIR || crank == 0) mbar_arrive_expect_tx(&full[s], (PAIR ? 2 : 1) * C::kStageBytes);
+          bool free_ok = lane == 0 ? mbar_wait(&empty[s], ph ^ 1) : true;
+          if (GATHER) free_ok = __shfl_sync(0xffffffffu, free_ok, 0);
+          if (!free_ok) { if (lane == 0) *s_abort = 1; break; }
           const int k0 = ti.kbeg + kb * BK;
           uint8_t* a_dst = smA + s * C::kABytes;
           uint8_t* b_dst = smB + s * C::kBBytes;
+          if (GATHER) {
+            const uint32_t fb = PAIR ? full0 + (uint32_t)(s * sizeof(uint64_t)) : smem_u32(&full[s]);
+            if (GROUP == kGroupM) {
+              if (PAIR) tma_gather4_pair(a_dst + lane * 512, &tmA, fb, k0, arow);
+              else tma_gather4(a_dst + lane * 512, &tmA, &full[s], k0, arow);
+            } else {
+              const int4 brow = load_rows4(args.gather_idx + k0 + 4 * (lane & 15));
+#pragma unroll
+              for (int at = lane >> 4; at < BNc / 64; at += 2) {
+                uint8_t* dst = b_dst + at * 8192 + (lane & 15) * 512;
+                if (PAIR) tma_gather4_pair(dst, &tmB, fb, nb + 64 * at, brow);
+                else tma_gather4(dst, &tmB, &full[s], nb + 64 * at, brow);
+              }
+            }
+          }
+          if (lane != 0) {
+            if (++s == S) { s = 0; ph ^= 1; }
+            continue;
+          }
+          if (!PAIR || crank == 0) mbar_arrive_expect_tx(&full[s], (PAIR ? 2 : 1) * C::kStageBytes);
           if (PAIR) {
             const uint32_t fb = full0 + (uint32_t)(s * sizeof(uint64_t));
-            if (!A_MN) {
+            if (GATHER && GROUP == kGroupM) {
+              // A rows were gathered above
+            } else if (!A_MN) {
               tma_load_2d_pair(a_dst, &tmA, fb, k0, ti.m0);
             } else {
               tma_load_2d_pair(a_dst, &tmA, fb, ti.m0, k0);
@@ -292,7 +334,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < BNc / 64; ++j) tma_load_3d_pair(b_dst + j * 8192, &tmB, fb, nb + 64 * j, k0, ti.g);
               }
-            } else {
+            } else if (!(GATHER && GROUP == kGroupK)) {
               if (!B_MN) {
                 tma_load_2d_pair(b_dst, &tmB, fb, k0, nb);
               } else {
@@ -301,7 +343,9 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
               }
             }
           } else {
-            if (!A_MN) {
+            if (GATHER && GROUP == kGroupM) {
+              // A rows were gathered above
+            } else if (!A_MN) {
               tma_load_2d(a_dst, &tmA, &full[s], k0, ti.m0);
             } else {
               tma_load_2d(a_dst, &tmA, &full[s], ti.m0, k0);
@@ -319,7 +363,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < BN / 64; ++j) tma_load_3d(b_dst + j * 8192, &tmB, &full[s], ti.n0 + 64 * j, k0, ti.g);
               }
-            } else {
+            } else if (!(GATHER && GROUP == kGroupK)) {
               if (!B_MN) {
                 tma_load_2d(b_dst, &tmB, &full[s], k0, ti.n0);
               } else {
@@ -333,7 +377,7 @@ __global__ void __launch_bounds__(Cfg<BN, EPI, PAIR>::kThreads, 1)
           if (++s == S) { s = 0; ph ^= 1; }
         }
       }
-      if (*s_abort && (!PAIR || crank == 0)) {
+      if (lane == 0 && *s_abort && (!PAIR || crank == 0)) {
         // Let copies already in flight land before the CTA exits (paired: the leader's
         // barriers count both CTAs' copies; the closing cluster barrier holds the peer).
         for (int i = 0; i < S; ++i)
@@ -695,11 +739,11 @@ static inline int num_sms() {
 }
 
 // grid: CTAs for the single-CTA kernel; for PAIR, the number of CTA pairs (launched as 2-CTA clusters).
-template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT, bool PAIR = false>
+template <int BN, bool A_MN, bool B_MN, int GROUP, int EPI, bool SPLIT, bool PAIR = false, bool GATHER = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args, int grid,
                    const CUtensorMap* td = nullptr, const CUtensorMap* te = nullptr) {
   using C = Cfg<BN, EPI, PAIR>;
-  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, GROUP, EPI, SPLIT, PAIR>;
+  auto kern = gemm_sm100_kernel<BN, A_MN, B_MN, GROUP, EPI, SPLIT, PAIR, GATHER>;
   static bool configured = false;
   if (!configured) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes));

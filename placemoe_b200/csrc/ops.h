@@ -8,12 +8,13 @@ namespace pm {
 // gemm_dense.cu, gemm_moe_fwd.cu, gemm_moe_bwd.cu (kernel template in gemm_sm100.cuh)
 void dense_gemm(torch::Tensor a, torch::Tensor b, torch::Tensor out, bool a_mn, bool b_mn, bool accumulate);
 void moe_fc1_swiglu(torch::Tensor x, torch::Tensor w1, torch::Tensor offsets, torch::Tensor scale, torch::Tensor h,
-                    c10::optional<torch::Tensor> gu_out, int64_t align);
+                    c10::optional<torch::Tensor> gu_out, int64_t align, c10::optional<torch::Tensor> gather_idx);
 void moe_grouped_gemm(torch::Tensor a, torch::Tensor w, torch::Tensor offsets, torch::Tensor out, bool b_mn,
                       int64_t align);
 void moe_fc2_dgrad_dswiglu(torch::Tensor dy, torch::Tensor w2, torch::Tensor offsets, torch::Tensor gu,
                            torch::Tensor scale, torch::Tensor dgu, torch::Tensor dscale, int64_t align);
-void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate);
+void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::Tensor dw, bool accumulate,
+               c10::optional<torch::Tensor> gather_idx);
 
 // norm_rope.cu
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);

@@ -157,7 +157,7 @@ class ExpertFFN(torch.autograd.Function):
         inter = w1.shape[1] // 2
         h = torch.empty(rows, inter, device=xd.device, dtype=torch.bfloat16)
         gu = torch.empty(rows, 2 * inter, device=xd.device, dtype=torch.bfloat16)
-        kn.moe_fc1_swiglu(xd, w1, offsets, scale, h, gu, align)
+        kn.moe_fc1_swiglu(xd, w1, offsets, scale, h, gu, align, None)
         y = torch.empty(rows, w2.shape[1], device=xd.device, dtype=torch.bfloat16)
         kn.moe_grouped_gemm(h, w2, offsets, y, False, align)
         ctx.save_for_backward(xd, scale, w1, w2, offsets, h, gu)
@@ -178,10 +178,66 @@ class ExpertFFN(torch.autograd.Function):
         dx = torch.empty_like(xd)
         kn.moe_grouped_gemm(dgu, w1, offsets, dx, True, ctx.align)
         if p2 is not None and p2.requires_grad:
-            kn.moe_wgrad(dy, h, offsets, *wgrad_target(p2))
+            kn.moe_wgrad(dy, h, offsets, *wgrad_target(p2), None)
         if p1 is not None and p1.requires_grad:
-            kn.moe_wgrad(dgu, xd, offsets, *wgrad_target(p1))
+            kn.moe_wgrad(dgu, xd, offsets, *wgrad_target(p1), None)
         return dx, dscale, None, None, None, None, None, None
+
+
+class GatheredExpertFFN(torch.autograd.Function):
+    """Expert FFN over dispatched rows of the token matrix, with optional recomputation.
+
+    x [T, H] bf16 tokens; row_token [rows] int32 is the token of every
+    dispatched row (-1 on padding), row_of the dispatched rows of every token,
+    k per token (for the backward sum).  The dispatched copy xd = x[row_token]
+    feeds the grouped GEMMs; with ``keep_rows=False`` it is dropped after the
+    forward and gathered again in the backward, which trades one gather for
+    ``rows x H`` bf16 of activation memory per layer.  (The GEMM kernels can
+    also read the rows straight from x with TMA row gathers -- ``gather_idx``
+    -- but four-row gathers issue too slowly to feed the tensor cores.)
+    Returns the expert outputs [rows, H]; the input gradient is returned per
+    token (summed over its dispatched rows).
+    """
+
+    @staticmethod
+    def forward(ctx, x, scale, w1, w2, offsets, row_token, end, row_of, p1, p2, align=ALIGN, keep_rows=True):
+        kn = kernels()
+        rows = row_token.numel()
+        inter = w1.shape[1] // 2
+        xd = torch.empty(rows, x.shape[1], device=x.device, dtype=torch.bfloat16)
+        kn.gather_rows(x, row_token, end, xd)
+        h = torch.empty(rows, inter, device=x.device, dtype=torch.bfloat16)
+        gu = torch.empty(rows, 2 * inter, device=x.device, dtype=torch.bfloat16)
+        kn.moe_fc1_swiglu(xd, w1, offsets, scale, h, gu, align, None)
+        y = torch.empty(rows, w2.shape[1], device=x.device, dtype=torch.bfloat16)
+        kn.moe_grouped_gemm(h, w2, offsets, y, False, align)
+        ctx.save_for_backward(x, xd if keep_rows else None, scale, w1, w2, offsets, row_token, end, row_of, h, gu)
+        ctx.params = (p1, p2)
+        ctx.align = align
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, xd, scale, w1, w2, offsets, row_token, end, row_of, h, gu = ctx.saved_tensors
+        p1, p2 = ctx.params
+        kn = kernels()
+        dy = dy.contiguous()
+        rows = row_token.numel()
+        dgu = torch.empty_like(gu)
+        dscale = torch.zeros(rows, device=x.device, dtype=torch.float32)
+        kn.moe_fc2_dgrad_dswiglu(dy, w2, offsets, gu, scale, dgu, dscale, ctx.align)
+        dxd = torch.empty(rows, x.shape[1], device=x.device, dtype=torch.bfloat16)
+        kn.moe_grouped_gemm(dgu, w1, offsets, dxd, True, ctx.align)
+        if p2 is not None and p2.requires_grad:
+            kn.moe_wgrad(dy, h, offsets, *wgrad_target(p2), None)
+        if p1 is not None and p1.requires_grad:
+            if xd is None:
+                xd = torch.empty(rows, x.shape[1], device=x.device, dtype=torch.bfloat16)
+                kn.gather_rows(x, row_token, end, xd)
+            kn.moe_wgrad(dgu, xd, offsets, *wgrad_target(p1), None)
+        dx = torch.empty_like(x)
+        kn.sum_rows(dxd, row_of, dx)
+        return dx, dscale, None, None, None, None, None, None, None, None, None, None
 
 
 class _GatherRows(torch.autograd.Function):
@@ -277,8 +333,12 @@ class _AuxLoss(torch.autograd.Function):
         return None, None, None, None, None, None, None
 
 
-def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=None, aux_coef=0.0):
-    """Single-device MoE layer. Returns (y [T, H] bf16, aux_loss or None, router stats)."""
+def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=None, aux_coef=0.0, keep_rows=True):
+    """Single-device MoE layer. Returns (y [T, H] bf16, aux_loss or None, router stats).
+
+    ``keep_rows=False`` recomputes the dispatched input rows in the backward
+    instead of keeping them (see :class:`GatheredExpertFFN`).
+    """
     t, hdim = x.shape
     kn = kernels()
     logits = linear_fp32(x, wg)
@@ -292,8 +352,8 @@ def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=N
     offsets, counts, row_of, row_token, row_scale = kn.moe_plan(idx, lut, w.detach(), num_slots, cap, align)
     end = offsets[num_slots:]
     scale = _ScaleGather.apply(w, row_scale, row_of)
-    xd = _GatherRows.apply(x, row_token, end, row_of, cap)
-    yd = ExpertFFN.apply(xd, scale, w1_bf16, w2_bf16, offsets, p1, p2, align)
+    yd = GatheredExpertFFN.apply(x.contiguous(), scale, w1_bf16, w2_bf16, offsets, row_token, end, row_of, p1, p2,
+                                 align, keep_rows)
     y = _SumRows.apply(yd, row_of, row_token, end, t)
     return y, aux, idx
 

@@ -203,6 +203,7 @@ def _cuda_local_experts(blk, recv_x, recv_row, recv_slot, recv_w, nrows):
     table[recv_row, pos] = row_of.view(-1)
     scale = moe_ops._ScaleGather.apply(recv_w, row_scale, row_of)
     w1, w2 = blk.compute_weights()
-    xd = moe_ops._GatherRows.apply(recv_x.contiguous(), row_src.contiguous(), end, table, cap)
-    yd = moe_ops.ExpertFFN.apply(xd, scale, w1, w2, offsets, blk.gate_up_proj, blk.down_proj, align)
-    return moe_ops._SumRows.apply(yd, table, row_src.contiguous(), end, nrows)
+    row_src = row_src.to(torch.int32).contiguous()
+    yd = moe_ops.GatheredExpertFFN.apply(recv_x.contiguous(), scale, w1, w2, offsets, row_src, end, table,
+                                         blk.gate_up_proj, blk.down_proj, align, blk.keep_expert_rows)
+    return moe_ops._SumRows.apply(yd, table, row_src, end, nrows)

@@ -191,7 +191,7 @@ class _P2PMoE(torch.autograd.Function):
         inter = w1.shape[1] // 2
         hbuf = torch.empty(loc["cap"], inter, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(loc["cap"], 2 * inter, device=dev, dtype=torch.bfloat16)
-        kn.moe_fc1_swiglu(xd, w1, loc["offsets"], loc["row_scale"], hbuf, gu, loc["align"])
+        kn.moe_fc1_swiglu(xd, w1, loc["offsets"], loc["row_scale"], hbuf, gu, loc["align"], None)
         yd = torch.empty(loc["cap"], h, device=dev, dtype=torch.bfloat16)
         kn.moe_grouped_gemm(hbuf, w2, loc["offsets"], yd, False, loc["align"])
         _mark("fwd.expert_gemms")
@@ -245,9 +245,9 @@ class _P2PMoE(torch.autograd.Function):
         dxd = torch.empty_like(xd)
         kn.moe_grouped_gemm(dgu, w1, loc["offsets"], dxd, True, loc["align"])
         if blk.down_proj.requires_grad:
-            kn.moe_wgrad(dyd, hbuf, loc["offsets"], *moe_ops.wgrad_target(blk.down_proj))
+            kn.moe_wgrad(dyd, hbuf, loc["offsets"], *moe_ops.wgrad_target(blk.down_proj), None)
         if blk.gate_up_proj.requires_grad:
-            kn.moe_wgrad(dgu, xd, loc["offsets"], *moe_ops.wgrad_target(blk.gate_up_proj))
+            kn.moe_wgrad(dgu, xd, loc["offsets"], *moe_ops.wgrad_target(blk.gate_up_proj), None)
         _mark("bwd.expert_gemms")
         # dispatch backward: per received row, sum over its assignments -> back to the source
         dpart = torch.empty(R_cap, h, device=dev, dtype=torch.bfloat16)

@@ -56,7 +56,8 @@ class TrainConfig:
     redundant_slots_per_rank: int = 0
     placemoe_artifact: str = ""  # schema-v2 artifact loaded at startup
     capture_routes: bool = False
-    ep_transport: str = "auto"  # "auto" | "p2p" | "nccl"
+    ep_transport: str = "auto"
+    recompute_expert_rows: bool = False  # drop dispatched expert inputs after forward, re-gather in backward  # "auto" | "p2p" | "nccl"
     gradient_checkpointing: bool = False
     device: str = "cuda"
     log_interval: int = 10
@@ -100,6 +101,8 @@ class Trainer:
         init = expert_init_from_full(self.model_cfg, topology, plans, self.rank, cfg.seed)
         self.model = build_model(self.model_cfg, topology.slots_per_rank, self.device, cfg.seed, init)
         self.model.gradient_checkpointing = cfg.gradient_checkpointing
+        for blk in self.model.moe_blocks():
+            blk.keep_expert_rows = not cfg.recompute_expert_rows
         self.model.train()
         self.pstate = parallelize_model(self.model, plans=plans, topology=topology, device=self.device,
                                         capture_routes=cfg.capture_routes, transport=cfg.ep_transport)

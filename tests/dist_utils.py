@@ -18,6 +18,10 @@ def _entry(rank, world, port, fn, args, errq):
 
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
                        "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank)})
+    import torch
+
+    # ranks share the machine's cores: no oversubscription
+    torch.set_num_threads(max(1, (os.cpu_count() or 2) // world))
     try:
         from datetime import timedelta
 
@@ -37,8 +41,11 @@ def run_distributed(fn, world: int, *args):
     procs = [ctx.Process(target=_entry, args=(r, world, port, fn, args, errq)) for r in range(world)]
     for p in procs:
         p.start()
+    import time
+
+    deadline = time.monotonic() + 900
     for p in procs:
-        p.join(300)
+        p.join(max(1.0, deadline - time.monotonic()))
     errors = []
     while not errq.empty():
         errors.append(errq.get())

@@ -98,7 +98,7 @@ def test_grouped_fc1_fc2_and_backward(E, H, I, align):
     k = kernels()
     h = torch.zeros(rows, I, device="cuda", dtype=torch.bfloat16)
     gu = torch.zeros(rows, 2 * I, device="cuda", dtype=torch.bfloat16)
-    k.moe_fc1_swiglu(x, w1, off_t, scale, h, gu, align)
+    k.moe_fc1_swiglu(x, w1, off_t, scale, h, gu, align, None)
     y = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
     k.moe_grouped_gemm(h, w2, off_t, y, False, align)
     dy = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
@@ -111,8 +111,8 @@ def test_grouped_fc1_fc2_and_backward(E, H, I, align):
     k.moe_grouped_gemm(dgu, w1, off_t, dx, True, align)
     dw1 = torch.zeros(E, 2 * I, H, device="cuda", dtype=torch.float32)
     dw2 = torch.zeros(E, H, I, device="cuda", dtype=torch.float32)
-    k.moe_wgrad(dgu, x, off_t, dw1, False)
-    k.moe_wgrad(dy, h, off_t, dw2, True)
+    k.moe_wgrad(dgu, x, off_t, dw1, False, None)
+    k.moe_wgrad(dy, h, off_t, dw2, True, None)
     torch.cuda.synchronize()
     check_device_error()
     for e in range(E):
@@ -136,3 +136,44 @@ def test_grouped_fc1_fc2_and_backward(E, H, I, align):
         _close(dscale[s: s + c], se.grad, 3e-2)
         _close(dw1[e], w1e.grad, 3e-2)
         _close(dw2[e], w2e.grad, 3e-2)
+
+
+@pytest.mark.parametrize("align", [128, 256])
+def test_gathered_fc1_and_wgrad_match_materialised_rows(align):
+    """TMA row-gather operands give the same results as an explicit gather of the rows."""
+    from placemoe_b200.ops import kernels, check_device_error
+
+    torch.manual_seed(4)
+    E, H, I, T = 8, 512, 256, 700
+    counts = [int(c) for c in torch.randint(0, 400, (E,))]
+    offs = _segments(counts, align)
+    rows = offs[-1] + align
+    tok = torch.full((rows,), -1, dtype=torch.int32)
+    for e in range(E):
+        tok[offs[e]: offs[e] + counts[e]] = torch.randint(0, T, (counts[e],), dtype=torch.int32)
+    tok = tok.cuda()
+    xt = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    xd = torch.zeros(rows, H, device="cuda", dtype=torch.bfloat16)
+    valid = tok >= 0
+    xd[valid] = xt[tok[valid].long()]
+    scale = torch.rand(rows, device="cuda") * valid.float()
+    w1 = (torch.randn(E, 2 * I, H, device="cuda") * 0.05).to(torch.bfloat16)
+    off_t = torch.tensor(offs, device="cuda", dtype=torch.int32)
+    k = kernels()
+    h0 = torch.zeros(rows, I, device="cuda", dtype=torch.bfloat16)
+    g0 = torch.zeros(rows, 2 * I, device="cuda", dtype=torch.bfloat16)
+    k.moe_fc1_swiglu(xd, w1, off_t, scale, h0, g0, align, None)
+    h1 = torch.zeros_like(h0)
+    g1 = torch.zeros_like(g0)
+    k.moe_fc1_swiglu(xt, w1, off_t, scale, h1, g1, align, tok)
+    dgu = torch.randn(rows, 2 * I, device="cuda", dtype=torch.bfloat16) * valid[:, None].to(torch.bfloat16)
+    dw0 = torch.zeros(E, 2 * I, H, device="cuda")
+    dw1 = torch.zeros(E, 2 * I, H, device="cuda")
+    k.moe_wgrad(dgu, xd, off_t, dw0, False, None)
+    k.moe_wgrad(dgu, xt, off_t, dw1, False, tok)
+    torch.cuda.synchronize()
+    check_device_error()
+    v = valid.cpu()
+    assert torch.equal(h0.cpu()[v], h1.cpu()[v])
+    assert torch.equal(g0.cpu()[v], g1.cpu()[v])
+    _close(dw1, dw0, 1e-5)
