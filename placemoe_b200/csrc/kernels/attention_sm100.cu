@@ -267,6 +267,309 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+// 2^x for x <= 0 on the FMA/ALU pipes (offloads the SFU): x = n + f with
+// n = round(x) (magic-number rounding) and f in [-1/2, 1/2]; 2^f by a cubic
+// fitted to 2^f on [-1/2, 1/2] with p(0) = 1 (iteratively reweighted least
+// squares on the relative error; max relative error 1.0e-4); 2^n is added to
+// the exponent field.  Inputs below -126 (masked scores) give ~2^-126.
+PM_DEVICE float exp2_poly(float x) {
+  x = fmaxf(x, -126.0f);
+  const float t = x + 12582912.0f;  // 1.5 * 2^23: round(x) in the low mantissa bits
+  const float f = x - (t - 12582912.0f);
+  const float p = fmaf(fmaf(fmaf(0.05500864f, f, 0.2422105f), f, 0.69328291f), f, 1.0f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// Forward with two query tiles per CTA: tile 0 = queries [q0, q0+128), tile 1 =
+// [q0+128, q0+256) of one (batch, head).  320 threads:
+//   warp 0      TMA: Q0, Q1 once; K_j / V_j through a 3-slot ring
+//   warp 1      MMA, one lane: S0_0, S1_0, then per key tile j:
+//               O0 += P0_j V_j, S0_{j+1}, O1 += P1_j V_j, S1_{j+1}
+//               so each softmax group works while the other tile's MMAs run
+//   warps 2-5   softmax of tile 0, warps 6-9 softmax of tile 1 (one row per
+//               thread): pass 1 reads the S row from TMEM for the row max, pass
+//               2 reads it again and writes P (bf16, swizzled smem).  The
+//               exponent base moves only when the row max grows by more than 8
+//               (log2 units), so O is rarely rescaled; about a quarter of the
+//               exponentials run as a polynomial on the FMA pipe.
+//   TMEM: S0 | S1 | O0 | O1 (512 columns).
+constexpr int kFwd2Threads = 320;
+constexpr int kPolyPer32 = 8;  // exponentials per 32 evaluated by exp2_poly
+
+// Row max of the raw scores of one 128-key S row in TMEM (keys > r masked when MASK).
+template <bool MASK>
+PM_DEVICE float srow_max(uint32_t t_s, int r) {
+  float mraw = -INFINITY;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    uint32_t v0[32], v1[32];
+    tmem_ld32(t_s + half * 64, v0);
+    tmem_ld32(t_s + half * 64 + 32, v1);
+    tmem_ld_wait();
+    if (MASK) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (half * 64 + i > r) v0[i] = __float_as_uint(-INFINITY);
+        if (half * 64 + 32 + i > r) v1[i] = __float_as_uint(-INFINITY);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; i += 2)
+      mraw = max3f(mraw, max3f(__uint_as_float(v0[i]), __uint_as_float(v0[i + 1]), __uint_as_float(v1[i])),
+                   __uint_as_float(v1[i + 1]));
+  }
+  return mraw;
+}
+
+// P = 2^(s c - m) of one S row -> bf16 into the swizzled P buffer; returns the row sum.
+template <bool MASK>
+PM_DEVICE float srow_exp_store(uint32_t t_s, int r, float c, float m, uint8_t* myP) {
+  const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-m, -m);
+  uint64_t sum2 = f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int cc = 0; cc < 4; ++cc) {
+    uint32_t v[32];
+    tmem_ld32(t_s + cc * 32, v);
+    tmem_ld_wait();
+    uint32_t pk[16];
+#pragma unroll
+    for (int i = 0; i < 32; i += 2) {
+      float x0, x1;
+      f2_unpack(fma_f2(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2), x0, x1);
+      if (MASK) {
+        if (cc * 32 + i > r) x0 = -INFINITY;
+        if (cc * 32 + i + 1 > r) x1 = -INFINITY;
+      }
+      const float p0 = ((i >> 1) % (16 / kPolyPer32) == 0) ? exp2_poly(x0) : fast_exp2(x0);
+      const float p1 = fast_exp2(x1);
+      sum2 = add_f2(sum2, f2_pack(p0, p1));
+      pk[i >> 1] = pack_bf16(p0, p1);
+    }
+#pragma unroll
+    for (int q8 = 0; q8 < 4; ++q8) {
+      const int chunk = cc * 4 + q8;  // 16-byte chunk of the 128-key row
+      st_swz(myP + (chunk >> 3) * 16384, r, chunk & 7,
+             make_uint4(pk[4 * q8], pk[4 * q8 + 1], pk[4 * q8 + 2], pk[4 * q8 + 3]));
+    }
+  }
+  float s0, s1;
+  f2_unpack(sum2, s0, s1);
+  return s0 + s1;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kFwd2Threads, 1)
+    attn_fwd2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  constexpr int ND = D / 64;
+  constexpr int kTB = ND * 16384;  // one [128 x D] bf16 tile
+  constexpr int kSlots = 3;
+  constexpr uint32_t kIdescS = make_idesc_bf16(128, 128, false, false);
+  constexpr uint32_t kIdescO = make_idesc_bf16(128, D, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
+  uint8_t* sQ = sm;                     // 2 tiles
+  uint8_t* sKV = sQ + 2 * kTB;          // kSlots tiles
+  uint8_t* sP = sKV + kSlots * kTB;     // 2 x 32 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * 32768);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;              // [kSlots]
+  uint64_t* kv_empty = bars + 1 + kSlots;    // [kSlots]
+  uint64_t* s_full = bars + 1 + 2 * kSlots;  // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* pv_done = p_full + 2;            // [2]
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(pv_done + 2);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int npairs = a.S / 256;
+  const int L = blockIdx.x;
+  const int pt = npairs - 1 - L / (a.B * a.Hq);  // heaviest tiles first
+  const int rem = L % (a.B * a.Hq);
+  const int b = rem / a.Hq, h = rem % a.Hq;
+  const int hk = h / (a.Hq / a.Hkv);
+  const int qa = 2 * pt;  // key-tile index of tile 0's diagonal
+  const int tq0 = b * a.S + qa * kTile;
+  const int n0 = qa + 1, n1 = qa + 2;  // key tiles seen by tile 0 / tile 1
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kSlots; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int g = 0; g < 2; ++g) { mbar_init(&s_full[g], 1); mbar_init(&p_full[g], 128); mbar_init(&pv_done[g], 1); }
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) { tmem_alloc(s_tmem, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTB);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+#pragma unroll
+        for (int d = 0; d < ND; ++d) tma_load_3d(sQ + g * kTB + d * 16384, &tmQ, q_full, d * 64, h, tq0 + g * kTile);
+      // ring use u: K_j = 2j, V_j = 2j + 1
+      for (int u = 0; u < 2 * n1; ++u) {
+        const int slot = u % kSlots;
+        if (!mbar_wait_abortable(&kv_empty[slot], ((u / kSlots) & 1) ^ 1, s_abort)) break;
+        const int tk0 = b * a.S + (u >> 1) * kTile;
+        mbar_arrive_expect_tx(&kv_full[slot], kTB);
+        const CUtensorMap* tm = (u & 1) ? &tmV : &tmK;
+#pragma unroll
+        for (int d = 0; d < ND; ++d) tma_load_3d(sKV + slot * kTB + d * 16384, tm, &kv_full[slot], d * 64, hk, tk0);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t aq0 = smem_u32(sQ), aq1 = smem_u32(sQ + kTB);
+      const uint32_t ap0 = smem_u32(sP), ap1 = smem_u32(sP + 32768);
+      auto kv_wait = [&](int u) { return mbar_wait_abortable(&kv_full[u % kSlots], (u / kSlots) & 1, s_abort); };
+      auto s_mma = [&](int g, int u) {
+        const uint32_t ak = smem_u32(sKV + (u % kSlots) * kTB);
+        const uint32_t aq = g ? aq1 : aq0;
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16(tmem + g * 128, kmaj_desc(aq, k), kmaj_desc(ak, k), kIdescS, k > 0);
+        umma_commit(&s_full[g]);
+      };
+      auto pv_mma = [&](int g, int u, bool first) {
+        const uint32_t av = smem_u32(sKV + (u % kSlots) * kTB);
+        const uint32_t ap = g ? ap1 : ap0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          umma_f16(tmem + 256 + g * D, kmaj_desc(ap, k), mnmaj_desc(av, k), kIdescO, (!first || k > 0));
+        umma_commit(&pv_done[g]);
+      };
+      bool ok = mbar_wait_abortable(q_full, 0, s_abort) && kv_wait(0);
+      if (ok) {
+        tc_fence_after();
+        s_mma(0, 0);
+        s_mma(1, 0);
+        umma_commit(&kv_empty[0]);
+      }
+      for (int j = 0; ok && j < n1; ++j) {
+        const int uk = 2 * (j + 1), uv = 2 * j + 1;
+        bool k_ready = false;
+        if (j < n0) {
+          ok = mbar_wait_abortable(&p_full[0], j & 1, s_abort) && kv_wait(uv);
+          if (!ok) break;
+          tc_fence_after();
+          pv_mma(0, uv, j == 0);
+          if (j + 1 < n0) {
+            if (!(ok = kv_wait(uk))) break;
+            k_ready = true;
+            tc_fence_after();
+            s_mma(0, uk);
+          }
+        }
+        ok = mbar_wait_abortable(&p_full[1], j & 1, s_abort) && kv_wait(uv);
+        if (!ok) break;
+        tc_fence_after();
+        pv_mma(1, uv, j == 0);
+        umma_commit(&kv_empty[uv % kSlots]);
+        if (j + 1 < n1) {
+          if (!k_ready && !(ok = kv_wait(uk))) break;
+          tc_fence_after();
+          s_mma(1, uk);
+          umma_commit(&kv_empty[uk % kSlots]);
+        }
+      }
+      if (!ok) *s_abort = 1;
+    }
+  } else {
+    // softmax: tile g, one query row per thread
+    const int g = (warp - 2) >> 2;
+    const int qd = warp & 3;
+    const int r = qd * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(qd * 32) << 16);
+    const uint32_t t_s = trow + g * 128, t_o = trow + 256 + g * D;
+    uint8_t* myP = sP + g * 32768;
+    const int ng = g ? n1 : n0;
+    const int diag = qa + g;
+    const float c = a.scale * kLog2e;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ng; ++j) {
+      if (!mbar_wait_abortable(&s_full[g], j & 1, s_abort)) { ok = false; break; }
+      tc_fence_after();
+      const bool masked = j == diag;
+      // pass 1: row max (raw scores; the scale is positive)
+      const float mraw = masked ? srow_max<true>(t_s, r) : srow_max<false>(t_s, r);
+      const float mx = mraw * c;
+      float alpha = 1.0f;
+      if (mx > m + 8.0f) {  // move the exponent base only when the max grew a lot
+        alpha = fast_exp2(m - mx);  // 0 on the first tile
+        m = mx;
+      }
+      l *= alpha;
+      if (j > 0) {
+        // P buffer free and O complete for key tile j - 1
+        if (!mbar_wait_abortable(&pv_done[g], (j - 1) & 1, s_abort)) { ok = false; break; }
+        tc_fence_after();
+        if (!__all_sync(0xffffffffu, alpha == 1.0f)) {
+          const uint64_t a2 = f2_pack(alpha, alpha);
+#pragma unroll
+          for (int cc = 0; cc < D / 16; ++cc) {
+            uint32_t v[16];
+            tmem_ld16(t_o + cc * 16, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; i += 2) {
+              float x0, x1;
+              f2_unpack(mul_f2(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), a2), x0, x1);
+              v[i] = __float_as_uint(x0);
+              v[i + 1] = __float_as_uint(x1);
+            }
+            tmem_st16(t_o + cc * 16, v);
+          }
+          tmem_st_wait();
+        }
+      }
+      // pass 2: P = 2^(s c - m) -> bf16, swizzled into the A operand buffer
+      l += masked ? srow_exp_store<true>(t_s, r, c, m, myP) : srow_exp_store<false>(t_s, r, c, m, myP);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&p_full[g]);
+    }
+    if (ok && mbar_wait_abortable(&pv_done[g], (ng - 1) & 1, s_abort)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* orow = a.o + ((size_t)(tq0 + g * kTile + r) * a.Hq + h) * D;
+#pragma unroll
+      for (int cc = 0; cc < D / 32; ++cc) {
+        uint32_t v[32];
+        tmem_ld32(t_o + cc * 32, v);
+        tmem_ld_wait();
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_uint4(pack_bf16(__uint_as_float(v[8 * i]) * inv, __uint_as_float(v[8 * i + 1]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 2]) * inv, __uint_as_float(v[8 * i + 3]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 4]) * inv, __uint_as_float(v[8 * i + 5]) * inv),
+                              pack_bf16(__uint_as_float(v[8 * i + 6]) * inv, __uint_as_float(v[8 * i + 7]) * inv));
+      }
+      a.lse[(size_t)h * a.T + tq0 + g * kTile + r] = (m + __log2f(l)) * kLn2;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+constexpr int fwd2_smem() {
+  return (2 + 3) * (D / 64) * 16384 + 2 * 32768 + 1024 + 256;
+}
+
 // delta[h, t] = sum_d dO[t, h, d] * O[t, h, d]
 __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ dout, int T,
                                   int Hq, int D, float* __restrict__ delta) {
@@ -543,8 +846,22 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   a.o = (__nv_bfloat16*)o.data_ptr();
   a.lse = lse.data_ptr<float>();
   CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v);
-  const int grid = a.B * Hq * ((int)S / kTile);
   auto stream = at::cuda::getCurrentCUDAStream();
+  if (S % 256 == 0) {  // two query tiles per CTA
+    const int grid2 = a.B * Hq * ((int)S / 256);
+    if (D == 128) {
+      auto kern = attn_fwd2_kernel<128>;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd2_smem<128>()));
+      kern<<<grid2, kFwd2Threads, fwd2_smem<128>(), stream>>>(mq, mk, mv, a);
+    } else {
+      auto kern = attn_fwd2_kernel<64>;
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd2_smem<64>()));
+      kern<<<grid2, kFwd2Threads, fwd2_smem<64>(), stream>>>(mq, mk, mv, a);
+    }
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return {o, lse};
+  }
+  const int grid = a.B * Hq * ((int)S / kTile);
   if (D == 128) {
     auto kern = attn_fwd_kernel<128>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fwd_smem<128>()));

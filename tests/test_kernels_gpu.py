@@ -191,16 +191,18 @@ def test_fused_linear_ce():
     assert rel(w.grad, wr.grad) < 3e-2
 
 
-@pytest.mark.parametrize("b,s,hq,hkv,d", [(1, 128, 1, 1, 128), (2, 512, 4, 2, 128), (1, 1024, 16, 16, 128),
-                                          (2, 256, 8, 2, 64)])
-def test_attention_fwd_bwd(b, s, hq, hkv, d):
+@pytest.mark.parametrize("b,s,hq,hkv,d,qscale", [(1, 128, 1, 1, 128, 1.0), (2, 512, 4, 2, 128, 1.0),
+                                                 (1, 1024, 16, 16, 128, 1.0), (2, 256, 8, 2, 64, 1.0),
+                                                 (1, 1024, 2, 1, 128, 8.0), (1, 384, 2, 2, 64, 4.0)])
+def test_attention_fwd_bwd(b, s, hq, hkv, d, qscale):
+    """qscale > 1 spreads the scores so that the running row max moves often (rescaling paths)."""
     from placemoe_b200.ops import kernels
     from placemoe_b200.ops.attention import attention_reference, causal_attention
 
     assert hasattr(kernels(), "attn_fwd"), "attention kernel must be built in"
     torch.manual_seed(7)
     t = b * s
-    q = torch.randn(t, hq, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    q = (torch.randn(t, hq, d, device="cuda") * qscale).to(torch.bfloat16).requires_grad_()
     k = torch.randn(t, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     v = torch.randn(t, hkv, d, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     o = causal_attention(q, k, v, s)
