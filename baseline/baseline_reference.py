@@ -136,7 +136,7 @@ def main(args) -> int:
             losses.append(loss.detach())
         veomni_clip_grad_norm(model, 1.0)
         opt.step()
-        opt.zero_grad(set_to_none=True)
+        opt.zero_grad()
         loss = torch.stack(losses).mean()
         return float(loss.item()) if read_loss else loss
 

@@ -43,7 +43,10 @@ def parse():
     p.add_argument("--seq", type=int, default=4096)
     p.add_argument("--batch-per-gpu", type=int, default=8)
     p.add_argument("--micro-batch", type=int, default=4)
-    p.add_argument("--redundant-slots", type=int, default=0)
+    p.add_argument("--redundant-slots", type=int, default=-1,
+                   help="extra expert slots per GPU for replicas (default: 1 when N > 1, else 0)")
+    p.add_argument("--plan-steps", type=int, default=-1,
+                   help="steps of captured routes the PlaceMoE planner uses before timing (default: 20 when N > 1)")
     p.add_argument("--artifact", default="")
     p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
     p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
@@ -103,6 +106,59 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max((num(r[3]) or 0) for r in rows)}
 
 
+def plan_placement(trainer, pool, args, rank, world):
+    """PlaceMoE static placement for the timed run: capture routes for ``plan_steps``
+    training steps, plan L,M on rank 0 (CPU planner), install on every rank with
+    parameter + optimizer-state migration.  Returns a summary for the JSON line."""
+    import tempfile
+
+    import torch.distributed as dist
+
+    from placemoe_b200.parallel.migration import migrate_layer
+    from placemoe_b200.parallel.route_capture import RouteRecorder
+    from placemoe_b200.placemoe import plan_placemoe
+    from placemoe_b200.placemoe.artifacts import validate_placemoe_artifact
+
+    root = tempfile.mkdtemp(prefix="pm_routes_") if rank == 0 else ""
+    holder = [root]
+    dist.broadcast_object_list(holder, src=0)
+    root = holder[0]
+    rec = RouteRecorder(trainer.model, root)
+    rec.enabled = True
+    for s in range(args.plan_steps):
+        trainer.train_step(next(pool))
+        rec.record_step(s)
+    rec.enabled = False
+    for blk in trainer.model.moe_blocks():
+        blk.route_sink = None
+    cfg = trainer.model_cfg
+    t0 = time.perf_counter()
+    payload = [None]
+    if rank == 0:
+        out = os.path.join(root, "layout.json")
+        plan_placemoe.main([
+            "--route-root", root, "--optimize-steps", ",".join(str(i) for i in range(args.plan_steps)),
+            "--ep-size", str(world), "--num-experts", str(cfg.num_experts),
+            "--redundant-slots-per-rank", str(args.redundant_slots), "--hidden-size", str(cfg.hidden_size),
+            "--layers", str(cfg.num_hidden_layers), "--workers", str(min(8, os.cpu_count() or 1)),
+            "--output-layout", out, "--output-report", os.path.join(root, "report.json"),
+        ])
+        with open(out) as f:
+            payload[0] = json.load(f)
+    dist.broadcast_object_list(payload, src=0)
+    planner_ms = (time.perf_counter() - t0) * 1e3
+    plans = validate_placemoe_artifact(payload[0])
+    t1 = time.perf_counter()
+    moved = 0
+    for blk in trainer.model.moe_blocks():
+        moved += migrate_layer(trainer, blk, plans[blk.layer_key])
+    trainer._norm_table = None
+    trainer.optimizer._tables.clear()
+    dist.barrier()
+    return {"plan_steps": args.plan_steps, "planner_ms": round(planner_ms, 1),
+            "install_ms": round((time.perf_counter() - t1) * 1e3, 1), "moved_slots": moved}
+
+
 def run_reference(args):
     from baseline_reference import run as ref_run  # noqa: E402  (baseline/ helper)
 
@@ -131,6 +187,10 @@ def main():
     rank, world = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if args.redundant_slots < 0:
+        args.redundant_slots = 1 if world > 1 else 0
+    if args.plan_steps < 0:
+        args.plan_steps = 20 if world > 1 and not args.artifact else 0
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     overrides = {"num_hidden_layers": args.layers} if args.layers else {}
@@ -147,6 +207,8 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+
+    plan_info = plan_placement(trainer, pool, args, rank, world) if args.plan_steps > 0 else None
 
     for i in range(args.warmup):
         trainer.train_step(next(pool))
@@ -213,6 +275,10 @@ def main():
                 "micro_batch": args.micro_batch,
                 "parallelism": f"dp{world}+ep{world}",
                 "ep_transport": args.ep_transport if world > 1 else "none",
+                "placement": (f"PlaceMoE static L,M planned from {args.plan_steps} captured steps, "
+                              f"{args.redundant_slots} replica slot(s)/GPU" if plan_info else
+                              ("artifact " + args.artifact if args.artifact else
+                               ("fixed EP" if world > 1 else "single GPU"))),
                 "router_bias": f"{mcfg.router_bias_scale} * log Zipf(s={mcfg.router_bias_zipf_s})",
                 "l2": "working set >> 126 MB L2 (no explicit flush)",
                 "baseline_metric": BASELINE_METRIC,
@@ -222,6 +288,7 @@ def main():
                     "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e, 3), "last_loss": last},
             "gpu_launches": launches,
             "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 2**30, 1),
+            "planner": plan_info,
             "model_tflops_per_gpu": round(flops / (ms / 1e3) / world / 1e12, 1),
         }
         print(json.dumps(line), flush=True)
