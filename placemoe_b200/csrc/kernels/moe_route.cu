@@ -458,6 +458,7 @@ void gather_rows(torch::Tensor src, torch::Tensor row_token, c10::optional<torch
   PM_CHECK_CUDA(src); PM_CHECK_CUDA(row_token); PM_CHECK_CUDA(out); PM_CHECK_CUDA_OPT(end);
   const int cap = (int)out.size(0);
   TORCH_CHECK(row_token.numel() >= cap, "row_token too short");
+  TORCH_CHECK(row_token.is_contiguous() && row_token.scalar_type() == torch::kInt32, "row_token must be contiguous int32");
   c10::cuda::CUDAGuard guard(src.device());
   const int* ep = end.has_value() ? end->data_ptr<int>() : nullptr;
   const int grid = std::max(1, std::min((cap + 7) / 8, sms() * 8));
@@ -468,6 +469,7 @@ void gather_rows(torch::Tensor src, torch::Tensor row_token, c10::optional<torch
 
 void sum_rows(torch::Tensor src, torch::Tensor row_of, torch::Tensor out) {
   TORCH_CHECK(src.is_contiguous() && out.is_contiguous(), "contiguous");
+  TORCH_CHECK(row_of.is_contiguous() && row_of.scalar_type() == torch::kInt32, "row_of must be contiguous int32");
   PM_CHECK_CUDA(src); PM_CHECK_CUDA(row_of); PM_CHECK_CUDA(out);
   const int H = (int)src.size(-1);
   const int T = (int)out.size(0);

@@ -119,8 +119,8 @@ def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = 
                       capture_routes: bool = False, transport: str = "auto") -> ParallelState:
     """Attach EP placement + dispatch to every MoE block and back dense grads with one bucket.
 
-    ``transport``: "auto" / "nccl" (all-to-all with exchanged split sizes) or "p2p" (peer-memory
-    kernels, CUDA only).
+    ``transport``: "auto" (peer-memory kernels on CUDA, all-to-all otherwise), "p2p" or "nccl"
+    (all-to-all with exchanged split sizes, the baseline).
     The model must already hold the local expert slots (built with
     ``num_local_slots = topology.slots_per_rank`` and filled through
     :func:`placement.slice_expert_weights` or an expert_init callback).
@@ -137,8 +137,8 @@ def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = 
     ep = None
     if world > 1:
         dev0 = device or next(model.parameters()).device
-        # "auto" uses the all-to-all transport until the peer-memory path measures faster end to end
-        use_p2p = transport == "p2p"
+        # "auto": peer-memory kernels on CUDA (no host synchronisation), all-to-all on CPU / gloo
+        use_p2p = transport == "p2p" or (transport == "auto" and dev0.type == "cuda")
         if use_p2p:
             from .p2p_ep import P2PExpertParallel
 

@@ -73,13 +73,15 @@ def build_dispatch(dest: torch.Tensor, lslot: torch.Tensor, world: int):
     """
     t, k = dest.shape
     dev = dest.device
-    onehot = F.one_hot(dest, world).amax(1)  # [T, W] 1 if the token goes to that GPU
-    row_counts = onehot.sum(0)
+    onehot_t = torch.zeros(world, t, dtype=torch.long, device=dev)
+    onehot_t[dest.reshape(-1), torch.arange(t, device=dev).repeat_interleave(k)] = 1  # [W, T]
+    onehot = onehot_t.t()  # [T, W] 1 if the token goes to that GPU
+    row_counts = onehot_t.sum(1)
     # send order: destination-major, token-minor
-    d_idx, t_idx = torch.nonzero(onehot.t(), as_tuple=True)
+    d_idx, t_idx = torch.nonzero(onehot_t, as_tuple=True)
     send_tok = t_idx
-    # position of (t, d) within destination d's chunk
-    pos_in_d = torch.cumsum(onehot, 0) - 1  # [T, W]
+    # position of (t, d) within destination d's chunk (scanned along the contiguous axis)
+    pos_in_d = (torch.cumsum(onehot_t, 1) - 1).t()  # [T, W]
     flat_d = dest.reshape(-1)
     flat_t = torch.arange(t, device=dev).repeat_interleave(k)
     order = torch.argsort(flat_d * (t * k) + torch.arange(t * k, device=dev))

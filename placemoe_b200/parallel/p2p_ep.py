@@ -113,13 +113,24 @@ class SymmetricArena:
 
 
 def _dispatch_tables(dest: torch.Tensor, world: int):
-    """dest [T, k] int64 -> onehot [T, W], pos_in_d [T, W], asg order pos [T, k] within destination."""
+    """dest [T, k] int64 -> onehot [T, W], pos_in_d [T, W], asg order pos [T, k] within destination.
+
+    Built with scatter and row-wise scans only: ``F.one_hot`` validates its
+    input with a device-to-host read, and a scan along a long outer dimension
+    with W inner columns runs on W threads.  Scans run over [W, n] rows.
+    """
     t, k = dest.shape
-    onehot = F.one_hot(dest, world).amax(1).to(torch.int32)  # [T, W]
-    pos_in_d = torch.cumsum(onehot, 0, dtype=torch.int32) - 1
-    oh_asg = F.one_hot(dest.reshape(-1), world).to(torch.int32)  # [T*k, W] in (t, j) order
-    asg_pos = (torch.cumsum(oh_asg, 0, dtype=torch.int32) - 1).gather(1, dest.reshape(-1, 1)).view(t, k)
-    return onehot, pos_in_d, asg_pos, oh_asg.sum(0)
+    dev = dest.device
+    onehot_t = torch.zeros(world, t, dtype=torch.int32, device=dev)
+    tok = torch.arange(t, device=dev).unsqueeze(1).expand(t, k)
+    onehot_t[dest.reshape(-1), tok.reshape(-1)] = 1  # [W, T] (duplicates write the same 1)
+    pos_t = torch.cumsum(onehot_t, 1, dtype=torch.int32) - 1  # [W, T]
+    flat = dest.reshape(-1)
+    oh_asg_t = torch.zeros(world, t * k, dtype=torch.int32, device=dev)
+    oh_asg_t[flat, torch.arange(t * k, device=dev)] = 1  # [W, T*k] in (t, j) order
+    asg_pos = (torch.cumsum(oh_asg_t, 1, dtype=torch.int32) - 1).gather(0, flat.view(1, -1)).view(t, k)
+    # [T, W] row-major: the index tables built from these are handed to kernels as flat arrays
+    return onehot_t.t().contiguous(), pos_t.t().contiguous(), asg_pos, oh_asg_t.sum(1)
 
 
 class _P2PMoE(torch.autograd.Function):
@@ -211,7 +222,8 @@ class _P2PMoE(torch.autograd.Function):
         y = torch.empty(t, h, device=dev, dtype=torch.bfloat16)
         kn.sum_rows(back, back_pos.contiguous(), y)
         _mark("fwd.token_sum")
-        ctx.save_for_backward(xd, hbuf, gu, w1, w2, dst_row, back_pos, d32, dst_asg.to(torch.int32), C)
+        ctx.save_for_backward(xd, hbuf, gu, w1, w2, dst_row.contiguous(), back_pos.contiguous(), d32,
+                              dst_asg.to(torch.int32), C)
         ctx.loc = loc
         ctx.blk, ctx.arena, ctx.shape = blk, arena, (t, h, k)
         return y
