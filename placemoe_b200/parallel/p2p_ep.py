@@ -32,6 +32,8 @@ NCCL all-to-all data plane replaced by peer stores.
 
 from __future__ import annotations
 
+import math
+
 import torch
 import torch.distributed as dist
 import torch.nn.functional as F
@@ -181,9 +183,13 @@ class _P2PMoE(torch.autograd.Function):
         n_rows = C[:, r, 0].sum()  # device scalars
         n_asg = C[:, r, 1].sum()
         R_cap = W * arena.tokens
-        A_cap = R_cap * k
+        # expert work is sized for `asg_cap` received assignments (a multiple of the balanced
+        # share); the largest count seen is kept on the device and checked once per step
+        ep = blk.ep
+        A_cap = ep.asg_cap(arena)
+        torch.maximum(ep.max_recv, n_asg.reshape(1).to(torch.int32), out=ep.max_recv)
         recv_x = arena.view("recv_rows", (R_cap, h), torch.bfloat16)
-        rmeta = arena.view("recv_meta", (A_cap, 4), torch.int32)
+        rmeta = arena.view("recv_meta", (R_cap * k, 4), torch.int32)[:A_cap]
         valid = torch.arange(A_cap, device=dev) < n_asg
         slots = torch.where(valid, rmeta[:, 1], torch.full_like(rmeta[:, 1], -1)).contiguous()
         rrow = torch.where(valid, rmeta[:, 0], torch.full_like(rmeta[:, 0], -1)).contiguous()
@@ -270,7 +276,7 @@ class _P2PMoE(torch.autograd.Function):
                         arena.layout["back_rows"], h)
         # routing-weight gradients: per received assignment -> source flat (t*k + j) index
         dw_asg = kn.gather_scalar(dscale, loc["row_of"])  # [A_cap]
-        n_asg = C[:, r, 1].sum().to(torch.int32).reshape(1)
+        n_asg = torch.clamp(C[:, r, 1].sum(), max=dw_asg.numel()).to(torch.int32).reshape(1)
         kn.p2p_put_words(dw_asg.contiguous().view(torch.int32), loc["asg_src_rank"], loc["asg_src_idx"], n_asg,
                          dw_asg.numel(), arena.peers, arena.layout["back_words"])
         _mark("bwd.back_puts")
@@ -326,15 +332,28 @@ def _local_plan(blk, rrow, slots, rw, R_cap, k, expected_asg):
             "row_scale": row_scale, "table": table, "align": align}
 
 
-class P2PExpertParallel:
-    """Drop-in replacement of :class:`ExpertParallel` on CUDA with the peer-memory transport."""
+class EPCapacityExceeded(RuntimeError):
+    """A rank received more expert assignments than its buffers hold in this step."""
 
-    def __init__(self, group=None, capture_routes: bool = False):
+
+class P2PExpertParallel:
+    """Drop-in replacement of :class:`ExpertParallel` on CUDA with the peer-memory transport.
+
+    Expert buffers are sized for ``capacity_factor`` times the balanced share
+    of received assignments (at most all of them), so no host read of the
+    received count is needed per layer.  The largest count of the step is
+    checked once per step (:meth:`check_capacity`, before the optimizer); on
+    overflow the trainer grows the factor and recomputes the step.
+    """
+
+    def __init__(self, group=None, capture_routes: bool = False, capacity_factor: float = 2.0):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.capture_routes = capture_routes
+        self.capacity_factor = capacity_factor
         self.arena: SymmetricArena | None = None
+        self.max_recv: torch.Tensor | None = None
         from .ep import ExpertParallel
 
         self._router = ExpertParallel._route.__get__(self)
@@ -342,7 +361,26 @@ class P2PExpertParallel:
     def _arena_for(self, t, k, h, device):
         if self.arena is None or not self.arena.fits(t, k, h):
             self.arena = SymmetricArena(self.group, self.world, self.rank, t, k, h, device)
+        if self.max_recv is None or self.max_recv.device != device:
+            self.max_recv = torch.zeros(1, dtype=torch.int32, device=device)
         return self.arena
+
+    def asg_cap(self, arena: SymmetricArena) -> int:
+        """Received assignments the expert buffers are sized for (at most everything)."""
+        full = arena.world * arena.tokens * arena.k
+        return min(full, int(math.ceil(self.capacity_factor * arena.tokens * arena.k)))
+
+    def check_capacity(self) -> None:
+        """Raise :class:`EPCapacityExceeded` if any rank overflowed since the last check (one host read)."""
+        if self.max_recv is None or self.arena is None:
+            return
+        worst = self.max_recv.clone()
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX, group=self.group)
+        self.max_recv.zero_()
+        cap = self.asg_cap(self.arena)
+        if int(worst.item()) > cap:
+            raise EPCapacityExceeded(f"received {int(worst.item())} expert assignments, capacity {cap} "
+                                     f"(capacity_factor {self.capacity_factor})")
 
     def moe_forward(self, blk, x, bias, aux_coef):
         t, h = x.shape

@@ -33,6 +33,7 @@ from ..models.moe_decoder import build_model
 from ..ops import moe as moe_ops
 from ..ops import mp as mp_ops
 from ..ops.optim import FusedAdamW
+from ..parallel.p2p_ep import EPCapacityExceeded
 from ..parallel.data_parallel import (expert_init_from_full, expert_topology, parallelize_model,
                                       redundant_slot_weights, sync_replica_gradients)
 from ..placemoe.artifacts import load_artifact
@@ -163,9 +164,23 @@ class Trainer:
         ids = input_ids.to(self.device, non_blocking=True)
         mb = max(1, cfg.micro_batch_size)
         n_micro = max(1, ids.shape[0] // mb)
-        losses = []
-        for i in range(n_micro):
-            losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+        ep = self.pstate.ep
+        for attempt in range(4):
+            losses = []
+            for i in range(n_micro):
+                losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+            if not hasattr(ep, "check_capacity"):
+                break
+            try:
+                ep.check_capacity()  # one host read per step: did any rank overflow its expert buffers?
+                break
+            except EPCapacityExceeded:
+                if attempt == 3:
+                    raise
+                # recompute the step with larger expert buffers (gradients restart from zero)
+                self._zero_all_grads()
+                ep.capacity_factor = min(float(self.world), ep.capacity_factor * 2)
+                self.metrics["ep_capacity_factor"] = ep.capacity_factor
         loss = torch.stack(losses).mean()
         self.optimizer_step()
         self.global_step += 1
@@ -223,6 +238,14 @@ class Trainer:
             g["lr"] = self.lr_at(self.global_step)
         self.optimizer.step()
         self.zero_grad()
+
+    def _zero_all_grads(self):
+        for p in self.model.parameters():
+            p.grad = None
+            g = getattr(p, "main_grad", None)
+            if g is not None:
+                g.zero_()
+                p._main_grad_stale = False
 
     def zero_grad(self):
         expert = {id(p) for p in self.model.expert_parameters()}
