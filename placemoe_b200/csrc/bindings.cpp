@@ -39,6 +39,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_allgather_words", &pm::p2p_allgather_words);
   m.def("p2p_barrier", &pm::p2p_barrier);
   m.def("p2p_reduce_f32", &pm::p2p_reduce_f32);
+  m.def("p2p_sum_f32", &pm::p2p_sum_f32);
   m.def("p2p_pull", &pm::p2p_pull);
   m.def("device_error", &pm::device_error, "read (and optionally clear) the kernels' error words");
 }

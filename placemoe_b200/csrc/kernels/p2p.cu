@@ -12,8 +12,8 @@
 //                  word, then acquire-wait until every peer's epoch reached ours.
 //                  Bounded: after the budget the kernel records kErrPeerTimeout and
 //                  returns (the host raises); it never traps or spins forever.
-//   p2p_gather_rows pull rows from peers (migration / replica-gradient exchange)
-//   p2p_reduce_rows sum the same rows of several peers into a local buffer
+//   p2p_sum_f32    sum fp32 buffers read from several peers (replica-gradient reduction)
+//   p2p_pull       bulk copy from one peer's buffer (expert-state migration)
 //
 // Ordering: puts of a phase are issued by kernels that complete before the
 // barrier kernel on the same stream; the barrier's system-scope release
@@ -132,6 +132,29 @@ __global__ void __launch_bounds__(256) p2p_reduce_f32_kernel(float* __restrict__
     }
 }
 
+// out[i] = sum over sources j of fp32 element i at peer[src_rank[j]] + src_off[j] (byte offsets):
+// the replica-gradient reduction, every copy of an expert read straight from its GPU.
+__global__ void __launch_bounds__(256) p2p_sum_f32_kernel(float* __restrict__ out, long long n,
+                                                          const long long* __restrict__ peers,
+                                                          const int* __restrict__ src_rank,
+                                                          const long long* __restrict__ src_off, int nsrc) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k = 0; k < nsrc; ++k) {
+      const float4 v = reinterpret_cast<const float4*>(peers[src_rank[k]] + src_off[k])[i];
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    reinterpret_cast<float4*>(out)[i] = acc;
+  }
+  if (blockIdx.x == 0)
+    for (long long i = n4 * 4 + threadIdx.x; i < n; i += blockDim.x) {
+      float acc = 0.f;
+      for (int k = 0; k < nsrc; ++k) acc += reinterpret_cast<const float*>(peers[src_rank[k]] + src_off[k])[i];
+      out[i] = acc;
+    }
+}
+
 // dst (local) <- peer[src_rank] + region_off, n bytes (16-byte multiple): pull copy over NVLink
 __global__ void __launch_bounds__(256) p2p_pull_kernel(uint4* __restrict__ dst, const long long* __restrict__ peers,
                                                        int src_rank, long long region_off, long long n16) {
@@ -211,6 +234,22 @@ void p2p_reduce_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor ranks,
   p2p_reduce_f32_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       out.data_ptr<float>(), n, reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), ranks.data_ptr<int>(),
       (int)ranks.numel(), region_off);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void p2p_sum_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor src_rank, torch::Tensor src_off) {
+  PM_CHECK_CUDA(out); PM_CHECK_CUDA(peers); PM_CHECK_CUDA(src_rank); PM_CHECK_CUDA(src_off);
+  TORCH_CHECK(out.scalar_type() == torch::kFloat32 && out.is_contiguous(), "out fp32 contiguous");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0, "out 16-byte aligned");
+  TORCH_CHECK(src_rank.scalar_type() == torch::kInt32 && src_off.scalar_type() == torch::kInt64 &&
+              src_rank.numel() == src_off.numel(), "src_rank int32 / src_off int64 of equal length");
+  if (out.numel() == 0 || src_rank.numel() == 0) return;
+  c10::cuda::CUDAGuard guard(out.device());
+  const long long n = out.numel();
+  const int grid = std::max(1, std::min((int)((n / 4 + 255) / 256), sm_cnt() * 4));
+  p2p_sum_f32_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      out.data_ptr<float>(), n, reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()),
+      src_rank.data_ptr<int>(), reinterpret_cast<const long long*>(src_off.data_ptr<int64_t>()), (int)src_rank.numel());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -67,6 +67,7 @@ void p2p_put_words(torch::Tensor vals, torch::Tensor dst_rank, torch::Tensor dst
 void p2p_allgather_words(torch::Tensor vals, torch::Tensor peers, int64_t region_off, int64_t my_rank);
 void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s);
 void p2p_reduce_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor ranks, int64_t region_off);
+void p2p_sum_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor src_rank, torch::Tensor src_off);
 void p2p_pull(torch::Tensor dst, torch::Tensor peers, int64_t src_rank, int64_t region_off);
 
 int device_error(bool reset);

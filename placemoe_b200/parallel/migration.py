@@ -14,9 +14,10 @@ in the staging buffers and the live tensors are written only after a second
 agreement, so every rank ends on the old placement or every rank on the new.  Emptied slots are
 zeroed.  bf16 compute copies of changed parameters are refreshed afterwards.
 
-Transports: a peer-to-peer copy kernel over NVLink when every GPU of the
-group is reachable by peer access (``p2p_migrate`` in the kernel library),
-else ``batch_isend_irecv`` in a globally ordered schedule (NCCL or gloo).
+Transports: a peer-memory copy over NVLink when the trainer holds a peer
+exchange buffer (``p2p_sync.p2p_transfer``: sources stage, destinations pull
+with the ``p2p_pull`` kernel), else ``batch_isend_irecv`` in a globally
+ordered schedule (NCCL or gloo).
 
 Reference parity: veomni/distributed/moe/hiermoe/expert_swap.py:1358-1542
 (_cover_grouped_slot_entries_atomic), :1580-1716 (optimizer state binding),
@@ -108,14 +109,17 @@ def migrate_layer(trainer, blk, new_plan: LayerPlan, group=None) -> int:
     #    aborts on every rank before any transfer is posted (nobody waits on a missing peer)
     staging: dict[int, torch.Tensor] = {}
     sends: list[tuple[int, torch.Tensor]] = []
+    outgoing: dict[int, torch.Tensor] = {}  # transfer index -> packed state (remote destination)
     recvs: list[tuple[int, int]] = []
     try:
-        for src, dst in transfers:  # globally consistent order
+        for i, (src, dst) in enumerate(transfers):  # globally consistent order
             rs, rd = src // spr, dst // spr
             if rd == rank and rs == rank:
                 staging[dst] = allocate_staging(_pack(_slot_state(blk, opt, src - rank * spr)))
             elif rs == rank:
-                sends.append((rd, allocate_staging(_pack(_slot_state(blk, opt, src - rank * spr)))))
+                buf = allocate_staging(_pack(_slot_state(blk, opt, src - rank * spr)))
+                sends.append((rd, buf))
+                outgoing[i] = buf
             elif rd == rank:
                 staging[dst] = allocate_staging(torch.empty_like(_pack(_slot_state(blk, opt, 0))))
                 recvs.append((rs, dst))
@@ -124,20 +128,27 @@ def migrate_layer(trainer, blk, new_plan: LayerPlan, group=None) -> int:
         ok = False
     if not _agree(ok, world, group):
         return 0  # every rank keeps the old placement
-    # 2) transfers (send/recv in the same global order on every rank)
+    # 2) transfers: a peer-memory copy kernel when the group has a peer exchange buffer,
+    #    else send/recv in the same global order on every rank
+    xchg = getattr(trainer, "peer_exchange", None)
     try:
-        ops = []
-        si = 0
-        for src, dst in transfers:
-            rs, rd = src // spr, dst // spr
-            if rs == rank and rd != rank:
-                ops.append(dist.P2POp(dist.isend, sends[si][1], rd, group=group))
-                si += 1
-            elif rd == rank and rs != rank:
-                ops.append(dist.P2POp(dist.irecv, staging[dst], rs, group=group))
-        if ops:
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()
+        if xchg is not None and world > 1:
+            from .p2p_sync import p2p_transfer
+
+            p2p_transfer(xchg, transfers, spr, rank, outgoing, staging)
+        else:
+            ops = []
+            si = 0
+            for src, dst in transfers:
+                rs, rd = src // spr, dst // spr
+                if rs == rank and rd != rank:
+                    ops.append(dist.P2POp(dist.isend, sends[si][1], rd, group=group))
+                    si += 1
+                elif rd == rank and rs != rank:
+                    ops.append(dist.P2POp(dist.irecv, staging[dst], rs, group=group))
+            if ops:
+                for w in dist.batch_isend_irecv(ops):
+                    w.wait()
         ok = True
     except Exception:
         ok = False

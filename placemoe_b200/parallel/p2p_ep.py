@@ -287,6 +287,9 @@ class _P2PMoE(torch.autograd.Function):
         kn.sum_rows(back, back_pos, dx)
         dw = arena.view("back_words", (R_cap * k,), torch.float32)[: t * k].clone().view(t, k)
         _mark("bwd.token_sum")
+        rs = getattr(blk.ep, "replica_sync", None)
+        if rs is not None:  # this layer's expert gradients are final: reduce replicas on the side stream
+            rs.layer_ready(blk)
         return dx, dw, None, None, None, None
 
 
@@ -354,6 +357,7 @@ class P2PExpertParallel:
         self.capacity_factor = capacity_factor
         self.arena: SymmetricArena | None = None
         self.max_recv: torch.Tensor | None = None
+        self.replica_sync = None  # p2p_sync.ReplicaGradSync, set by the trainer
         from .ep import ExpertParallel
 
         self._router = ExpertParallel._route.__get__(self)

@@ -109,6 +109,16 @@ class Trainer:
                                         capture_routes=cfg.capture_routes, transport=cfg.ep_transport)
         self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
                                     weight_decay=cfg.weight_decay)
+        # peer-memory exchange for replica gradients and migration (CUDA, peer-memory EP transport)
+        self.peer_exchange = None
+        self.replica_sync = None
+        if self.world > 1 and self.device.type == "cuda" and hasattr(self.pstate.ep, "replica_sync"):
+            from ..parallel.p2p_sync import PeerExchange, ReplicaGradSync
+
+            nbytes = max(p.numel() * 4 for p in self.model.expert_parameters())
+            self.peer_exchange = PeerExchange(None, self.device, nbytes)
+            self.replica_sync = ReplicaGradSync(self.peer_exchange)
+            self.pstate.ep.replica_sync = self.replica_sync
         self._norm_table = None
         self.global_step = 0
         self.hot_update = None  # set by placement runtime (hot updates)
@@ -165,10 +175,15 @@ class Trainer:
         mb = max(1, cfg.micro_batch_size)
         n_micro = max(1, ids.shape[0] // mb)
         ep = self.pstate.ep
+        rsync = self.replica_sync
         for attempt in range(4):
             losses = []
             for i in range(n_micro):
+                if rsync is not None:  # replicas are reduced during the last micro-batch's backward
+                    rsync.armed = i == n_micro - 1
                 losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+            if rsync is not None:
+                rsync.armed = False
             if not hasattr(ep, "check_capacity"):
                 break
             try:
@@ -178,6 +193,8 @@ class Trainer:
                 if attempt == 3:
                     raise
                 # recompute the step with larger expert buffers (gradients restart from zero)
+                if rsync is not None:
+                    rsync.wait()
                 self._zero_all_grads()
                 ep.capacity_factor = min(float(self.world), ep.capacity_factor * 2)
                 self.metrics["ep_capacity_factor"] = ep.capacity_factor
@@ -192,8 +209,10 @@ class Trainer:
         cfg = self.cfg
         # gradients of micro-batches were accumulated; average them
         nmb = max(1, cfg.batch_per_rank // max(1, cfg.micro_batch_size))
+        if self.replica_sync is not None:
+            self.replica_sync.wait()  # replicas were reduced over peer memory during the backward
         moe_ops.settle_stale_grads(self.model.expert_parameters())
-        if self.world > 1:
+        if self.replica_sync is None and self.world > 1:
             sync_replica_gradients(self.model, self.pstate.placements)
             if self.pstate.dense_bucket is not None:
                 self.pstate.dense_bucket.reduce()

@@ -1,0 +1,109 @@
+"""Peer-memory replica-gradient reduction and migration transfers vs their NCCL counterparts (2 GPUs).
+
+Runs as 2 child processes, one per GPU, with NVLS disabled; skipped on fewer than 2 GPUs.
+"""
+
+import os
+
+import pytest
+import torch
+
+from dist_utils import free_port
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _worker(rank, world, port, out_q):
+    import torch.distributed as dist
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank), "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        import numpy as np
+
+        from placemoe_b200.models.config import get_preset
+        from placemoe_b200.models.moe_decoder import MoEBlock
+        from placemoe_b200.ops import check_device_error
+        from placemoe_b200.parallel.data_parallel import expert_topology, sync_replica_gradients
+        from placemoe_b200.parallel.p2p_sync import PeerExchange, ReplicaGradSync, p2p_transfer, sync_layer
+        from placemoe_b200.parallel.placement import build_placements
+        from placemoe_b200.placemoe.seeds import mirrored_r2_plan
+
+        cfg = get_preset("small_qwen3_moe")
+        topo = expert_topology(cfg.num_experts, world, cfg.num_experts // world)  # two copies of every expert
+        plan = mirrored_r2_plan(topo)
+        with torch.device("cuda"):
+            blk = MoEBlock(cfg, 0, topo.slots_per_rank)
+        blk.placement = build_placements({blk.layer_key: plan}, topo, rank, [blk.layer_key])[blk.layer_key]
+        g = torch.Generator(device="cuda").manual_seed(10 + rank)
+        grads = {}
+        for p in (blk.gate_up_proj, blk.down_proj):
+            p.main_grad = torch.randn(p.shape, device="cuda", generator=g)
+            grads[p] = p.main_grad.clone()
+
+        class _M:
+            def moe_blocks(self):
+                return [blk]
+
+        sync_replica_gradients(_M(), {blk.layer_key: blk.placement})
+        ref = {p: p.main_grad.clone() for p in grads}
+        for p in grads:
+            p.main_grad.copy_(grads[p])
+        x = PeerExchange(None, "cuda", max(p.numel() * 4 for p in grads))
+        rs = ReplicaGradSync(x)
+        sync_layer(blk, rs._plan(blk), x)
+        torch.cuda.synchronize()
+        check_device_error()
+        err_sync = max((p.main_grad - ref[p]).abs().max().item() for p in grads)
+
+        # migration transfers: every slot state moves to the other rank's slot of the same index
+        spr = topo.slots_per_rank
+        transfers = [(s, (s + spr) % (2 * spr)) for s in range(2 * spr)]
+        n = 4096
+        outgoing, staging, expect = {}, {}, {}
+        for i, (s, d) in enumerate(transfers):
+            payload = torch.full((n,), float(s * 1000 + 7), device="cuda")
+            if s // spr == rank:
+                outgoing[i] = payload
+            if d // spr == rank:
+                staging[d] = torch.zeros(n, device="cuda")
+                expect[d] = payload
+        p2p_transfer(x, transfers, spr, rank, outgoing, staging)
+        torch.cuda.synchronize()
+        check_device_error()
+        err_mig = max((staging[d] - expect[d]).abs().max().item() for d in staging)
+        out_q.put((rank, err_sync, err_mig, int(np.asarray(plan.slot_to_logical).size)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_p2p_replica_sync_and_migration_match_nccl():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = {}
+    while not q.empty():
+        r, e1, e2, _ = q.get()
+        res[r] = (e1, e2)
+    assert len(res) == 2
+    for r, (e1, e2) in res.items():
+        assert e1 < 1e-5, (r, e1)
+        assert e2 == 0.0, (r, e2)
