@@ -43,7 +43,7 @@ class TextTrainer:
             placemoe_artifact=self.placemoe.initial_artifact, capture_routes=t.hiermoe.capture_routes,
             gradient_checkpointing=t.gradient_checkpointing,
             device="cuda" if torch.cuda.is_available() else "cpu", log_interval=t.log_interval,
-            output_dir=t.output_dir, save_steps=t.save_steps,
+            output_dir=t.output_dir, save_steps=t.save_steps, ep_transport=t.hiermoe.transport,
         )
         self.trainer = Trainer(cfg, mcfg)
         self.data = SyntheticTokens(mcfg.vocab_size, per_rank, args.data.max_seq_len, seed=args.data.seed,
@@ -64,11 +64,21 @@ class TextTrainer:
             load_checkpoint(self.trainer, t.load_checkpoint_path)
         if self.trainer.rank == 0:
             save_args(args, t.output_dir)
+        from .callbacks import CallbackList, EnvironmentMeterCallback, RouterMonitorCallback
+
+        world = self.trainer.world
+        self.callbacks = CallbackList([
+            RouterMonitorCallback(t.log_interval),
+            EnvironmentMeterCallback(per_rank * args.data.max_seq_len * world,
+                                     mcfg.flops_per_token(args.data.max_seq_len), t.log_interval,
+                                     os.path.join(t.output_dir, "metrics.jsonl")),
+        ])
 
     def train(self):
         t = self.args.train
         tr = self.trainer
         t0 = time.perf_counter()
+        self.callbacks.on_train_begin(tr)
         for step in range(tr.global_step, t.max_steps):
             if self.recorder is not None:
                 self.recorder.enabled = step < max(t.hiermoe.route_capture_steps, 0) or t.hiermoe.capture_routes
@@ -84,6 +94,8 @@ class TextTrainer:
                 from ..checkpoint import save_checkpoint
 
                 save_checkpoint(tr, os.path.join(t.output_dir, "checkpoints"))
+            self.callbacks.on_step_end(tr, step, loss)
+        self.callbacks.on_train_end(tr)
         if dist.is_initialized():
             dist.barrier()
         return tr
