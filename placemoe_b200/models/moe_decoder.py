@@ -105,6 +105,7 @@ class MoEBlock(nn.Module):
         self.last_route = None  # [T, k] logical routes of the last forward (route capture)
         self.route_sink = None  # RouteRecorder when routes are captured for the planner
         self.keep_expert_rows = True  # False: recompute dispatched rows in the backward (less memory)
+        self.router_replay = None  # ops.router_replay.RouterReplay (record / replay selected experts)
 
     @property
     def num_local_slots(self) -> int:
@@ -139,12 +140,14 @@ class MoEBlock(nn.Module):
             lut = self.placement.local_lut_device(x.device) if self.placement is not None else None
             y, aux, route = moe_ops.moe_block(x, self.gate, bias, w1, w2, self.gate_up_proj, self.down_proj,
                                               cfg.num_experts_per_tok, cfg.norm_topk_prob, self.num_local_slots,
-                                              lut=lut, aux_coef=aux_coef, keep_rows=self.keep_expert_rows)
+                                              lut=lut, aux_coef=aux_coef, keep_rows=self.keep_expert_rows,
+                                              replay=self.router_replay, layer=self.layer_idx)
         else:
             lut = self.placement.local_lut_cpu() if self.placement is not None else None
             y, aux, route = moe_ops.moe_block_reference(x, self.gate, bias, self.gate_up_proj, self.down_proj,
                                                         cfg.num_experts_per_tok, cfg.norm_topk_prob, aux_coef, lut,
-                                                        return_route=True)
+                                                        return_route=True, replay=self.router_replay,
+                                                        layer=self.layer_idx)
         self.last_aux_loss = aux
         self.last_route = route
         if self.route_sink is not None and route is not None:

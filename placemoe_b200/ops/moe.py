@@ -74,7 +74,21 @@ def load_balancing_loss(prob_sum: torch.Tensor, count: torch.Tensor, num_tokens:
     return e * (f * p).sum()
 
 
-def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None, return_route=False):
+def apply_router_replay(replay, layer: int, logits, bias, w, idx, renorm: bool):
+    """Record the routes, or substitute recorded ones (weights recomputed from ``logits``)."""
+    if replay is None or replay.mode == "off":
+        return w, idx
+    if replay.mode == "record":
+        replay.record(layer, idx)
+        return w, idx
+    from .router_replay import replay_weights
+
+    idx = replay.fetch(layer).to(idx.device, idx.dtype)
+    return replay_weights(logits, bias, idx, renorm), idx
+
+
+def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None, return_route=False, replay=None,
+                        layer: int = 0):
     """Eager oracle.  x [T, H]; wg [E, H]; w1 [S, 2I, H]; w2 [S, H, I]; lut: logical -> slot."""
     t = x.shape[0]
     logits = x.float() @ wg.float().t()
@@ -83,6 +97,7 @@ def moe_block_reference(x, wg, bias, w1, w2, k, renorm, aux_coef=0.0, lut=None, 
     w, idx = torch.topk(p, k, dim=-1)
     if renorm:
         w = w / w.sum(-1, keepdim=True)
+    w, idx = apply_router_replay(replay, layer, logits, bias, w, idx, renorm)
     slots = lut[idx] if lut is not None else idx
     inter = w1.shape[1] // 2
     y = torch.zeros(t, x.shape[1], dtype=torch.float32, device=x.device)
@@ -333,7 +348,8 @@ class _AuxLoss(torch.autograd.Function):
         return None, None, None, None, None, None, None
 
 
-def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=None, aux_coef=0.0, keep_rows=True):
+def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=None, aux_coef=0.0, keep_rows=True,
+              replay=None, layer: int = 0):
     """Single-device MoE layer. Returns (y [T, H] bf16, aux_loss or None, router stats).
 
     ``keep_rows=False`` recomputes the dispatched input rows in the backward
@@ -345,8 +361,13 @@ def moe_block(x, wg, bias, w1_bf16, w2_bf16, p1, p2, k, renorm, num_slots, lut=N
     holder: dict = {}
     w, idx, ps, cnt = _Router.apply(logits, bias, k, renorm, holder)
     aux = None
-    if aux_coef:
-        aux = _AuxLoss.apply(w, ps, cnt, t, k, float(aux_coef), holder)
+    if replay is not None and replay.mode == "replay":
+        w, idx = apply_router_replay(replay, layer, logits, bias, w, idx, renorm)
+        idx = idx.to(torch.int32).contiguous()
+    else:
+        if aux_coef:
+            aux = _AuxLoss.apply(w, ps, cnt, t, k, float(aux_coef), holder)
+        apply_router_replay(replay, layer, logits, bias, w, idx, renorm)
     align = segment_align(t * k, num_slots)
     cap = capacity_rows(t, k, num_slots, align)
     offsets, counts, row_of, row_token, row_scale = kn.moe_plan(idx, lut, w.detach(), num_slots, cap, align)

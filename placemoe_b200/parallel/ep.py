@@ -111,7 +111,12 @@ class ExpertParallel:
             logits = moe_ops.linear_fp32(x, blk.gate)
             holder: dict = {}
             w, idx, ps, cnt = moe_ops._Router.apply(logits, bias, k, cfg.norm_topk_prob, holder)
+            replay = getattr(blk, "router_replay", None)
+            if replay is not None and replay.mode == "replay":
+                w, idx = moe_ops.apply_router_replay(replay, blk.layer_idx, logits, bias, w, idx, cfg.norm_topk_prob)
+                return w, idx.long(), None
             aux = moe_ops._AuxLoss.apply(w, ps, cnt, t, k, float(aux_coef), holder) if aux_coef else None
+            moe_ops.apply_router_replay(replay, blk.layer_idx, logits, bias, w, idx, cfg.norm_topk_prob)
             return w, idx.long(), aux
         logits = x.float() @ blk.gate.float().t()
         z = logits + (bias.float() if bias is not None else 0.0)
@@ -119,6 +124,8 @@ class ExpertParallel:
         w, idx = torch.topk(p, k, dim=-1)
         if cfg.norm_topk_prob:
             w = w / w.sum(-1, keepdim=True)
+        w, idx = moe_ops.apply_router_replay(getattr(blk, "router_replay", None), blk.layer_idx, logits, bias, w, idx,
+                                             cfg.norm_topk_prob)
         aux = None
         if aux_coef:
             count = torch.zeros(p.shape[-1], device=x.device).index_add_(0, idx.reshape(-1),

@@ -34,6 +34,12 @@ class TextTrainer:
         if args.model.overrides:
             mcfg = mcfg.with_(**args.model.overrides)
         self.placemoe = PlaceMoERuntimeConfig.from_environment()
+        from ..parallel.hiermoe_state import configure_hiermoe
+
+        # fail fast on invalid MoE-parallel settings, before any model is built
+        self.hiermoe = configure_hiermoe(t.hiermoe, ep_size=world, ranks_per_node=int(os.environ.get(
+            "LOCAL_WORLD_SIZE", str(world))), activation_checkpointing_enabled=t.gradient_checkpointing,
+            has_artifact=bool(self.placemoe.initial_artifact))
         cfg = TrainConfig(
             model=args.model.preset, seq_len=args.data.max_seq_len, batch_per_rank=per_rank,
             micro_batch_size=min(t.micro_batch_size, per_rank), lr=t.lr, betas=tuple(t.betas), eps=t.eps,
@@ -48,6 +54,9 @@ class TextTrainer:
         self.trainer = Trainer(cfg, mcfg)
         self.data = SyntheticTokens(mcfg.vocab_size, per_rank, args.data.max_seq_len, seed=args.data.seed,
                                     rank=self.trainer.rank)
+        from ..placemoe.oracle import OracleCapture
+
+        self.oracle = OracleCapture(self.trainer.model)  # planner inputs on request (environment)
         self.recorder = None
         if t.hiermoe.capture_routes or t.hiermoe.route_capture_steps:
             from ..parallel.route_capture import RouteRecorder
@@ -82,9 +91,11 @@ class TextTrainer:
         for step in range(tr.global_step, t.max_steps):
             if self.recorder is not None:
                 self.recorder.enabled = step < max(t.hiermoe.route_capture_steps, 0) or t.hiermoe.capture_routes
+            self.oracle.before_step(step)
             loss = tr.train_step(next(self.data))
             if self.recorder is not None and self.recorder.enabled:
                 self.recorder.record_step(step)
+            self.oracle.after_step(step)
             if tr.rank == 0 and (step % max(1, t.log_interval) == 0 or step == t.max_steps - 1):
                 gn = tr.metrics.get("grad_norm")
                 gn = float(gn) if gn is not None else float("nan")
