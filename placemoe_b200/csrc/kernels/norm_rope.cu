@@ -1,8 +1,9 @@
 // RMSNorm and the fused QK-norm + RoPE kernels (sm_100a).
 //
-// rmsnorm_fwd/bwd: one warp per row, 16-byte vector accesses, fp32 math;
-//   backward accumulates d(weight) per CTA in registers/shared memory and
-//   adds it to the fp32 output with one atomic per element per CTA.
+// rmsnorm_fwd/bwd: persistent warp-per-row kernels that stream rows through a
+//   shared-memory ring (cp.async.bulk + mbarrier), fp32 math; the backward
+//   keeps d(weight) partials in registers and adds them to the fp32 output
+//   with one atomic per element per CTA.
 // qkv_rope_fwd/bwd: CTAs stride over tokens and split the fused QKV projection into
 //   q/k/v, applies RMSNorm to q and k (groups of `q_group`/`k_group`
 //   elements: head_dim for Qwen3-MoE per-head norms, the full width for
@@ -26,109 +27,198 @@ __device__ __forceinline__ float ldw(const WT* w, int i) { return static_cast<fl
 template <>
 __device__ __forceinline__ float ldw<__nv_bfloat16>(const __nv_bfloat16* w, int i) { return __bfloat162float(w[i]); }
 
-// H is a multiple of 256; each lane owns H/256 vectors of 8 elements.
-template <int VPL, typename WT>
-__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
-                                                          __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
-                                                          int rows, int H, float eps) {
-  const int warp = (blockIdx.x * 8) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)warp * H);
-  float v[VPL][8];
-  float ss = 0.f;
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    uint4 q = xr[i * 32 + lane];
-    uint32_t u[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      v[i][2 * j] = bf16_lo(u[j]);
-      v[i][2 * j + 1] = bf16_hi(u[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
-  }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / H + eps);
-  if (lane == 0) rstd[warp] = r;
-  uint4* yr = reinterpret_cast<uint4*>(y + (size_t)warp * H);
-#pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c0 = (i * 32 + lane) * 8;
-    uint32_t o[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      o[j] = pack_bf16(v[i][2 * j] * r * ldw(w, c0 + 2 * j), v[i][2 * j + 1] * r * ldw(w, c0 + 2 * j + 1));
-    yr[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
-  }
-}
-
-template <int VPL, typename WT>
-__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
-                                                          const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
-                                                          const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                                          float* __restrict__ dw, int rows, int H) {
-  const int lane = threadIdx.x & 31;
-  const int wid = threadIdx.x >> 5;
-  float dwacc[VPL][8];
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) dwacc[i][j] = 0.f;
-  for (int row = blockIdx.x * 8 + wid; row < rows; row += gridDim.x * 8) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * H);
-    const uint4* gr = reinterpret_cast<const uint4*>(dy + (size_t)row * H);
-    const float r = rstd[row];
-    float xv[VPL][8], gw[VPL][8];
-    float dot = 0.f;
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      uint4 qx = xr[i * 32 + lane], qg = gr[i * 32 + lane];
-      uint32_t ux[4] = {qx.x, qx.y, qx.z, qx.w}, ug[4] = {qg.x, qg.y, qg.z, qg.w};
-      const int c0 = (i * 32 + lane) * 8;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xv[i][2 * j] = bf16_lo(ux[j]);
-        xv[i][2 * j + 1] = bf16_hi(ux[j]);
-        const float g0 = bf16_lo(ug[j]), g1 = bf16_hi(ug[j]);
-        dwacc[i][2 * j] += g0 * xv[i][2 * j] * r;
-        dwacc[i][2 * j + 1] += g1 * xv[i][2 * j + 1] * r;
-        gw[i][2 * j] = g0 * ldw(w, c0 + 2 * j);
-        gw[i][2 * j + 1] = g1 * ldw(w, c0 + 2 * j + 1);
-      }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) dot += gw[i][j] * xv[i][j];
-    }
-    dot = warp_sum(dot);
-    const float c = dot * r * r * r / H;
-    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
-#pragma unroll
-    for (int i = 0; i < VPL; ++i) {
-      uint32_t o[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        o[j] = pack_bf16(r * gw[i][2 * j] - c * xv[i][2 * j], r * gw[i][2 * j + 1] - c * xv[i][2 * j + 1]);
-      dr[i * 32 + lane] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-  }
-  // reduce d(weight) over the 8 warps of the CTA, then one atomic per element
-  extern __shared__ float sdw[];  // [H]
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
-  __syncthreads();
-#pragma unroll
-  for (int i = 0; i < VPL; ++i)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) atomicAdd(&sdw[(i * 32 + lane) * 8 + j], dwacc[i][j]);
-  __syncthreads();
-  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
-}
+// RMSNorm rows are streamed through shared memory: every warp owns rows
+// gw, gw + NW, ... (NW = warps in the grid) and its lane 0 keeps up to S of
+// them in flight with cp.async.bulk copies into a per-warp ring of stages,
+// one mbarrier per stage.  Bytes in flight therefore live in shared memory,
+// not registers, which is what a bandwidth-bound row op needs to cover HBM
+// latency.  Lane l owns the 16-byte chunks l, l + 32, ... of a row (VPL of
+// them), so a lane's d(weight) partials always belong to the same columns.
+constexpr int kRowWarps = 8;
+constexpr int kRowMaxStages = 4;
+constexpr int kRowSmemBudget = 220 * 1024;
+constexpr int kRowBarBytes = kRowWarps * kRowMaxStages * 8;
 
 static int sm_count() {
   int dev, n;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   return n;
+}
+
+// Issue the bulk copies of `nt` bf16 rows (same row index, `nt` tensors) into stage s.
+template <int NT>
+__device__ __forceinline__ void row_issue(uint8_t* stage, uint64_t* bar, const __nv_bfloat16* const (&src)[NT],
+                                          size_t row, int H) {
+  const uint32_t rb = (uint32_t)H * 2;
+  mbar_arrive_expect_tx(bar, rb * NT);
+#pragma unroll
+  for (int t = 0; t < NT; ++t) bulk_load(stage + t * rb, src[t] + row * H, rb, bar);
+}
+
+template <int VPL, typename WT>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
+                                                          __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                          int rows, int H, float eps, int S) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NW = gridDim.x * kRowWarps, gw = blockIdx.x * kRowWarps + warp;
+  const uint32_t rb = (uint32_t)H * 2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kRowMaxStages;
+  float* ws = reinterpret_cast<float*>(smem + kRowBarBytes);
+  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 4 + (size_t)warp * S * rb;
+  const __nv_bfloat16* src[1] = {x};
+  for (int i = threadIdx.x; i < H; i += blockDim.x) ws[i] = ldw(w, i);
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    for (int s = 0; s < S && gw + s * NW < rows; ++s) row_issue<1>(ring + s * rb, &bars[s], src, gw + s * NW, H);
+  }
+  __syncthreads();
+  for (int k = 0;; ++k) {
+    const int row = gw + k * NW;
+    if (row >= rows) break;
+    const int s = k % S;
+    // warp-uniform exit when the wait runs out of budget (error recorded)
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (k / S) & 1))) break;
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * rb);
+    uint4 q[VPL];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      q[i] = xs[i * 32 + lane];
+      const uint32_t u[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = bf16_lo(u[j]), b = bf16_hi(u[j]);
+        ss += a * a + b * b;
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && row + S * NW < rows) row_issue<1>(ring + s * rb, &bars[s], src, row + S * NW, H);
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss / H + eps);
+    if (lane == 0) rstd[row] = r;
+    uint4* yr = reinterpret_cast<uint4*>(y + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = i * 32 + lane;
+      const float4 w0 = reinterpret_cast<const float4*>(ws)[2 * c], w1 = reinterpret_cast<const float4*>(ws)[2 * c + 1];
+      const uint32_t u[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
+      uint4 o;
+      o.x = pack_bf16(bf16_lo(u[0]) * r * w0.x, bf16_hi(u[0]) * r * w0.y);
+      o.y = pack_bf16(bf16_lo(u[1]) * r * w0.z, bf16_hi(u[1]) * r * w0.w);
+      o.z = pack_bf16(bf16_lo(u[2]) * r * w1.x, bf16_hi(u[2]) * r * w1.y);
+      o.w = pack_bf16(bf16_lo(u[3]) * r * w1.z, bf16_hi(u[3]) * r * w1.w);
+      yr[c] = o;
+    }
+  }
+}
+
+// Backward: dx = r*(dy*w) - (sum(dy*w*x) * r^3 / H) * x and dw += dy*x*r per row.
+// Stage s of a warp holds [x row | dy row]; d(weight) partials stay in
+// registers over all rows of the warp, are summed over the CTA's warps in
+// shared memory and added to the fp32 output with one atomic per column per CTA.
+template <int VPL, typename WT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
+                                                          const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
+                                                          const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
+                                                          float* __restrict__ dw, int rows, int H, int S) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NW = gridDim.x * kRowWarps, gw = blockIdx.x * kRowWarps + warp;
+  const uint32_t rb = (uint32_t)H * 2;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kRowMaxStages;
+  float* ws = reinterpret_cast<float*>(smem + kRowBarBytes);
+  float* sdw = ws + H;
+  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 8 + (size_t)warp * S * 2 * rb;
+  const __nv_bfloat16* src[2] = {x, dy};
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    ws[i] = ldw(w, i);
+    sdw[i] = 0.f;
+  }
+  if (lane == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    for (int s = 0; s < S && gw + s * NW < rows; ++s) row_issue<2>(ring + s * 2 * rb, &bars[s], src, gw + s * NW, H);
+  }
+  __syncthreads();
+  constexpr bool kKeep = VPL <= 8;
+  constexpr int kAcc = kKeep ? VPL : 1;
+  float dwacc[kAcc][8];
+#pragma unroll
+  for (int i = 0; i < kAcc; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
+  for (int k = 0;; ++k) {
+    const int row = gw + k * NW;
+    if (row >= rows) break;
+    const int s = k % S;
+    const float r = rstd[row];
+    // warp-uniform exit when the wait runs out of budget (error recorded)
+    if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (k / S) & 1))) break;
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * 2 * rb);
+    const uint4* gs = reinterpret_cast<const uint4*>(ring + s * 2 * rb + rb);
+    uint4 qx[VPL], qg[VPL];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = i * 32 + lane;
+      qx[i] = xs[c];
+      qg[i] = gs[c];
+      const uint32_t ux[4] = {qx[i].x, qx[i].y, qx[i].z, qx[i].w}, ug[4] = {qg[i].x, qg[i].y, qg[i].z, qg[i].w};
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        const float x0 = bf16_lo(ux[e2]), x1 = bf16_hi(ux[e2]);
+        const float g0 = bf16_lo(ug[e2]), g1 = bf16_hi(ug[e2]);
+        const float2 wv = reinterpret_cast<const float2*>(ws)[4 * c + e2];
+        dot += g0 * wv.x * x0 + g1 * wv.y * x1;
+        if constexpr (kKeep) {
+          dwacc[i][2 * e2] += g0 * x0 * r;
+          dwacc[i][2 * e2 + 1] += g1 * x1 * r;
+        } else {  // wide rows: shared-memory accumulation keeps the registers for the row
+          atomicAdd(&sdw[8 * c + 2 * e2], g0 * x0 * r);
+          atomicAdd(&sdw[8 * c + 2 * e2 + 1], g1 * x1 * r);
+        }
+      }
+    }
+    if constexpr (kKeep) {
+      __syncwarp();
+      if (lane == 0 && row + S * NW < rows) row_issue<2>(ring + s * 2 * rb, &bars[s], src, row + S * NW, H);
+    }
+    dot = warp_sum(dot);
+    const float cf = dot * r * r * r / H;
+    uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = i * 32 + lane;
+      if constexpr (!kKeep) {  // wide rows: read the stage again instead of holding it in registers
+        qx[i] = xs[c];
+        qg[i] = gs[c];
+      }
+      const uint32_t ux[4] = {qx[i].x, qx[i].y, qx[i].z, qx[i].w}, ug[4] = {qg[i].x, qg[i].y, qg[i].z, qg[i].w};
+      uint32_t o[4];
+#pragma unroll
+      for (int e2 = 0; e2 < 4; ++e2) {
+        const float2 wv = reinterpret_cast<const float2*>(ws)[4 * c + e2];
+        o[e2] = pack_bf16(r * bf16_lo(ug[e2]) * wv.x - cf * bf16_lo(ux[e2]),
+                          r * bf16_hi(ug[e2]) * wv.y - cf * bf16_hi(ux[e2]));
+      }
+      dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    if constexpr (!kKeep) {
+      __syncwarp();
+      if (lane == 0 && row + S * NW < rows) row_issue<2>(ring + s * 2 * rb, &bars[s], src, row + S * NW, H);
+    }
+  }
+  if constexpr (kKeep) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) atomicAdd(&sdw[8 * (i * 32 + lane) + e], dwacc[i][e]);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
 }
 
 #define PM_VPL_DISPATCH(H, ...)                                       \
@@ -141,55 +231,87 @@ static int sm_count() {
     default: TORCH_CHECK(false, "rmsnorm: hidden size must be 256 * {1,2,4,8,16}"); \
   }
 
+// Stages per warp and the CTA's shared-memory bytes for `nt` streamed tensors.
+static void row_stream_shape(int H, int nt, int fixed_floats, int* S, int* smem) {
+  const int stage = nt * H * 2;
+  const int fixed = kRowBarBytes + fixed_floats * H * 4;
+  const int s = (kRowSmemBudget - fixed) / (kRowWarps * stage);
+  TORCH_CHECK(s >= 1, "rmsnorm: hidden size too large for the shared-memory ring");
+  *S = std::min(s, kRowMaxStages);
+  *smem = fixed + kRowWarps * *S * stage;
+}
+
+static void check_row_ptr(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
   const int H = (int)x.size(-1);
   const int rows = (int)(x.numel() / H);
   TORCH_CHECK(w.numel() == H && w.is_contiguous(), "weight size");
   PM_CHECK_CUDA(w);
+  check_row_ptr(x, "x");
   c10::cuda::CUDAGuard guard(x.device());
   auto y = torch::empty_like(x);
   auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
   if (rows == 0) return {y, rstd};
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int grid = (rows + 7) / 8;
+  int S, smem;
+  row_stream_shape(H, 1, 1, &S, &smem);
+  const int grid = std::min(sm_count(), (rows + kRowWarps - 1) / kRowWarps);
+#define PM_RMS_FWD(WT_, WPTR)                                                                                      \
+  PM_VPL_DISPATCH(H, {                                                                                             \
+    auto kern = rmsnorm_fwd_kernel<VPL, WT_>;                                                                      \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));                 \
+    kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)x.data_ptr(), WPTR, (__nv_bfloat16*)y.data_ptr(),      \
+                                      rstd.data_ptr<float>(), rows, H, (float)eps, S);                             \
+  })
   if (w.scalar_type() == torch::kFloat32) {
-    PM_VPL_DISPATCH(H, rmsnorm_fwd_kernel<VPL, float><<<grid, 256, 0, stream>>>(
-        (const __nv_bfloat16*)x.data_ptr(), w.data_ptr<float>(), (__nv_bfloat16*)y.data_ptr(),
-        rstd.data_ptr<float>(), rows, H, (float)eps));
+    PM_RMS_FWD(float, w.data_ptr<float>());
   } else {
     TORCH_CHECK(w.scalar_type() == torch::kBFloat16, "weight must be fp32 or bf16");
-    PM_VPL_DISPATCH(H, rmsnorm_fwd_kernel<VPL, __nv_bfloat16><<<grid, 256, 0, stream>>>(
-        (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
-        rstd.data_ptr<float>(), rows, H, (float)eps));
+    PM_RMS_FWD(__nv_bfloat16, (const __nv_bfloat16*)w.data_ptr());
   }
+#undef PM_RMS_FWD
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {y, rstd};
 }
 
 // returns dx (bf16) and accumulates into dw (fp32, [H])
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw) {
-  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == torch::kBFloat16, "dy/x contiguous bf16");
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == torch::kBFloat16 &&
+                  x.scalar_type() == torch::kBFloat16, "dy/x contiguous bf16");
   TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous(), "dw must be fp32");
   PM_CHECK_CUDA(dy); PM_CHECK_CUDA(x); PM_CHECK_CUDA(w); PM_CHECK_CUDA(rstd); PM_CHECK_CUDA(dw);
   const int H = (int)x.size(-1);
   const int rows = (int)(x.numel() / H);
+  TORCH_CHECK(dy.numel() == x.numel() && w.numel() == H && dw.numel() == H && rstd.numel() == rows,
+              "rmsnorm_bwd: shapes");
+  check_row_ptr(x, "x");
+  check_row_ptr(dy, "dy");
   c10::cuda::CUDAGuard guard(x.device());
   auto dx = torch::empty_like(x);
   if (rows == 0) return dx;
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int grid = std::min((rows + 7) / 8, sm_count() * 4);
-  const size_t smem = (size_t)H * sizeof(float);
+  int S, smem;
+  row_stream_shape(H, 2, 2, &S, &smem);
+  const int grid = std::min(sm_count(), (rows + kRowWarps - 1) / kRowWarps);
+#define PM_RMS_BWD(WT_, WPTR)                                                                                  \
+  PM_VPL_DISPATCH(H, {                                                                                         \
+    auto kern = rmsnorm_bwd_kernel<VPL, WT_>;                                                                  \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));             \
+    kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), \
+                                      WPTR, rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(),             \
+                                      dw.data_ptr<float>(), rows, H, S);                                       \
+  })
   if (w.scalar_type() == torch::kFloat32) {
-    PM_VPL_DISPATCH(H, rmsnorm_bwd_kernel<VPL, float><<<grid, 256, smem, stream>>>(
-        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), w.data_ptr<float>(),
-        rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(), dw.data_ptr<float>(), rows, H));
+    PM_RMS_BWD(float, w.data_ptr<float>());
   } else {
-    PM_VPL_DISPATCH(H, rmsnorm_bwd_kernel<VPL, __nv_bfloat16><<<grid, 256, smem, stream>>>(
-        (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(),
-        (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(),
-        dw.data_ptr<float>(), rows, H));
+    TORCH_CHECK(w.scalar_type() == torch::kBFloat16, "weight must be fp32 or bf16");
+    PM_RMS_BWD(__nv_bfloat16, (const __nv_bfloat16*)w.data_ptr());
   }
+#undef PM_RMS_BWD
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;
 }
@@ -221,7 +343,7 @@ struct QkvArgs {
   float* dkw;
 };
 
-// One block of 256 threads per token (grid-stride).  Thread j owns 16-byte
+// One block of 256 threads per token (persistent grid).  Thread j owns 16-byte
 // chunks j, j + 256, ... of the q region and of the k region (8 consecutive
 // elements each), so every global access is a 16-byte vector.  A head spans
 // D / 8 consecutive threads; the RoPE partner of a chunk (offset +-D/2 in its
@@ -308,8 +430,32 @@ PM_DEVICE void qkv_fwd_chunk(const float (&x)[8], float ssq, int c, int nch, int
   if (c < nch) store8(dst + 8 * c, out);
 }
 
+// Token ring: CTA b handles tokens b, b + G, ... (G = grid size); thread 0
+// keeps S of them in flight with cp.async.bulk copies into shared-memory
+// stages (one mbarrier each) and refills a stage once every thread of the
+// CTA has read it.  A wait that runs out of budget ends the CTA uniformly
+// (__syncthreads_or) after recording the error.
+constexpr int kQkvBarBytes = 128;
+
+PM_DEVICE void qkv_issue_fwd(const QkvArgs& a, uint8_t* stage, uint64_t* bar, int t, int width) {
+  const uint32_t rb = (uint32_t)width * 2;
+  mbar_arrive_expect_tx(bar, rb);
+  bulk_load(stage, a.qkv + (size_t)t * width, rb, bar);
+}
+
+// Backward stage: [q|k inputs (nq + nk)][dq (nq)][dk (nk)][dv (nk)], bf16.
+PM_DEVICE void qkv_issue_bwd(const QkvArgs& a, uint8_t* stage, uint64_t* bar, int t, int nq, int nk) {
+  const int width = nq + 2 * nk;
+  mbar_arrive_expect_tx(bar, (uint32_t)(2 * nq + 3 * nk) * 2);
+  bulk_load(stage, a.qkv + (size_t)t * width, (uint32_t)(nq + nk) * 2, bar);
+  bulk_load(stage + (size_t)(nq + nk) * 2, a.dq + (size_t)t * nq, (uint32_t)nq * 2, bar);
+  bulk_load(stage + (size_t)(2 * nq + nk) * 2, a.dk + (size_t)t * nk, (uint32_t)nk * 2, bar);
+  bulk_load(stage + (size_t)(2 * nq + 2 * nk) * 2, a.dv + (size_t)t * nk, (uint32_t)nk * 2, bar);
+}
+
 template <int D, int MQ, int MK>
-__global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
+__global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a, int S) {
+  extern __shared__ __align__(128) uint8_t qsm[];
   __shared__ float red[2][kQkvThreads / 32];
   const int j = threadIdx.x, lane = j & 31;
   const int nq = a.Hq * D, nk = a.Hkv * D;
@@ -319,15 +465,33 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
   const bool first_half = o < D / 2;
   const int ai = o % (D / 2);  // rotation-angle index of the chunk's first element
   const bool full_q = a.q_group > D, full_k = a.k_group > D;
-  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-    const __nv_bfloat16* row = a.qkv + (size_t)t * width;
-    int p = a.pos[t];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qsm);
+  uint8_t* ring = qsm + kQkvBarBytes;
+  const size_t stage_bytes = (size_t)width * 2;
+  const int G = gridDim.x;
+  if (j == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+    for (int s = 0; s < S && (int)blockIdx.x + s * G < a.T; ++s)
+      qkv_issue_fwd(a, ring + s * stage_bytes, &bar[s], blockIdx.x + s * G, width);
+  }
+  __syncthreads();
+  int p_next = blockIdx.x < a.T ? a.pos[blockIdx.x] : 0;
+  for (int it = 0;; ++it) {
+    const int t = blockIdx.x + it * G;
+    if (t >= a.T) break;
+    const int s = it % S;
+    const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(ring + s * stage_bytes);
+    int p = p_next;
+    if (t + (int)gridDim.x < a.T) p_next = a.pos[t + gridDim.x];  // next token's position in flight
     if (p < 0 || p >= a.rope_len) {
       if (j == 0) set_error(kErrBounds);
       p = 0;
     }
     float cs[8], sn[8];
     load_rope(a.rope + (size_t)p * (D / 2) + ai, cs, sn);
+    const bool ok = mbar_wait(&bar[s], (it / S) & 1);
+    if (__syncthreads_or(!ok)) break;
     float xq[MQ][8], xk[MK][8], sq[MQ], sk[MK];
     float tq = 0.f, tk = 0.f;
 #pragma unroll
@@ -356,6 +520,9 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
       for (int e = 0; e < 8; ++e) sk[i] += xk[i][e] * xk[i][e];
       tk += sk[i];
     }
+    for (int c = j; c < nkc; c += kQkvThreads)
+      *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + 8 * c) = *reinterpret_cast<const uint4*>(row + nq + nk + 8 * c);
+    // every read of stage s is done once all threads passed the next barrier
     float rq_full = 1.f, rk_full = 1.f;
     if (full_q || full_k) {
       const float2 tot = block_sum2(tq, tk, red);
@@ -365,7 +532,10 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
         if (full_q) a.rq[t] = rq_full;
         if (full_k) a.rk[t] = rk_full;
       }
+    } else {
+      __syncthreads();
     }
+    if (j == 0 && t + S * G < a.T) qkv_issue_fwd(a, ring + s * stage_bytes, &bar[s], t + S * G, width);
 #pragma unroll
     for (int i = 0; i < MQ; ++i)
       qkv_fwd_chunk<D>(xq[i], sq[i], j + kQkvThreads * i, nqc, a.q_group, a.qw, rq_full, a.rq, a.Hq, t,
@@ -374,8 +544,6 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_fwd_kernel(QkvArgs a) {
     for (int i = 0; i < MK; ++i)
       qkv_fwd_chunk<D>(xk[i], sk[i], j + kQkvThreads * i, nkc, a.k_group, a.kw, rk_full, a.rk, a.Hkv, t,
                        a.k + (size_t)t * nk, cs, sn, o, first_half, a.eps, lane);
-    for (int c = j; c < nkc; c += kQkvThreads)
-      *reinterpret_cast<uint4*>(a.v + (size_t)t * nk + 8 * c) = *reinterpret_cast<const uint4*>(row + nq + nk + 8 * c);
   }
 }
 
@@ -412,22 +580,14 @@ PM_DEVICE float qkv_bwd_load(const __nv_bfloat16* dsrc, const __nv_bfloat16* xsr
 // Backward, phase 2 of a chunk: input gradient through the norm, weight-gradient partials.
 template <int D>
 PM_DEVICE void qkv_bwd_store(const float (&x)[8], const float (&g)[8], float dot_part, float dot_full, int c, int nch,
-                             int G, const float* wt, const float* rsave, int H, int t, __nv_bfloat16* dst,
-                             float (&dwa)[8], int o) {
+                             int G, const float* wt, float r, __nv_bfloat16* dst, float (&dwa)[8], int o) {
   constexpr int HL = D / 8;
   float dx[8];
   if (!G) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) dx[e] = g[e];
   } else {
-    float r, dot;
-    if (G == D) {
-      dot = head_sum<HL>(dot_part);
-      r = c < nch ? rsave[(size_t)t * H + (8 * c) / D] : 0.f;
-    } else {
-      dot = dot_full;
-      r = rsave[t];
-    }
+    const float dot = G == D ? head_sum<HL>(dot_part) : dot_full;
     float w8[8];
     if (G == D) load8f(wt + o, w8);
     else if (c < nch) load8f(wt + 8 * c, w8);
@@ -478,7 +638,8 @@ PM_DEVICE void qkv_dw_flush(const float (&dwa)[M][8], int nch, int G, float* dw,
 }
 
 template <int D, int MQ, int MK>
-__global__ void __launch_bounds__(kQkvThreads) qkv_rope_bwd_kernel(QkvArgs a) {
+__global__ void __launch_bounds__(kQkvThreads) qkv_rope_bwd_kernel(QkvArgs a, int S) {
+  extern __shared__ __align__(128) uint8_t qsm[];
   constexpr int NW = kQkvThreads / 32;
   __shared__ float red[2][NW];
   __shared__ float sdw[2][NW][D];  // per-head norm weights: per-warp partials
@@ -498,46 +659,83 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_bwd_kernel(QkvArgs a) {
 #pragma unroll
     for (int i = 0; i < MK; ++i) dwk[i][e] = 0.f;
   }
-  for (int t = blockIdx.x; t < a.T; t += gridDim.x) {
-    const __nv_bfloat16* row = a.qkv + (size_t)t * width;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qsm);
+  uint8_t* ring = qsm + kQkvBarBytes;
+  const size_t stage_bytes = (size_t)(2 * nq + 3 * nk) * 2;
+  const int G = gridDim.x;
+  if (j == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(&bar[s], 1);
+    fence_barrier_init();
+    for (int s = 0; s < S && (int)blockIdx.x + s * G < a.T; ++s)
+      qkv_issue_bwd(a, ring + s * stage_bytes, &bar[s], blockIdx.x + s * G, nq, nk);
+  }
+  __syncthreads();
+  int p_next = blockIdx.x < a.T ? a.pos[blockIdx.x] : 0;
+  for (int it = 0;; ++it) {
+    const int t = blockIdx.x + it * G;
+    if (t >= a.T) break;
+    const int s = it % S;
+    const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(ring + s * stage_bytes);
+    const __nv_bfloat16* sdq = row + nq + nk;
+    const __nv_bfloat16* sdk = sdq + nq;
+    const __nv_bfloat16* sdv = sdk + nk;
     __nv_bfloat16* drow = a.dqkv + (size_t)t * width;
-    int p = a.pos[t];
+    int p = p_next;
+    if (t + (int)gridDim.x < a.T) p_next = a.pos[t + gridDim.x];  // next token's position in flight
     if (p < 0 || p >= a.rope_len) {
       if (j == 0) set_error(kErrBounds);
       p = 0;
     }
     float cs[8], sn[8];
     load_rope(a.rope + (size_t)p * (D / 2) + ai, cs, sn);
+    // saved inverse norms, loaded with the operands (not after the block reduction)
+    float rq_s[MQ], rk_s[MK];
+#pragma unroll
+    for (int i = 0; i < MQ; ++i) {
+      const int c = j + kQkvThreads * i;
+      rq_s[i] = !a.q_group ? 0.f : (a.q_group == D ? (c < nqc ? a.rq[(size_t)t * a.Hq + (8 * c) / D] : 0.f) : a.rq[t]);
+    }
+#pragma unroll
+    for (int i = 0; i < MK; ++i) {
+      const int c = j + kQkvThreads * i;
+      rk_s[i] = !a.k_group ? 0.f : (a.k_group == D ? (c < nkc ? a.rk[(size_t)t * a.Hkv + (8 * c) / D] : 0.f) : a.rk[t]);
+    }
+    const bool ok = mbar_wait(&bar[s], (it / S) & 1);
+    if (__syncthreads_or(!ok)) break;
     float xq[MQ][8], gq[MQ][8], xk[MK][8], gk[MK][8], dq_h[MQ], dk_h[MK];
     float pq = 0.f, pk = 0.f;
 #pragma unroll
     for (int i = 0; i < MQ; ++i) {
-      dq_h[i] = qkv_bwd_load<D>(a.dq + (size_t)t * nq, row, j + kQkvThreads * i, nqc, a.q_group, a.qw, xq[i], gq[i],
-                                cs, sn, o, first_half);
+      dq_h[i] = qkv_bwd_load<D>(sdq, row, j + kQkvThreads * i, nqc, a.q_group, a.qw, xq[i], gq[i], cs, sn, o,
+                                first_half);
       pq += dq_h[i];
     }
 #pragma unroll
     for (int i = 0; i < MK; ++i) {
-      dk_h[i] = qkv_bwd_load<D>(a.dk + (size_t)t * nk, row + nq, j + kQkvThreads * i, nkc, a.k_group, a.kw, xk[i],
-                                gk[i], cs, sn, o, first_half);
+      dk_h[i] = qkv_bwd_load<D>(sdk, row + nq, j + kQkvThreads * i, nkc, a.k_group, a.kw, xk[i], gk[i], cs, sn, o,
+                                first_half);
       pk += dk_h[i];
     }
+    for (int c = j; c < nkc; c += kQkvThreads)
+      *reinterpret_cast<uint4*>(drow + nq + nk + 8 * c) = *reinterpret_cast<const uint4*>(sdv + 8 * c);
+    // every read of stage s is done once all threads passed the next barrier
     float tq = 0.f, tk = 0.f;
     if (full_q || full_k) {
       const float2 tot = block_sum2(pq, pk, red);
       tq = tot.x;
       tk = tot.y;
+    } else {
+      __syncthreads();
     }
+    if (j == 0 && t + S * G < a.T) qkv_issue_bwd(a, ring + s * stage_bytes, &bar[s], t + S * G, nq, nk);
 #pragma unroll
     for (int i = 0; i < MQ; ++i)
-      qkv_bwd_store<D>(xq[i], gq[i], dq_h[i], tq, j + kQkvThreads * i, nqc, a.q_group, a.qw, a.rq, a.Hq, t, drow,
+      qkv_bwd_store<D>(xq[i], gq[i], dq_h[i], tq, j + kQkvThreads * i, nqc, a.q_group, a.qw, rq_s[i], drow,
                        dwq[i], o);
 #pragma unroll
     for (int i = 0; i < MK; ++i)
-      qkv_bwd_store<D>(xk[i], gk[i], dk_h[i], tk, j + kQkvThreads * i, nkc, a.k_group, a.kw, a.rk, a.Hkv, t,
-                       drow + nq, dwk[i], o);
-    for (int c = j; c < nkc; c += kQkvThreads)
-      *reinterpret_cast<uint4*>(drow + nq + nk + 8 * c) = *reinterpret_cast<const uint4*>(a.dv + (size_t)t * nk + 8 * c);
+      qkv_bwd_store<D>(xk[i], gk[i], dk_h[i], tk, j + kQkvThreads * i, nkc, a.k_group, a.kw, rk_s[i], drow + nq,
+                       dwk[i], o);
   }
   qkv_dw_flush<D, MQ>(dwq, nqc, a.q_group, a.dqw, sdw[0], o);
   qkv_dw_flush<D, MK>(dwk, nkc, a.k_group, a.dkw, sdw[1], o);
@@ -556,21 +754,38 @@ __global__ void __launch_bounds__(kQkvThreads) qkv_rope_bwd_kernel(QkvArgs a) {
   }
 }
 
-#define PM_QKV_DISPATCH(KERNEL, D_, MQ_, MK_, GRID, ARGS)                                              \
-  do {                                                                                                 \
-    auto st = at::cuda::getCurrentCUDAStream();                                                        \
-    if (D_ == 128) {                                                                                   \
-      if (MQ_ == 1 && MK_ == 1) KERNEL<128, 1, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);                 \
-      else if (MQ_ == 2 && MK_ == 1) KERNEL<128, 2, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);            \
-      else if (MQ_ <= 4 && MK_ == 1) KERNEL<128, 4, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);            \
-      else KERNEL<128, 4, 2><<<GRID, kQkvThreads, 0, st>>>(ARGS);                                      \
-    } else {                                                                                           \
-      if (MQ_ == 1 && MK_ == 1) KERNEL<64, 1, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);                  \
-      else if (MQ_ == 2 && MK_ == 1) KERNEL<64, 2, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);             \
-      else if (MQ_ <= 4 && MK_ == 1) KERNEL<64, 4, 1><<<GRID, kQkvThreads, 0, st>>>(ARGS);             \
-      else KERNEL<64, 4, 2><<<GRID, kQkvThreads, 0, st>>>(ARGS);                                       \
-    }                                                                                                  \
+// Stages per CTA, dynamic shared memory and resident CTAs per SM for a ring of `stage` bytes.
+template <typename K>
+static void qkv_launch(K kern, int T, int stage, const QkvArgs& a) {
+  int S = 3;
+  while (S > 1 && kQkvBarBytes + S * stage > 160 * 1024) --S;
+  const int smem = kQkvBarBytes + S * stage;
+  TORCH_CHECK(smem <= 200 * 1024, "qkv rope: token row too wide for the shared-memory ring");
+  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  int per_sm = 0;
+  C10_CUDA_CHECK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQkvThreads, smem));
+  const int grid = std::min(T, sm_count() * std::max(per_sm, 1));
+  kern<<<grid, kQkvThreads, smem, at::cuda::getCurrentCUDAStream()>>>(a, S);
+}
+
+#define PM_QKV_DISPATCH(KERNEL, D_, MQ_, MK_, T_, STAGE, ARGS)                                  \
+  do {                                                                                          \
+    if (D_ == 128) {                                                                            \
+      if (MQ_ == 1 && MK_ == 1) qkv_launch(KERNEL<128, 1, 1>, T_, STAGE, ARGS);                 \
+      else if (MQ_ == 2 && MK_ == 1) qkv_launch(KERNEL<128, 2, 1>, T_, STAGE, ARGS);            \
+      else if (MQ_ <= 4 && MK_ == 1) qkv_launch(KERNEL<128, 4, 1>, T_, STAGE, ARGS);            \
+      else qkv_launch(KERNEL<128, 4, 2>, T_, STAGE, ARGS);                                      \
+    } else {                                                                                    \
+      if (MQ_ == 1 && MK_ == 1) qkv_launch(KERNEL<64, 1, 1>, T_, STAGE, ARGS);                  \
+      else if (MQ_ == 2 && MK_ == 1) qkv_launch(KERNEL<64, 2, 1>, T_, STAGE, ARGS);             \
+      else if (MQ_ <= 4 && MK_ == 1) qkv_launch(KERNEL<64, 4, 1>, T_, STAGE, ARGS);             \
+      else qkv_launch(KERNEL<64, 4, 2>, T_, STAGE, ARGS);                                       \
+    }                                                                                           \
   } while (0)
+
+static void check_aligned16(const torch::Tensor& t, const char* name) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, name, " must be 16-byte aligned");
+}
 
 static void qkv_chunk_counts(int64_t Hq, int64_t Hkv, int64_t D, int& mq, int& mk) {
   const int64_t nqc = Hq * D / 8, nkc = Hkv * D / 8;
@@ -624,8 +839,8 @@ std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, to
   a.rq = rq.data_ptr<float>(); a.rk = rk.data_ptr<float>();
   int mq, mk;
   qkv_chunk_counts(Hq, Hkv, D, mq, mk);
-  const int grid = std::min(T, sm_count() * 8);
-  PM_QKV_DISPATCH(qkv_rope_fwd_kernel, D, mq, mk, grid, a);
+  check_aligned16(qkv, "qkv");
+  PM_QKV_DISPATCH(qkv_rope_fwd_kernel, D, mq, mk, T, (int)((Hq + 2 * Hkv) * D * 2), a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return {q, k, v, rq, rk};
 }
@@ -637,6 +852,9 @@ torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
                            c10::optional<torch::Tensor> dkw, int64_t Hq, int64_t Hkv, int64_t D, int64_t q_group,
                            int64_t k_group) {
   TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous(), "grads must be contiguous");
+  TORCH_CHECK(dq.scalar_type() == torch::kBFloat16 && dk.scalar_type() == torch::kBFloat16 &&
+                  dv.scalar_type() == torch::kBFloat16 && qkv.scalar_type() == torch::kBFloat16,
+              "qkv_rope_bwd: bf16 tensors");
   PM_CHECK_CUDA(dq); PM_CHECK_CUDA(dk); PM_CHECK_CUDA(dv); PM_CHECK_CUDA(qkv); PM_CHECK_CUDA(pos);
   PM_CHECK_CUDA(rq); PM_CHECK_CUDA(rk); PM_CHECK_CUDA_OPT(qw); PM_CHECK_CUDA_OPT(kw);
   PM_CHECK_CUDA_OPT(dqw); PM_CHECK_CUDA_OPT(dkw);
@@ -660,8 +878,13 @@ torch::Tensor qkv_rope_bwd(torch::Tensor dq, torch::Tensor dk, torch::Tensor dv,
   a.dkw = k_group ? dkw->data_ptr<float>() : nullptr;
   int mq, mk;
   qkv_chunk_counts(Hq, Hkv, D, mq, mk);
-  const int grid = std::min(T, sm_count() * 4);
-  PM_QKV_DISPATCH(qkv_rope_bwd_kernel, D, mq, mk, grid, a);
+  check_aligned16(qkv, "qkv");
+  check_aligned16(dq, "dq");
+  check_aligned16(dk, "dk");
+  check_aligned16(dv, "dv");
+  TORCH_CHECK(dq.numel() == (int64_t)T * Hq * D && dk.numel() == (int64_t)T * Hkv * D && dv.numel() == dk.numel(),
+              "qkv_rope_bwd: gradient shapes");
+  PM_QKV_DISPATCH(qkv_rope_bwd_kernel, D, mq, mk, T, (int)((2 * Hq + 3 * Hkv) * D * 2), a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dqkv;
 }

@@ -13,12 +13,16 @@ def rel(a, b):
     return ((a - b).abs().max() / (b.abs().max() + 1e-6)).item()
 
 
-def test_rmsnorm_fwd_bwd():
+# rows > 148 SMs x 8 warps x 4 stages exercise the reuse of every ring stage
+@pytest.mark.parametrize("rows,hidden,wdtype", [(1000, 2048, torch.float32), (20011, 2048, torch.float32),
+                                                (9000, 4096, torch.bfloat16), (5, 256, torch.float32),
+                                                (12000, 512, torch.float32)])
+def test_rmsnorm_fwd_bwd(rows, hidden, wdtype):
     from placemoe_b200.ops.norm import rmsnorm, rmsnorm_reference
 
     torch.manual_seed(0)
-    x = torch.randn(1000, 2048, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    w = (1 + 0.1 * torch.randn(2048, device="cuda")).requires_grad_()
+    x = torch.randn(rows, hidden, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda")).to(wdtype).requires_grad_()
     y = rmsnorm(x, w, 1e-6)
     g = torch.randn_like(y)
     y.backward(g)
@@ -31,13 +35,15 @@ def test_rmsnorm_fwd_bwd():
     assert rel(w.grad, wr.grad) < 1e-2
 
 
-@pytest.mark.parametrize("hq,hkv,d,mode", [(16, 16, 128, "full"), (32, 4, 128, "per_head"), (8, 2, 64, "per_head"),
-                                         (64, 32, 128, "per_head"), (24, 8, 64, "full")])
-def test_qkv_norm_rope(hq, hkv, d, mode):
+# t = 5000 gives every CTA of the persistent grid several tokens, so every ring stage is reused
+@pytest.mark.parametrize("hq,hkv,d,mode,t", [(16, 16, 128, "full", 512), (32, 4, 128, "per_head", 512),
+                                           (8, 2, 64, "per_head", 512), (64, 32, 128, "per_head", 512),
+                                           (24, 8, 64, "full", 512), (16, 16, 128, "full", 5000),
+                                           (32, 4, 128, "per_head", 5000)])
+def test_qkv_norm_rope(hq, hkv, d, mode, t):
     from placemoe_b200.ops.norm import qkv_norm_rope, rope_inv_freq
 
     torch.manual_seed(1)
-    t = 512
     width = (hq + 2 * hkv) * d
     qkv = torch.randn(t, width, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     qg, kg = (d, d) if mode == "per_head" else (hq * d, hkv * d)
