@@ -57,8 +57,13 @@ class TrainingArguments:
     output_dir: str = "output"
     global_batch_size: int = 8  # sequences per step over all ranks
     micro_batch_size: int = 2  # sequences per micro-batch per rank
+    optimizer: str = "adamw"  # "adamw" | "muon"
     lr: float = 3e-4
     lr_warmup_ratio: float = 0.0
+    lr_decay_style: str = "cosine"  # "constant" | "linear" | "cosine"
+    lr_min_ratio: float = 0.1
+    muon_lr: float = 0.02
+    muon_momentum: float = 0.95
     weight_decay: float = 0.1
     max_grad_norm: float = 1.0
     betas: tuple = (0.9, 0.95)

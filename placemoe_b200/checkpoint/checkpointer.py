@@ -60,31 +60,30 @@ def _owned_slots(blk):
 
 def _state_dicts(trainer, for_load: bool):
     """Model/optimizer state keyed by logical names; for loading, every local slot requests its expert."""
+    from ..optim import state_tensors
+
     model, opt = trainer.model, trainer.optimizer
     ms, os_ = {}, {}
     for name, p in model.named_parameters():
         if is_expert_param(name):
             continue
         ms[name] = p.data
-        st = opt.state.get(p)
-        if st:
-            os_[f"{name}.exp_avg"] = st["exp_avg"]
-            os_[f"{name}.exp_avg_sq"] = st["exp_avg_sq"]
+        for sk, t in state_tensors(opt, p):
+            os_[f"{name}.{sk}"] = t
     for blk in model.moe_blocks():
         pl = blk.placement
         pairs = ([(j, int(pl.local_logical[j])) for j in range(pl.slots_per_rank) if pl.local_logical[j] >= 0]
                  if for_load else _owned_slots(blk))
         for pname in ("gate_up_proj", "down_proj"):
             p = getattr(blk, pname)
-            st = opt.state.get(p)
+            sts = state_tensors(opt, p)
             for j, e in pairs:
                 key = _expert_key(blk.layer_key, e, pname)
                 if for_load and key in ms:  # second local copy of the same expert: filled after load
                     continue
                 ms[key] = p.data[j]
-                if st:
-                    os_[f"{key}.exp_avg"] = st["exp_avg"][j]
-                    os_[f"{key}.exp_avg_sq"] = st["exp_avg_sq"][j]
+                for sk, t in sts:
+                    os_[f"{key}.{sk}"] = t[j]
     return ms, os_
 
 
@@ -133,6 +132,8 @@ def placement_digest(trainer) -> int:
 
 def load_checkpoint(trainer, path: str, *, restore_placement: bool = True) -> dict:
     """Restore model + optimizer (+ placement when the topology matches) from ``global_step_N``."""
+    from ..optim import state_tensors
+
     if os.path.basename(os.path.normpath(path)).startswith("global_step_") is False:
         steps = sorted(int(d.split("_")[-1]) for d in os.listdir(path) if d.startswith("global_step_"))
         if not steps:
@@ -176,10 +177,8 @@ def load_checkpoint(trainer, path: str, *, restore_placement: bool = True) -> di
                 for pname in ("gate_up_proj", "down_proj"):
                     p = getattr(blk, pname)
                     p.data[j].copy_(p.data[first[e]])
-                    st = trainer.optimizer.state.get(p)
-                    if st:
-                        st["exp_avg"][j].copy_(st["exp_avg"][first[e]])
-                        st["exp_avg_sq"][j].copy_(st["exp_avg_sq"][first[e]])
+                    for _, t in state_tensors(trainer.optimizer, p):
+                        t[j].copy_(t[first[e]])
             else:
                 first[e] = j
     with torch.no_grad():
@@ -189,7 +188,7 @@ def load_checkpoint(trainer, path: str, *, restore_placement: bool = True) -> di
     for st in trainer.optimizer.state.values():
         st["step"] = step
     trainer.global_step = int(extra["global_step"])
-    trainer.optimizer._tables.clear()
+    trainer.optimizer.reset_tables()
     return extra
 
 

@@ -36,6 +36,10 @@ class FusedAdamW(torch.optim.Optimizer):
         self._tables: dict = {}
         self.grad_scale: torch.Tensor | None = None  # optional device scalar (clip coefficient)
 
+    def reset_tables(self) -> None:
+        """Drop the cached device tables (parameters or states were re-bound)."""
+        self._tables.clear()
+
     def _state(self, p):
         st = self.state[p]
         if not st:

@@ -216,7 +216,7 @@ class HotUpdateManager:
                     continue
                 moved += migrate_layer(self.trainer, blk, plan, group=self.group)
             self.trainer._norm_table = None
-        self.trainer.optimizer._tables.clear()
+        self.trainer.optimizer.reset_tables()
         if dist.is_initialized():
             dist.barrier(group=self.group)
         self.events.append({"event": "applied", "kind": kind.value, "step": step, "planner_ms": planner_ms,

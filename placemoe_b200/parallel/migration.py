@@ -56,13 +56,13 @@ def plan_transfers(old_layout: np.ndarray, old_owners: np.ndarray, new_layout: n
 
 
 def _slot_state(blk, opt, j: int) -> list[torch.Tensor]:
+    """Parameter and optimizer-state rows of local slot j (AdamW moments or Muon momentum)."""
+    from ..optim import state_tensors
+
     ts = []
     for p in (blk.gate_up_proj, blk.down_proj):
         ts.append(p.data[j])
-        st = opt.state.get(p)
-        if st:
-            ts.append(st["exp_avg"][j])
-            ts.append(st["exp_avg_sq"][j])
+        ts.extend(t[j] for _, t in state_tensors(opt, p))
     return ts
 
 

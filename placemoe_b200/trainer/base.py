@@ -20,7 +20,6 @@ Reference parity: veomni/trainer/base.py:239-331 (_setup), :452-535, :695-727
 
 from __future__ import annotations
 
-import math
 import os
 import time
 from dataclasses import dataclass, field
@@ -32,7 +31,7 @@ from ..models.config import MoEModelConfig, get_preset
 from ..models.moe_decoder import build_model
 from ..ops import moe as moe_ops
 from ..ops import mp as mp_ops
-from ..ops.optim import FusedAdamW
+from ..optim import build_lr_scheduler, build_optimizer
 from ..parallel.p2p_ep import EPCapacityExceeded
 from ..parallel.data_parallel import (expert_init_from_full, expert_topology, parallelize_model,
                                       redundant_slot_weights, sync_replica_gradients)
@@ -53,6 +52,11 @@ class TrainConfig:
     max_grad_norm: float = 1.0
     warmup_steps: int = 0
     total_steps: int = 100
+    optimizer: str = "adamw"  # "adamw" | "muon" (Muon for hidden matrices, AdamW for the rest)
+    lr_scheduler: str = "cosine"  # "constant" | "linear" | "cosine" after linear warmup
+    min_lr_ratio: float = 0.1
+    muon_lr: float = 0.02
+    muon_momentum: float = 0.95
     seed: int = 0
     redundant_slots_per_rank: int = 0
     placemoe_artifact: str = ""  # schema-v2 artifact loaded at startup
@@ -107,8 +111,11 @@ class Trainer:
         self.model.train()
         self.pstate = parallelize_model(self.model, plans=plans, topology=topology, device=self.device,
                                         capture_routes=cfg.capture_routes, transport=cfg.ep_transport)
-        self.optimizer = FusedAdamW(self.model.parameters(), lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
-                                    weight_decay=cfg.weight_decay)
+        self.optimizer = build_optimizer(self.model, cfg.optimizer, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                         weight_decay=cfg.weight_decay, muon_lr=cfg.muon_lr,
+                                         muon_momentum=cfg.muon_momentum)
+        self.lr_schedule = build_lr_scheduler(cfg.lr_scheduler, cfg.lr, cfg.warmup_steps, cfg.total_steps,
+                                              cfg.min_lr_ratio)
         # peer-memory exchange for replica gradients and migration (CUDA, peer-memory EP transport)
         self.peer_exchange = None
         self.replica_sync = None
@@ -126,11 +133,7 @@ class Trainer:
 
     # ------------------------------------------------------------------ utils
     def lr_at(self, step: int) -> float:
-        c = self.cfg
-        if c.warmup_steps and step < c.warmup_steps:
-            return c.lr * (step + 1) / c.warmup_steps
-        prog = min(1.0, (step - c.warmup_steps) / max(1, c.total_steps - c.warmup_steps))
-        return c.lr * (0.1 + 0.9 * 0.5 * (1 + math.cos(math.pi * prog)))
+        return self.lr_schedule(step)
 
     def _grad_sq_norm(self) -> torch.Tensor:
         """Squared global grad norm (device scalar); redundant expert copies are excluded."""
@@ -253,8 +256,10 @@ class Trainer:
                     for p in self.model.parameters():
                         if p.grad is not None:
                             p.grad.mul_(coef)
+        mult = self.lr_schedule.multiplier(self.global_step)
         for g in self.optimizer.param_groups:
-            g["lr"] = self.lr_at(self.global_step)
+            g.setdefault("initial_lr", g["lr"])
+            g["lr"] = g["initial_lr"] * mult  # each group keeps its own base rate (Muon vs AdamW)
         self.optimizer.step()
         self.zero_grad()
 

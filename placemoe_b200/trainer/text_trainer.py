@@ -43,7 +43,9 @@ class TextTrainer:
         cfg = TrainConfig(
             model=args.model.preset, seq_len=args.data.max_seq_len, batch_per_rank=per_rank,
             micro_batch_size=min(t.micro_batch_size, per_rank), lr=t.lr, betas=tuple(t.betas), eps=t.eps,
-            weight_decay=t.weight_decay, max_grad_norm=t.max_grad_norm,
+            weight_decay=t.weight_decay, max_grad_norm=t.max_grad_norm, optimizer=t.optimizer,
+            lr_scheduler=t.lr_decay_style, min_lr_ratio=t.lr_min_ratio, muon_lr=t.muon_lr,
+            muon_momentum=t.muon_momentum,
             warmup_steps=int(t.lr_warmup_ratio * t.max_steps), total_steps=t.max_steps, seed=t.seed,
             redundant_slots_per_rank=t.hiermoe.redundant_slot_increment_per_device,
             placemoe_artifact=self.placemoe.initial_artifact, capture_routes=t.hiermoe.capture_routes,

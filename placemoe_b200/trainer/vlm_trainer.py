@@ -54,7 +54,7 @@ class VLMTrainer(TextTrainer):
         self.vision.to(tr.device)
         tr.optimizer.add_param_group({"params": list(self.vision.parameters()), **{
             k: v for k, v in tr.optimizer.defaults.items()}})
-        tr.optimizer._tables.clear()
+        tr.optimizer.reset_tables()
         g = torch.Generator().manual_seed(1234 + tr.rank)
         self._pix = lambda b: torch.randn(b, self.n_img, 14 * 14 * 3, generator=g)
         model = tr.model
