@@ -203,11 +203,12 @@ def _hf_names(cfg, li: int):
         "q_norm": f"{p}.self_attn.q_norm.weight", "k_norm": f"{p}.self_attn.k_norm.weight",
         "gate": f"{p}.mlp.gate.weight",
         "expert": f"{p}.mlp.experts.{{e}}.{{w}}.weight",
+        "dense": f"{p}.mlp.{{w}}.weight",
     }
 
 
 def export_hf(trainer, out_dir: str) -> str | None:
-    """HuggingFace safetensors export with logical experts (rank 0 writes)."""
+    """HuggingFace safetensors export with logical experts, or the dense MLP (rank 0 writes)."""
     from safetensors.torch import save_file
 
     rank, world = _world()
@@ -218,10 +219,16 @@ def export_hf(trainer, out_dir: str) -> str | None:
         n = _hf_names(cfg, li)
         blk = layer.mlp
         owned = {}
-        for j, e in _owned_slots(blk):
+        dense = cfg.is_dense
+        if dense and rank == 0:
+            gu = blk.w_gate_up.data[0].to("cpu", torch.bfloat16)
+            tensors[n["dense"].format(w="gate_proj")] = gu[: cfg.intermediate_size].clone()
+            tensors[n["dense"].format(w="up_proj")] = gu[cfg.intermediate_size:].clone()
+            tensors[n["dense"].format(w="down_proj")] = blk.w_down.data[0].to("cpu", torch.bfloat16)
+        for j, e in ([] if dense else _owned_slots(blk)):
             gu = blk.gate_up_proj.data[j].to("cpu", torch.bfloat16)
             owned[e] = (gu[:inter].clone(), gu[inter:].clone(), blk.down_proj.data[j].to("cpu", torch.bfloat16))
-        if world > 1:
+        if world > 1 and not dense:
             gathered = [None] * world
             dist.all_gather_object(gathered, owned)
             owned = {k: v for d in gathered for k, v in d.items()}
@@ -242,7 +249,8 @@ def export_hf(trainer, out_dir: str) -> str | None:
             tensors[n["k_norm"]] = at.k_norm.data.to("cpu", torch.bfloat16)
         tensors[n["input_layernorm"]] = layer.input_layernorm.weight.data.to("cpu", torch.bfloat16)
         tensors[n["post_attention_layernorm"]] = layer.post_attention_layernorm.weight.data.to("cpu", torch.bfloat16)
-        tensors[n["gate"]] = blk.gate.data.to("cpu", torch.bfloat16)
+        if not dense:
+            tensors[n["gate"]] = blk.gate.data.to("cpu", torch.bfloat16)
     if rank != 0:
         return None
     tensors["model.embed_tokens.weight"] = model.embed_tokens.data.to("cpu", torch.bfloat16)
@@ -251,13 +259,14 @@ def export_hf(trainer, out_dir: str) -> str | None:
         tensors["lm_head.weight"] = model.lm_head.data.to("cpu", torch.bfloat16)
     os.makedirs(out_dir, exist_ok=True)
     save_file(tensors, os.path.join(out_dir, "model.safetensors"), metadata={"format": "pt"})
+    arch = {"olmoe": "OlmoeForCausalLM", "qwen3": "Qwen3ForCausalLM", "llama": "LlamaForCausalLM"}
     hf_cfg = {
-        "model_type": cfg.model_type, "architectures": ["OlmoeForCausalLM" if cfg.model_type == "olmoe"
-                                                        else "Qwen3MoeForCausalLM"],
+        "model_type": cfg.model_type, "architectures": [arch.get(cfg.model_type, "Qwen3MoeForCausalLM")],
         "vocab_size": cfg.vocab_size, "hidden_size": cfg.hidden_size, "num_hidden_layers": cfg.num_hidden_layers,
         "num_attention_heads": cfg.num_attention_heads, "num_key_value_heads": cfg.num_key_value_heads,
         "head_dim": cfg.head_dim, "moe_intermediate_size": cfg.moe_intermediate_size,
-        "intermediate_size": cfg.moe_intermediate_size, "num_experts": cfg.num_experts,
+        "intermediate_size": cfg.intermediate_size if cfg.is_dense else cfg.moe_intermediate_size,
+        "num_experts": cfg.num_experts,
         "num_experts_per_tok": cfg.num_experts_per_tok, "norm_topk_prob": cfg.norm_topk_prob,
         "rope_theta": cfg.rope_theta, "rms_norm_eps": cfg.rms_norm_eps,
         "router_aux_loss_coef": cfg.router_aux_loss_coef, "tie_word_embeddings": cfg.tie_word_embeddings,
@@ -298,6 +307,11 @@ def load_hf_weights(trainer, hf_dir: str) -> None:
             layer.input_layernorm.weight.copy_(get(n["input_layernorm"]))
             layer.post_attention_layernorm.weight.copy_(get(n["post_attention_layernorm"]))
             blk = layer.mlp
+            if cfg.is_dense:
+                blk.w_gate_up[0].copy_(torch.cat([get(n["dense"].format(w="gate_proj")),
+                                                  get(n["dense"].format(w="up_proj"))], 0))
+                blk.w_down[0].copy_(get(n["dense"].format(w="down_proj")))
+                continue
             blk.gate.copy_(get(n["gate"]))
             for j, e in enumerate(blk.placement.local_logical.tolist()):
                 if e < 0:

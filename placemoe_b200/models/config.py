@@ -1,4 +1,5 @@
-"""Model configurations for the Qwen3-MoE / OLMoE decoder families.
+"""Model configurations for the Qwen3-MoE / OLMoE decoder families and the dense
+Qwen3 / Llama families.
 
 The presets carry the shapes named by the benchmark configurations:
 
@@ -9,8 +10,11 @@ The presets carry the shapes named by the benchmark configurations:
 * ``qwen3_30b_a3b``   48 layers, hidden 2048, 32q/4kv heads x 128, QK-norm,
   128 experts top-8, moe_intermediate 768, vocab 151936.
 
+Dense presets (``num_experts == 0``, SwiGLU MLP of ``intermediate_size``):
+``tiny_qwen3_dense``, ``qwen3_8b``, ``llama3_8b``.
+
 ``from_hf_config`` maps a HuggingFace ``config.json`` (model_type
-``qwen3_moe`` / ``olmoe``) onto the same dataclass.
+``qwen3_moe`` / ``olmoe`` / ``qwen3`` / ``llama``) onto the same dataclass.
 
 Reference parity: model configs under veomni/models/transformers/qwen3_moe and
 tests/toy_config/qwen3_moe_toy/config.json.
@@ -36,6 +40,7 @@ class MoEModelConfig:
     num_key_value_heads: int = 4
     head_dim: int = 128
     moe_intermediate_size: int = 768
+    intermediate_size: int = 0  # dense SwiGLU MLP width (dense families: num_experts == 0)
     num_experts: int = 128
     num_experts_per_tok: int = 8
     norm_topk_prob: bool = True
@@ -51,6 +56,11 @@ class MoEModelConfig:
     router_bias_scale: float = 1.0
     router_bias_seed_per_layer: bool = False
     extra: dict = field(default_factory=dict)
+
+    @property
+    def is_dense(self) -> bool:
+        """Dense decoder (Llama / Qwen3 dense): a SwiGLU MLP in every layer instead of experts."""
+        return self.num_experts == 0
 
     @property
     def q_size(self) -> int:
@@ -70,7 +80,7 @@ class MoEModelConfig:
         h, i, e = self.hidden_size, self.moe_intermediate_size, self.num_experts
         attn = h * (self.q_size + 2 * self.kv_size) + self.q_size * h
         norms = 2 * h + (self.q_size + self.kv_size if self.qk_norm == "full" else 2 * self.head_dim if self.qk_norm == "per_head" else 0)
-        layer = attn + norms + e * h + e * 3 * h * i
+        layer = attn + norms + (3 * h * self.intermediate_size if self.is_dense else e * h + e * 3 * h * i)
         emb = self.vocab_size * h * (1 if self.tie_word_embeddings else 2)
         return self.num_hidden_layers * layer + emb + h
 
@@ -79,7 +89,7 @@ class MoEModelConfig:
         h, i, k = self.hidden_size, self.moe_intermediate_size, self.num_experts_per_tok
         proj = 2 * h * (self.q_size + 2 * self.kv_size) + 2 * self.q_size * h
         router = 2 * h * self.num_experts
-        experts = k * 2 * 3 * h * i
+        experts = 2 * 3 * h * self.intermediate_size if self.is_dense else k * 2 * 3 * h * i
         attn = 2 * 2 * self.q_size * (seq_len / 2)  # QK^T and PV, causal average
         per_layer = proj + router + experts + attn
         head = 2 * h * self.vocab_size
@@ -173,6 +183,23 @@ PRESETS: dict[str, MoEModelConfig] = {
 }
 
 
+# dense decoder families (same attention; SwiGLU MLP instead of experts)
+PRESETS.update({
+    "tiny_qwen3_dense": MoEModelConfig(
+        model_type="qwen3", vocab_size=1024, hidden_size=256, num_hidden_layers=2, num_attention_heads=8,
+        num_key_value_heads=2, head_dim=32, intermediate_size=512, num_experts=0, num_experts_per_tok=0,
+        router_aux_loss_coef=0.0),
+    "qwen3_8b": MoEModelConfig(
+        model_type="qwen3", vocab_size=151936, hidden_size=4096, num_hidden_layers=36, num_attention_heads=32,
+        num_key_value_heads=8, head_dim=128, intermediate_size=12288, num_experts=0, num_experts_per_tok=0,
+        router_aux_loss_coef=0.0),
+    "llama3_8b": MoEModelConfig(
+        model_type="llama", vocab_size=128256, hidden_size=4096, num_hidden_layers=32, num_attention_heads=32,
+        num_key_value_heads=8, head_dim=128, intermediate_size=14336, num_experts=0, num_experts_per_tok=0,
+        rope_theta=500000.0, rms_norm_eps=1e-5, qk_norm="none", router_aux_loss_coef=0.0),
+})
+
+
 def get_preset(name: str, **overrides) -> MoEModelConfig:
     if name not in PRESETS:
         raise KeyError(f"unknown model preset {name!r}; available: {sorted(PRESETS)}")
@@ -190,6 +217,16 @@ def from_hf_config(path_or_dict) -> MoEModelConfig:
     mt = d.get("model_type", "qwen3_moe")
     heads = d["num_attention_heads"]
     hd = d.get("head_dim") or d["hidden_size"] // heads
+    if mt in ("qwen3", "llama"):
+        return MoEModelConfig(
+            model_type=mt, vocab_size=d["vocab_size"], hidden_size=d["hidden_size"],
+            num_hidden_layers=d["num_hidden_layers"], num_attention_heads=heads,
+            num_key_value_heads=d.get("num_key_value_heads", heads), head_dim=hd,
+            intermediate_size=d["intermediate_size"], num_experts=0, num_experts_per_tok=0,
+            rope_theta=float(d.get("rope_theta", 10000.0)), rms_norm_eps=float(d.get("rms_norm_eps", 1e-6)),
+            qk_norm="per_head" if mt == "qwen3" else "none", router_aux_loss_coef=0.0,
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)),
+            initializer_range=float(d.get("initializer_range", 0.02)))
     if mt in ("qwen3_moe", "qwen3_vl_moe_text"):
         qk = "per_head"
     elif mt == "olmoe":

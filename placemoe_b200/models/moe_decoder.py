@@ -155,13 +155,34 @@ class MoEBlock(nn.Module):
         return y
 
 
+class DenseMLP(nn.Module):
+    """SwiGLU MLP of the dense families (Llama, Qwen3 dense): down(silu(gate x) * up x).
+
+    The gate and up projections are one [1, 2I, H] tensor (gate rows first) and
+    the down projection [1, H, I], so the CUDA path runs the fused SwiGLU
+    grouped GEMM with a single group.  The names differ from the expert
+    tensors on purpose: these weights are replicated and reduced like every
+    other dense parameter.
+    """
+
+    def __init__(self, cfg: MoEModelConfig):
+        super().__init__()
+        h, i = cfg.hidden_size, cfg.intermediate_size
+        self.w_gate_up = nn.Parameter(torch.empty(1, 2 * i, h))
+        self.w_down = nn.Parameter(torch.empty(1, h, i))
+        self.last_aux_loss = None
+
+    def forward(self, x):
+        return moe_ops.dense_swiglu_mlp(x, self.w_gate_up, self.w_down)
+
+
 class DecoderLayer(nn.Module):
     def __init__(self, cfg: MoEModelConfig, layer_idx: int, num_local_slots: int | None = None):
         super().__init__()
         self.input_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         self.self_attn = Attention(cfg)
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
-        self.mlp = MoEBlock(cfg, layer_idx, num_local_slots)
+        self.mlp = DenseMLP(cfg) if cfg.is_dense else MoEBlock(cfg, layer_idx, num_local_slots)
 
     def forward(self, x, pos, seq_len):
         x = x + self.self_attn(self.input_layernorm(x), pos, seq_len)
@@ -203,6 +224,10 @@ class MoEForCausalLM(nn.Module):
             base = 16 * (li + 1)
             normal_(layer.self_attn.qkv_proj, base + 1)
             normal_(layer.self_attn.o_proj, base + 2)
+            if isinstance(layer.mlp, DenseMLP):
+                normal_(layer.mlp.w_gate_up, base + 4)
+                normal_(layer.mlp.w_down, base + 5)
+                continue
             normal_(layer.mlp.gate, base + 3)
             if expert_init is None:
                 normal_(layer.mlp.gate_up_proj, base + 4)
@@ -214,7 +239,7 @@ class MoEForCausalLM(nn.Module):
         return self
 
     def moe_blocks(self):
-        return [layer.mlp for layer in self.layers]
+        return [layer.mlp for layer in self.layers if isinstance(layer.mlp, MoEBlock)]
 
     def expert_parameters(self):
         for blk in self.moe_blocks():

@@ -199,6 +199,38 @@ class ExpertFFN(torch.autograd.Function):
         return dx, dscale, None, None, None, None, None, None
 
 
+_DENSE_META: dict = {}
+
+
+def dense_swiglu_mlp(x: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """down(silu(gate x) * up x) for dense decoders; w_gate_up [1, 2I, H] (gate rows first), w_down [1, H, I].
+
+    CUDA runs the grouped SwiGLU GEMMs with one group covering every token
+    (rows padded to the segment alignment), so the dense MLP shares the fused
+    epilogues and fp32 master-gradient accumulation of the expert path.
+    """
+    inter = w_gate_up.shape[1] // 2
+    if not x.is_cuda:
+        gu = x.float() @ w_gate_up[0].float().t()
+        return ((F.silu(gu[:, :inter]) * gu[:, inter:]) @ w_down[0].float().t()).to(x.dtype)
+    from .mp import shadow
+
+    t = x.shape[0]
+    rows = -(-t // ALIGN) * ALIGN
+    key = (rows, x.device)
+    meta = _DENSE_META.get(key)
+    if meta is None:
+        meta = (torch.tensor([0, rows], dtype=torch.int32, device=x.device),
+                torch.ones(rows, dtype=torch.float32, device=x.device))
+        _DENSE_META[key] = meta
+    offsets, scale = meta
+    xb = x.to(torch.bfloat16).contiguous()
+    if rows != t:
+        xb = F.pad(xb, (0, 0, 0, rows - t))
+    y = ExpertFFN.apply(xb, scale, shadow(w_gate_up), shadow(w_down), offsets, w_gate_up, w_down, ALIGN)
+    return y[:t] if rows != t else y
+
+
 class GatheredExpertFFN(torch.autograd.Function):
     """Expert FFN over dispatched rows of the token matrix, with optional recomputation.
 

@@ -129,13 +129,13 @@ def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = 
     rank = dist.get_rank(group) if dist.is_initialized() else 0
     cfg = model.config
     if topology is None:
-        topology = expert_topology(cfg.num_experts, world)
+        topology = expert_topology(cfg.num_experts or world, world)
     if topology.ep_size != world:
         raise ValueError("expert parallel size must equal the process-group size")
     keys = [blk.layer_key for blk in model.moe_blocks()]
     placements = build_placements(plans, topology, rank, keys)
     ep = None
-    if world > 1:
+    if world > 1 and keys:
         dev0 = device or next(model.parameters()).device
         # "auto": peer-memory kernels on CUDA (no host synchronisation), all-to-all on CPU / gloo
         use_p2p = transport == "p2p" or (transport == "auto" and dev0.type == "cuda")

@@ -97,7 +97,9 @@ class Trainer:
             self.device = torch.device(cfg.device)
         self.model_cfg = model_cfg or get_preset(cfg.model, **cfg.model_overrides)
         plans = None
-        topology = expert_topology(self.model_cfg.num_experts, self.world, cfg.redundant_slots_per_rank)
+        # dense families hold no experts: a placeholder topology of one slot per rank
+        topology = expert_topology(self.model_cfg.num_experts or self.world, self.world,
+                                   cfg.redundant_slots_per_rank)
         if cfg.placemoe_artifact:
             _, topology, plans = load_artifact(cfg.placemoe_artifact)
             if topology.ep_size != self.world or topology.num_experts != self.model_cfg.num_experts:

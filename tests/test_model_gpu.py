@@ -53,3 +53,30 @@ def test_trainer_steps_reduce_loss():
     from placemoe_b200.ops import check_device_error
 
     check_device_error()
+
+
+def test_dense_model_matches_cpu_reference():
+    """Dense SwiGLU decoder (Qwen3-dense shape): the one-group grouped GEMMs against the CPU formulas."""
+    from placemoe_b200.models.config import get_preset
+    from placemoe_b200.models.moe_decoder import build_model
+
+    cfg = get_preset("tiny_qwen3_dense", hidden_size=512, head_dim=64, num_attention_heads=8,
+                     num_key_value_heads=2, intermediate_size=1024)
+    torch.manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256))
+    cpu = build_model(cfg, device="cpu", seed=3)
+    gpu = build_model(cfg, device="cuda", seed=3)
+    with torch.no_grad():
+        for (_, a), (_, b) in zip(cpu.named_parameters(), gpu.named_parameters()):
+            a.copy_(a.bfloat16().float())
+            b.copy_(a)
+    loss_c, _ = cpu(ids, labels=ids)
+    loss_c.backward()
+    loss_g, _ = gpu(ids.cuda(), labels=ids.cuda())
+    loss_g.backward()
+    assert abs(loss_g.item() - loss_c.item()) < 2e-2 * abs(loss_c.item())
+    for name in ["layers.0.mlp.w_gate_up", "layers.1.mlp.w_down", "layers.0.self_attn.qkv_proj"]:
+        gc = dict(cpu.named_parameters())[name].grad.float()
+        gg = dict(gpu.named_parameters())[name].main_grad.float().cpu()
+        rel = ((gg - gc).norm() / (gc.norm() + 1e-12)).item()
+        assert rel < 0.08, f"{name}: relative grad error {rel:.3f}"

@@ -53,7 +53,7 @@ def test_muon_descends_on_a_matrix_objective():
         w.grad = None
         loss.backward()
         opt.step()
-    assert float((w - target).pow(2).sum()) < 0.2 * first
+    assert (w - target).pow(2).sum().item() < 0.2 * first
     with pytest.raises(ValueError):
         Muon([torch.nn.Parameter(torch.zeros(4))])
 
