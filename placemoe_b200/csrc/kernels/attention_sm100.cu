@@ -13,16 +13,12 @@
 //           written bf16 into 128B-swizzled shared memory (the A operand).
 //   TMEM: S0 | S1 | O   (512 columns allocated).
 //
-// Backward, one CTA per (batch, kv head, 128-key tile); loops over the q heads
-// of the GQA group and the q tiles at or after the key tile:
-//   S^T = K Q^T and dP^T = V dO^T (TMEM), softmax threads own one key row:
-//   P^T = exp2(S^T * c - lse), dS^T = P^T (dP^T - delta) * scale, both written
-//   to swizzled smem.  Then dV += P^T dO, dK += dS^T Q (TMEM accumulators over
-//   the whole loop) and dQ_tile = dS K (TMEM, reusing the S^T columns) which
-//   the same threads add to an fp32 dQ buffer with vector reductions.
-//   The same swizzled smem bytes serve as a K-major operand (rows = keys) and,
-//   reinterpreted, as an MN-major operand (rows = queries), so no transposes
-//   are materialised.
+// Backward, one CTA per (batch, kv head, 128-key tile), looping over the q heads of
+// the GQA group and the q tiles at or after the key tile: a warp-specialised
+// pipeline (TMA warp, MMA warp, two compute warpgroups) in which P^T stays in
+// TMEM as the A operand of dV += P^T dO, dQ tiles leave through TMA
+// reduce-adds of swizzled fp32 staging boxes, and the MMAs of consecutive
+// tiles overlap the elementwise work (details above the kernel).
 //
 // Reference parity: flash attention forward/backward used by
 // veomni/ops/kernels/attention/__init__.py:151-353 (FA2/FA3/FA4 backends).
@@ -589,53 +585,132 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 }
 
 // ---------------------------------------------------------------- backward
+// One CTA per (batch, kv head, 128-key tile), 320 threads; iterations i run over
+// the q heads of the GQA group and the q tiles at or after the key tile.
+//   warp 0      TMA: K, V once; Q_i (+ its LSE and delta rows) through two stages,
+//               dO_i through one stage.
+//   warp 1      MMA, one lane, in this order per iteration:
+//                 dP_i^T = V dO_i^T               -> TMEM B
+//                 dV    += P_i^T dO_i              (A operand = P^T read from TMEM A)
+//                 S_{i+1}^T = K Q_{i+1}^T         -> TMEM A (after dV_i has read P_i^T)
+//                 dK    += dS_i^T Q_i              (dS^T from shared memory)
+//                 dQ_i   = dS_i K                 -> TMEM B (dP_i^T was consumed)
+//               so the tensor pipe only waits while dQ_i is read out of TMEM.
+//   warps 2-9   two warpgroups; warp w owns TMEM lane quarter w % 4 (32 key rows, or
+//               32 query rows of dQ) and column group (w - 2) / 4 (64 queries, D / 2
+//               head dims), with packed f32x2 arithmetic:
+//               P^T = 2^(S^T c - lse) written bf16 into its own S^T columns (TMEM),
+//               dS^T = P^T (dP^T - delta) scale written to swizzled shared memory,
+//               dQ_i read from TMEM into fp32 staging boxes [128 queries x 32 dims]
+//               (128B-swizzled) that one thread per warpgroup adds to the fp32 dQ
+//               buffer with TMA reduce-adds.  Boxes 0-1 have their own 32 KB; boxes
+//               2-3 (D = 128) reuse the dS^T buffer, free once dQ_i completed, and
+//               dS_{i+1} is written only after those reductions finished reading it.
+//   TMEM: A = S^T / P^T (128 cols) | B = dP^T / dQ (128) | dV (D) | dK (D).
+// P^T of queries [64g, 64g + 64) sits in columns [64g, 64g + 32) of A (two bf16 per
+// column), so each MMA k-step of 16 queries reads 8 columns.
+// CTAs run (batch, kv head) outer and key tile inner, so the CTAs resident at one time
+// share a few heads and their Q / dO tiles and dQ reductions stay in L2.
+constexpr int kBwdThreads = 320;
+constexpr int kBwdCompute = 256;  // threads of the two compute warpgroups
+
+// K, V, two Q stages, dO, dS^T, dQ staging (32 KB), LSE / delta stages, barriers.  The
+// base of dynamic shared memory must be 1024-byte aligned (checked in the kernel).
 template <int D>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+constexpr int bwd_smem() {
+  return 5 * (D / 64) * 16384 + 32768 + 32768 + 2048 + 128;
+}
+
+// P = 2^(S c - lse) for 32 queries of one key row (column offset `rel` = key row - first
+// query, masked queries < key when MASK): bf16 pairs for TMEM and P * scale in f32x2 pairs.
+template <bool MASK>
+PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, float scale, int rel,
+                         uint32_t* pk, uint64_t* ps) {
+  const uint64_t c2 = f2_pack(c, c), sc2 = f2_pack(scale, scale);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float4 l = lse4[j];
+    const uint64_t x0 = fma_f2(f2_pack(__uint_as_float(sv[4 * j]), __uint_as_float(sv[4 * j + 1])), c2,
+                               f2_pack(-l.x, -l.y));
+    const uint64_t x1 = fma_f2(f2_pack(__uint_as_float(sv[4 * j + 2]), __uint_as_float(sv[4 * j + 3])), c2,
+                               f2_pack(-l.z, -l.w));
+    float e[4];
+    f2_unpack(x0, e[0], e[1]);
+    f2_unpack(x1, e[2], e[3]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      e[k] = fast_exp2(e[k]);
+      if (MASK && 4 * j + k < rel) e[k] = 0.f;
+    }
+    pk[2 * j] = pack_bf16(e[0], e[1]);
+    pk[2 * j + 1] = pack_bf16(e[2], e[3]);
+    ps[2 * j] = mul_f2(f2_pack(e[0], e[1]), sc2);
+    ps[2 * j + 1] = mul_f2(f2_pack(e[2], e[3]), sc2);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO, AttnArgs a) {
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    const __grid_constant__ CUtensorMap tmDQ, AttnArgs a) {
   constexpr int ND = D / 64;
   constexpr int kTB = ND * 16384;  // one [128 x D] bf16 tile
-  constexpr uint32_t kIdescS = make_idesc_bf16(128, 128, false, false);   // St, dPt
-  constexpr uint32_t kIdescKV = make_idesc_bf16(128, D, false, true);    // dV, dK, dQ (A K-major)
-  constexpr uint32_t kIdescQ = make_idesc_bf16(128, D, true, true);      // dQ (A MN-major)
+  constexpr int kQD = D / 2;       // head dims per compute thread (dQ, dK, dV)
+  constexpr int kBoxes = kQD / 32;  // dQ staging boxes per warpgroup
+  constexpr bool kBoxesInDS = D == 128;  // boxes 2-3 (warpgroup 1) are staged in the dS^T buffer
+  constexpr uint32_t kIdescS = make_idesc_bf16(128, 128, false, false);  // S^T, dP^T
+  constexpr uint32_t kIdescKV = make_idesc_bf16(128, D, false, true);   // dV, dK
+  constexpr uint32_t kIdescQ = make_idesc_bf16(128, D, true, true);     // dQ (A = dS, MN-major)
 
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  uint8_t* sm = smem_raw + (((raw + 1023u) & ~1023u) - raw);
-  uint8_t* sK = sm;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  if (smem_u32(smem_raw) & 1023u) {  // swizzled tiles need 1024-byte alignment: refuse, do not misread
+    if (threadIdx.x == 0) set_error(kErrArgs);
+    return;
+  }
+  uint8_t* sK = smem_raw;
   uint8_t* sV = sK + kTB;
-  uint8_t* sQ = sV + kTB;
-  uint8_t* sDO = sQ + kTB;
-  uint8_t* sP = sDO + kTB;     // 32 KB: P^T [keys x queries]
-  uint8_t* sDS = sP + 32768;   // 32 KB: dS^T
-  float* sLse = reinterpret_cast<float*>(sDS + 32768);  // [128], log2 units
-  float* sDelta = sLse + 128;                          // [128]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + 128);
+  uint8_t* sQ0 = sV + kTB;        // two Q stages
+  uint8_t* sDO = sQ0 + 2 * kTB;
+  uint8_t* sDS = sDO + kTB;       // 32 KB: dS^T [keys x queries]
+  uint8_t* sStage = sDS + 32768;  // 32 KB: dQ staging boxes 0-1
+  float* sLse = reinterpret_cast<float*>(sStage + 32768);  // [2][128], log2 units
+  float* sDelta = sLse + 256;                               // [2][128]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + 256);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* s_full = bars + 3;
-  uint64_t* ds_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* st_free = bars + 6;
-  uint64_t* dkv_full = bars + 7;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* q_full = bars + 1;   // [2]
+  uint64_t* q_empty = bars + 3;  // [2]
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_empty = bars + 6;
+  uint64_t* s_full = bars + 7;
+  uint64_t* dp_full = bars + 8;
+  uint64_t* dq_full = bars + 9;
+  uint64_t* p_done = bars + 10;
+  uint64_t* ds_done = bars + 11;
+  uint64_t* dq_drained = bars + 12;
+  uint64_t* dkv_full = bars + 13;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = a.S / kTile;
   const int G = a.Hq / a.Hkv;
   const int L = blockIdx.x;
-  const int kt = L / (a.B * a.Hkv);  // light tiles (large kt) last is fine: kt small = more work, scheduled first
-  const int rem = L % (a.B * a.Hkv);
+  const int kt = L % nq;  // within a head, the key tiles with the most q tiles start first
+  const int rem = L / nq;
   const int b = rem / a.Hkv, hk = rem % a.Hkv;
   const int tk0 = b * a.S + kt * kTile;
   const int nqt = nq - kt;
   const int n_it = G * nqt;
 
   if (threadIdx.x == 0) {
-    mbar_init(kv_full, 1); mbar_init(qdo_full, 1); mbar_init(qdo_empty, 1); mbar_init(s_full, 1);
-    mbar_init(ds_full, 128); mbar_init(dq_full, 1); mbar_init(st_free, 128); mbar_init(dkv_full, 1);
+    mbar_init(kv_full, 1);
+    mbar_init(&q_full[0], 1); mbar_init(&q_full[1], 1);
+    mbar_init(&q_empty[0], 1); mbar_init(&q_empty[1], 1);
+    mbar_init(do_full, 1); mbar_init(do_empty, 1);
+    mbar_init(s_full, 1); mbar_init(dp_full, 1); mbar_init(dq_full, 1);
+    mbar_init(p_done, kBwdCompute); mbar_init(ds_done, kBwdCompute); mbar_init(dq_drained, kBwdCompute);
+    mbar_init(dkv_full, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -644,7 +719,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
-  const uint32_t t_st = tmem, t_dp = tmem + 128, t_dv = tmem + 256, t_dk = tmem + 256 + D;
+  const uint32_t tA = tmem, tB = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -656,117 +731,192 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       for (int it = 0; it < n_it; ++it) {
         const int h = hk * G + it / nqt;
-        const int qt = kt + it % nqt;
-        const int tq0 = b * a.S + qt * kTile;
-        if (!mbar_wait_abortable(qdo_empty, (it & 1) ^ 1, s_abort)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * kTB + 1024);
+        const int tq0 = b * a.S + (kt + it % nqt) * kTile;
+        const int st = it & 1;
+        if (!mbar_wait_abortable(&q_empty[st], ((it >> 1) & 1) ^ 1, s_abort)) break;
+        mbar_arrive_expect_tx(&q_full[st], kTB + 1024);
 #pragma unroll
-        for (int d = 0; d < ND; ++d) {
-          tma_load_3d(sQ + d * 16384, &tmQ, qdo_full, d * 64, h, tq0);
-          tma_load_3d(sDO + d * 16384, &tmDO, qdo_full, d * 64, h, tq0);
-        }
-        bulk_load(sLse, a.lse_in + (size_t)h * a.T + tq0, 512, qdo_full);
-        bulk_load(sDelta, a.delta + (size_t)h * a.T + tq0, 512, qdo_full);
+        for (int d = 0; d < ND; ++d) tma_load_3d(sQ0 + st * kTB + d * 16384, &tmQ, &q_full[st], d * 64, h, tq0);
+        bulk_load(sLse + st * 128, a.lse_in + (size_t)h * a.T + tq0, 512, &q_full[st]);
+        bulk_load(sDelta + st * 128, a.delta + (size_t)h * a.T + tq0, 512, &q_full[st]);
+        if (!mbar_wait_abortable(do_empty, (it & 1) ^ 1, s_abort)) break;
+        mbar_arrive_expect_tx(do_full, kTB);
+#pragma unroll
+        for (int d = 0; d < ND; ++d) tma_load_3d(sDO + d * 16384, &tmDO, do_full, d * 64, h, tq0);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aDO = smem_u32(sDO);
-      const uint32_t aP = smem_u32(sP), aDS = smem_u32(sDS);
-      bool ok = mbar_wait_abortable(kv_full, 0, s_abort);
-      for (int it = 0; ok && it < n_it; ++it) {
-        if (!mbar_wait_abortable(qdo_full, it & 1, s_abort)) break;
-        if (!mbar_wait_abortable(st_free, (it & 1) ^ 1, s_abort)) break;
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aDO = smem_u32(sDO), aDS = smem_u32(sDS);
+      const uint32_t aQ0 = smem_u32(sQ0);
+      bool ok = mbar_wait_abortable(kv_full, 0, s_abort) && mbar_wait_abortable(&q_full[0], 0, s_abort);
+      if (ok) {
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_f16(t_st, kmaj_desc(aK, k), kmaj_desc(aQ, k), kIdescS, k > 0);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) umma_f16(t_dp, kmaj_desc(aV, k), kmaj_desc(aDO, k), kIdescS, k > 0);
+        for (int k = 0; k < D / 16; ++k) umma_f16(tA, kmaj_desc(aK, k), kmaj_desc(aQ0, k), kIdescS, k > 0);
         umma_commit(s_full);
-        if (!mbar_wait_abortable(ds_full, it & 1, s_abort)) break;
+      }
+      for (int it = 0; ok && it < n_it; ++it) {
+        const uint32_t aQ = aQ0 + (it & 1) * kTB;
+        // dP_i^T -> B once dO_i landed and dQ_{i-1} left B
+        if (!mbar_wait_abortable(do_full, it & 1, s_abort)) break;
+        if (it > 0 && !mbar_wait_abortable(dq_drained, (it - 1) & 1, s_abort)) break;
         tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_f16(t_dv, kmaj_desc(aP, k), mnmaj_desc(aDO, k), kIdescKV, (it > 0 || k > 0));
+        for (int k = 0; k < D / 16; ++k) umma_f16(tB, kmaj_desc(aV, k), kmaj_desc(aDO, k), kIdescS, k > 0);
+        umma_commit(dp_full);
+        // dV += P_i^T dO_i with P^T from TMEM
+        if (!mbar_wait_abortable(p_done, it & 1, s_abort)) break;
+        tc_fence_after();
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_f16(t_dk, kmaj_desc(aDS, k), mnmaj_desc(aQ, k), kIdescKV, (it > 0 || k > 0));
+        for (int k = 0; k < 8; ++k)
+          umma_f16_ts(tDV, tA + (k >> 2) * 64 + (k & 3) * 8, mnmaj_desc(aDO, k), kIdescKV, (it > 0 || k > 0));
+        umma_commit(do_empty);
+        // S_{i+1}^T -> A (ordered after dV_i, which read P_i^T from A)
+        if (it + 1 < n_it) {
+          if (!mbar_wait_abortable(&q_full[(it + 1) & 1], ((it + 1) >> 1) & 1, s_abort)) break;
+          tc_fence_after();
+          const uint32_t aQn = aQ0 + ((it + 1) & 1) * kTB;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) umma_f16(t_st, mnmaj_desc(aDS, k), mnmaj_desc(aK, k), kIdescQ, k > 0);
-        umma_commit(qdo_empty);
+          for (int k = 0; k < D / 16; ++k) umma_f16(tA, kmaj_desc(aK, k), kmaj_desc(aQn, k), kIdescS, k > 0);
+          umma_commit(s_full);
+        }
+        // dK += dS_i^T Q_i, dQ_i = dS_i K -> B
+        if (!mbar_wait_abortable(ds_done, it & 1, s_abort)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_f16(tDK, kmaj_desc(aDS, k), mnmaj_desc(aQ, k), kIdescKV, (it > 0 || k > 0));
+        umma_commit(&q_empty[it & 1]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) umma_f16(tB, mnmaj_desc(aDS, k), mnmaj_desc(aK, k), kIdescQ, k > 0);
         umma_commit(dq_full);
       }
-      umma_commit(dkv_full);
+      umma_commit(dkv_full);  // also on abort: every issued MMA completes before TMEM is freed
     }
   } else {
     const int qd = warp & 3;
+    const int cg = (warp - 2) >> 2;
     const int r = qd * 32 + lane;  // key row (S^T, dP^T, dV, dK) / query row (dQ)
     const uint32_t lrow = (uint32_t)(qd * 32) << 16;
     const float c = a.scale * kLog2e;
+    // dQ staging: a box holds 32 head dims of all 128 queries; warpgroup cg owns boxes
+    // kBoxes * cg ...; boxes 0-1 live in the staging buffer, 2-3 in the dS^T buffer
+    uint8_t* bx0 = cg == 0 ? sStage : (kBoxesInDS ? sDS : sStage + 16384);
+    const bool issuer = qd == 0 && lane == 0;
+    // A failed (bounded) wait only skips work: every thread still reaches the named barriers,
+    // and the decision to stop is taken uniformly by all compute threads (bar.red.and).
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / nqt;
       const int qt = kt + it % nqt;
       const int tq0 = b * a.S + qt * kTile;
-      if (!mbar_wait_abortable(s_full, it & 1, s_abort)) { ok = false; break; }
-      tc_fence_after();
-      const bool diag = qt == kt;
-#pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t sv[32], pv[32];
-        tmem_ld32(t_st + lrow + cc * 32, sv);
-        tmem_ld32(t_dp + lrow + cc * 32, pv);
-        tmem_ld_wait();
-        float p[32], ds[32];
+      const int st = it & 1;
+      const float4* lse4 = reinterpret_cast<const float4*>(sLse + st * 128 + cg * 64);
+      const float4* dl4 = reinterpret_cast<const float4*>(sDelta + st * 128 + cg * 64);
+      // q_full makes the LSE / delta rows of this stage visible to these threads
+      ok = ok && mbar_wait_abortable(&q_full[st], (it >> 1) & 1, s_abort) &&
+           mbar_wait_abortable(s_full, it & 1, s_abort);
+      ok = __all_sync(0xffffffffu, ok);
+      uint64_t ps[32];  // P * scale, pairs of queries
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int q = cc * 32 + i;
-          float e = fast_exp2(__uint_as_float(sv[i]) * c - sLse[q]);
-          if (diag && q < r) e = 0.f;
-          p[i] = e;
-          ds[i] = e * (__uint_as_float(pv[i]) - sDelta[q]) * a.scale;
+        for (int half = 0; half < 2; ++half) {
+          uint32_t sv[32], pk[16];
+          const int q0 = cg * 64 + half * 32;
+          tmem_ld32(tA + lrow + q0, sv);
+          tmem_ld_wait();
+          if (qt == kt) bwd_probs<true>(sv, lse4 + half * 8, c, a.scale, r - q0, pk, ps + half * 16);
+          else bwd_probs<false>(sv, lse4 + half * 8, c, a.scale, 0, pk, ps + half * 16);
+          // P^T bf16 over the group's own S^T columns (already read)
+          tmem_st16(tA + lrow + cg * 64 + half * 16, pk);
         }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int chunk = cc * 4 + g;  // 8 queries per 16-byte chunk
-          uint4 pk = make_uint4(pack_bf16(p[8 * g], p[8 * g + 1]), pack_bf16(p[8 * g + 2], p[8 * g + 3]),
-                                pack_bf16(p[8 * g + 4], p[8 * g + 5]), pack_bf16(p[8 * g + 6], p[8 * g + 7]));
-          uint4 dk = make_uint4(pack_bf16(ds[8 * g], ds[8 * g + 1]), pack_bf16(ds[8 * g + 2], ds[8 * g + 3]),
-                                pack_bf16(ds[8 * g + 4], ds[8 * g + 5]), pack_bf16(ds[8 * g + 6], ds[8 * g + 7]));
-          st_swz(sP + (chunk >> 3) * 16384, r, chunk & 7, pk);
-          st_swz(sDS + (chunk >> 3) * 16384, r, chunk & 7, dk);
-        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(p_done);
       }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(ds_full);
-      // dQ tile (rows = queries) -> fp32 accumulation buffer
-      if (!mbar_wait_abortable(dq_full, it & 1, s_abort)) { ok = false; break; }
-      tc_fence_after();
-      float* dst = a.dq_acc + ((size_t)(tq0 + r) * a.Hq + h) * D;
-#pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
-        uint32_t v[32];
-        tmem_ld32(t_st + lrow + cc * 32, v);
+      // dS^T = P^T (dP^T - delta) * scale -> swizzled shared memory
+      ok = ok && mbar_wait_abortable(dp_full, it & 1, s_abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if constexpr (kBoxesInDS) {
+        // the dQ reductions of the previous tile read staging boxes 2-3 out of the dS^T buffer
+        if (issuer && cg == 1) bulk_wait_read_0();
+        ok = named_bar_and(5, kBwdCompute, ok);
+      }
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t pv[32], dsk[16];
+          tmem_ld32(tB + lrow + cg * 64 + half * 32, pv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float4 d = dl4[half * 8 + j];
+            const uint64_t t0 = add_f2(f2_pack(__uint_as_float(pv[4 * j]), __uint_as_float(pv[4 * j + 1])),
+                                       f2_pack(-d.x, -d.y));
+            const uint64_t t1 = add_f2(f2_pack(__uint_as_float(pv[4 * j + 2]), __uint_as_float(pv[4 * j + 3])),
+                                       f2_pack(-d.z, -d.w));
+            float u0, u1, u2, u3;
+            f2_unpack(mul_f2(ps[half * 16 + 2 * j], t0), u0, u1);
+            f2_unpack(mul_f2(ps[half * 16 + 2 * j + 1], t1), u2, u3);
+            dsk[2 * j] = pack_bf16(u0, u1);
+            dsk[2 * j + 1] = pack_bf16(u2, u3);
+          }
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            const int chunk = cg * 8 + half * 4 + g;  // 8 queries per 16-byte chunk
+            st_swz(sDS + (chunk >> 3) * 16384, r, chunk & 7,
+                   make_uint4(dsk[4 * g], dsk[4 * g + 1], dsk[4 * g + 2], dsk[4 * g + 3]));
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        mbar_arrive(ds_done);
+      }
+      // dQ_i (rows = queries): TMEM -> registers (B released) -> staging boxes -> TMA reduce-add
+      ok = ok && mbar_wait_abortable(dq_full, it & 1, s_abort);
+      ok = __all_sync(0xffffffffu, ok);
+      uint32_t dq[kQD];
+      if (ok) {
+        tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < kBoxes; ++cc) {
+          uint32_t (&v)[32] = *reinterpret_cast<uint32_t(*)[32]>(dq + cc * 32);
+          tmem_ld32(tB + lrow + cg * kQD + cc * 32, v);
+        }
         tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(dq_drained);
+      }
+      if (issuer) bulk_wait_read_0();  // this group's previous reductions have read its staging
+      if (!named_bar_and(6, kBwdCompute, ok)) { ok = false; break; }
+#pragma unroll
+      for (int cc = 0; cc < kBoxes; ++cc)
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          red_add_v4(dst + cc * 32 + 4 * i, __uint_as_float(v[4 * i]), __uint_as_float(v[4 * i + 1]),
-                     __uint_as_float(v[4 * i + 2]), __uint_as_float(v[4 * i + 3]));
+          st_swz(bx0 + cc * 16384, r, i,
+                 make_uint4(dq[cc * 32 + 4 * i], dq[cc * 32 + 4 * i + 1], dq[cc * 32 + 4 * i + 2],
+                            dq[cc * 32 + 4 * i + 3]));
+      fence_proxy_async_smem();
+      named_bar_sync(1 + cg, 128);
+      if (issuer) {
+#pragma unroll
+        for (int cc = 0; cc < kBoxes; ++cc) tma_reduce_add_3d(&tmDQ, bx0 + cc * 16384, cg * kQD + cc * 32, h, tq0);
+        bulk_commit();
       }
-      tc_fence_before();
-      mbar_arrive(st_free);
     }
+    if (issuer) bulk_wait_all();  // reductions complete before the CTA's shared memory goes away
     if (ok && mbar_wait_abortable(dkv_full, 0, s_abort)) {
       tc_fence_after();
-      __nv_bfloat16* dvrow = a.dv + ((size_t)(tk0 + r) * a.Hkv + hk) * D;
-      __nv_bfloat16* dkrow = a.dk + ((size_t)(tk0 + r) * a.Hkv + hk) * D;
 #pragma unroll 1
-      for (int cc = 0; cc < D / 32; ++cc) {
+      for (int cc = 0; cc < kQD / 32; ++cc) {
         uint32_t v[32], w[32];
-        tmem_ld32(t_dv + lrow + cc * 32, v);
-        tmem_ld32(t_dk + lrow + cc * 32, w);
+        tmem_ld32(tDV + lrow + cg * kQD + cc * 32, v);
+        tmem_ld32(tDK + lrow + cg * kQD + cc * 32, w);
         tmem_ld_wait();
-        uint4* dv4 = reinterpret_cast<uint4*>(dvrow + cc * 32);
-        uint4* dk4 = reinterpret_cast<uint4*>(dkrow + cc * 32);
+        uint4* dv4 = reinterpret_cast<uint4*>(a.dv + ((size_t)(tk0 + r) * a.Hkv + hk) * D + cg * kQD + cc * 32);
+        uint4* dk4 = reinterpret_cast<uint4*>(a.dk + ((size_t)(tk0 + r) * a.Hkv + hk) * D + cg * kQD + cc * 32);
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           dv4[i] = make_uint4(pack_bf16(__uint_as_float(v[8 * i]), __uint_as_float(v[8 * i + 1])),
@@ -784,6 +934,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
+    // every MMA this CTA issued has completed once dkv_full fired (bounded wait)
+    mbar_wait(dkv_full, 0);
+    __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -816,6 +969,21 @@ static CUtensorMap head_map(const torch::Tensor& t) {
   return m;
 }
 
+// fp32 dQ accumulator [T, Hq, D] -> dims {D, Hq, T}, box {32, 1, 128}, 128B swizzle (reduce-add target)
+static CUtensorMap dq_acc_map(const torch::Tensor& t) {
+  const int64_t T = t.size(0), H = t.size(1), D = t.size(2);
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)(D * 4), (cuuint64_t)(H * D * 4)};
+  cuuint32_t box[3] = {32, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, t.data_ptr(), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "dQ tensor map failed: ", (int)r);
+  return m;
+}
+
 static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torch::Tensor& v, int64_t S) {
   TORCH_CHECK(q.is_cuda() && q.scalar_type() == torch::kBFloat16 && q.is_contiguous() && q.dim() == 3, "q [T,Hq,D] bf16");
   TORCH_CHECK(k.sizes() == v.sizes() && k.is_contiguous() && v.is_contiguous(), "k/v layout");
@@ -829,8 +997,6 @@ static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torc
 
 template <int D>
 static int fwd_smem() { return 1024 + (5 * (D / 64) * 16384) + 32768 + 256; }
-template <int D>
-static int bwd_smem() { return 1024 + 4 * (D / 64) * 16384 + 2 * 32768 + 1024 + 256; }
 
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S) {
   check_qkv(q, k, v, S);
@@ -905,15 +1071,16 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   auto lse2 = (lse * kLog2e).contiguous();
   a.lse_in = lse2.data_ptr<float>();
   CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v), mdo = head_map(dout);
+  CUtensorMap mdq = dq_acc_map(dq_acc);
   const int grid = a.B * Hkv * ((int)S / kTile);
   if (D == 128) {
     auto kern = attn_bwd_kernel<128>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<128>()));
-    kern<<<grid, kAttnThreads, bwd_smem<128>(), stream>>>(mq, mk, mv, mdo, a);
+    kern<<<grid, kBwdThreads, bwd_smem<128>(), stream>>>(mq, mk, mv, mdo, mdq, a);
   } else {
     auto kern = attn_bwd_kernel<64>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<64>()));
-    kern<<<grid, kAttnThreads, bwd_smem<64>(), stream>>>(mq, mk, mv, mdo, a);
+    kern<<<grid, kBwdThreads, bwd_smem<64>(), stream>>>(mq, mk, mv, mdo, mdq, a);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const long long n = (long long)T * Hq * D;

@@ -184,6 +184,23 @@ PM_DEVICE void tma_reduce_add_3d(const void* tmap, const void* smem_src, int x, 
       : "memory");
 }
 PM_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// named CTA barrier over `count` threads (a multiple of 32); id 0 is __syncthreads
+PM_DEVICE void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// named barrier that also returns the AND of `pred` over its `count` threads (uniform decision)
+PM_DEVICE bool named_bar_and(int id, int count, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n"
+      " setp.ne.u32 p, %1, 0;\n"
+      " bar.red.and.pred q, %2, %3, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(count)
+      : "memory");
+  return r != 0;
+}
 // at most one committed group may still be reading shared memory
 PM_DEVICE void bulk_wait_read_1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
 // no committed group is still reading shared memory

@@ -199,7 +199,8 @@ def test_fused_linear_ce():
 
 @pytest.mark.parametrize("b,s,hq,hkv,d,qscale", [(1, 128, 1, 1, 128, 1.0), (2, 512, 4, 2, 128, 1.0),
                                                  (1, 1024, 16, 16, 128, 1.0), (2, 256, 8, 2, 64, 1.0),
-                                                 (1, 1024, 2, 1, 128, 8.0), (1, 384, 2, 2, 64, 4.0)])
+                                                 (1, 1024, 2, 1, 128, 8.0), (1, 384, 2, 2, 64, 4.0),
+                                                 (1, 512, 8, 1, 128, 1.0)])
 def test_attention_fwd_bwd(b, s, hq, hkv, d, qscale):
     """qscale > 1 spreads the scores so that the running row max moves often (rescaling paths)."""
     from placemoe_b200.ops import kernels
