@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--artifact", default="")
     p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
     p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
+    p.add_argument("--dense-sharding", default="auto", choices=["auto", "on", "off"],
+                   help="shard dense masters/moments/gradients over the ranks (peer-memory RS/AG); auto = N > 1")
     p.add_argument("--recompute-expert-rows", action="store_true",
                    help="re-gather dispatched expert inputs in the backward instead of keeping them (memory)")
     return p.parse_args()
@@ -153,7 +155,7 @@ def plan_placement(trainer, pool, args, rank, world):
     for blk in trainer.model.moe_blocks():
         moved += migrate_layer(trainer, blk, plans[blk.layer_key])
     trainer._norm_table = None
-    trainer.optimizer._tables.clear()
+    trainer.optimizer.reset_tables()
     dist.barrier()
     return {"plan_steps": args.plan_steps, "planner_ms": round(planner_ms, 1),
             "install_ms": round((time.perf_counter() - t1) * 1e3, 1), "moved_slots": moved}
@@ -198,7 +200,8 @@ def main():
     cfg = TrainConfig(model=args.model, seq_len=args.seq, batch_per_rank=args.batch_per_gpu,
                       micro_batch_size=args.micro_batch, redundant_slots_per_rank=args.redundant_slots,
                       placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1,
-                      ep_transport=args.ep_transport, recompute_expert_rows=args.recompute_expert_rows)
+                      ep_transport=args.ep_transport, recompute_expert_rows=args.recompute_expert_rows,
+                      dense_sharding=args.dense_sharding)
     trainer = Trainer(cfg, mcfg)
     pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank)
     dev_batches = [b.to("cuda") for b in pool.batches]
@@ -273,7 +276,7 @@ def main():
                 "global_batch": args.batch_per_gpu * world,
                 "seq_len": args.seq,
                 "micro_batch": args.micro_batch,
-                "parallelism": f"dp{world}+ep{world}",
+                "parallelism": f"dp{world}+ep{world}" + ("+dense-shard" if trainer.dense_shards is not None else ""),
                 "ep_transport": args.ep_transport if world > 1 else "none",
                 "placement": (f"PlaceMoE static L,M planned from {args.plan_steps} captured steps, "
                               f"{args.redundant_slots} replica slot(s)/GPU" if plan_info else

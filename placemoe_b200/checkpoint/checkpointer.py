@@ -95,10 +95,25 @@ def _placement_state(trainer) -> dict:
     return out
 
 
+def _sync_params(trainer) -> None:
+    """Sharded optimizers write their current masters into ``param.data`` (collective)."""
+    sync = getattr(trainer.optimizer, "sync_params", None)
+    if sync is not None:
+        sync()
+
+
+def _reload_params(trainer) -> None:
+    """Optimizers that keep their own copies re-read loaded ``param.data`` / state."""
+    reload = getattr(trainer.optimizer, "reload_from_params", None)
+    if reload is not None:
+        reload()
+
+
 def save_checkpoint(trainer, root: str) -> str:
     rank, _ = _world()
     path = os.path.join(root, f"global_step_{trainer.global_step}")
     os.makedirs(path, exist_ok=True)
+    _sync_params(trainer)
     # make sure optimizer state exists for every parameter (zeros before the first step)
     for p in trainer.model.parameters():
         trainer.optimizer._state(p)
@@ -189,6 +204,7 @@ def load_checkpoint(trainer, path: str, *, restore_placement: bool = True) -> di
         st["step"] = step
     trainer.global_step = int(extra["global_step"])
     trainer.optimizer.reset_tables()
+    _reload_params(trainer)
     return extra
 
 
@@ -212,6 +228,7 @@ def export_hf(trainer, out_dir: str) -> str | None:
     from safetensors.torch import save_file
 
     rank, world = _world()
+    _sync_params(trainer)
     model, cfg = trainer.model, trainer.model_cfg
     tensors: dict[str, torch.Tensor] = {}
     inter = cfg.moe_intermediate_size
@@ -320,6 +337,7 @@ def load_hf_weights(trainer, hf_dir: str) -> None:
                 u = get(n["expert"].format(e=e, w="up_proj"))
                 blk.gate_up_proj[j].copy_(torch.cat([g, u], 0))
                 blk.down_proj[j].copy_(get(n["expert"].format(e=e, w="down_proj")))
+    _reload_params(trainer)
 
 
 __all__ = ["save_checkpoint", "load_checkpoint", "export_hf", "load_hf_weights", "placement_digest", "np"]

@@ -72,6 +72,18 @@ class MultiOptimizer:
         for opt in self.optimizers.values():
             opt.reset_tables()
 
+    def sync_params(self) -> None:
+        """Make every ``param.data`` current (sharded optimizers gather their masters; collective)."""
+        for opt in self.optimizers.values():
+            if hasattr(opt, "sync_params"):
+                opt.sync_params()
+
+    def reload_from_params(self) -> None:
+        """Push loaded ``param.data`` / state into optimizers that keep their own copies."""
+        for opt in self.optimizers.values():
+            if hasattr(opt, "reload_from_params"):
+                opt.reload_from_params()
+
     @property
     def defaults(self):
         return self._fallback().defaults

@@ -57,6 +57,9 @@ class TrainConfig:
     min_lr_ratio: float = 0.1
     muon_lr: float = 0.02
     muon_momentum: float = 0.95
+    # "auto": shard dense masters / moments / reduced gradients over the ranks (peer-memory
+    # reduce-scatter + all-gather) when N > 1 on CUDA with AdamW; "on" / "off" force it
+    dense_sharding: str = "auto"
     seed: int = 0
     redundant_slots_per_rank: int = 0
     placemoe_artifact: str = ""  # schema-v2 artifact loaded at startup
@@ -128,10 +131,45 @@ class Trainer:
             self.peer_exchange = PeerExchange(None, self.device, nbytes)
             self.replica_sync = ReplicaGradSync(self.peer_exchange)
             self.pstate.ep.replica_sync = self.replica_sync
+        self.dense_shards = None
+        if self._want_dense_sharding():
+            self._setup_dense_shards()
         self._norm_table = None
         self.global_step = 0
         self.hot_update = None  # set by placement runtime (hot updates)
         self.metrics: dict = {}
+
+    # ------------------------------------------------------------- sharding
+    def _want_dense_sharding(self) -> bool:
+        mode = self.cfg.dense_sharding
+        if mode not in ("auto", "on", "off"):
+            raise ValueError("dense_sharding must be 'auto', 'on' or 'off'")
+        if mode == "on" and self.cfg.optimizer != "adamw":
+            raise ValueError("dense sharding is built for AdamW (Muon needs whole matrices)")
+        if mode == "off" or self.world == 1 or self.cfg.optimizer != "adamw":
+            return False
+        return mode == "on" or (self.device.type == "cuda" and self.replica_sync is not None)
+
+    def _setup_dense_shards(self) -> None:
+        """AdamW over shards of the dense matrices; small fp32-read parameters stay replicated."""
+        from ..ops.optim import FusedAdamW
+        from ..optim import MultiOptimizer
+        from ..parallel.data_parallel import DenseGradBucket, is_expert_param
+        from ..parallel.dense_shard import ShardedDenseAdamW, shardable
+
+        cfg = self.cfg
+        named = list(self.model.named_parameters())
+        shard = [p for n, p in named if not is_expert_param(n) and shardable(n, p)]
+        rep = [p for n, p in named if not is_expert_param(n) and not shardable(n, p)]
+        experts = [p for n, p in named if is_expert_param(n)]
+        self.dense_shards = ShardedDenseAdamW(shard, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                              weight_decay=cfg.weight_decay)
+        if self.pstate.dense_bucket is not None:
+            self.pstate.dense_bucket = DenseGradBucket(rep, self.device) if rep else None
+        self.optimizer = MultiOptimizer({
+            "experts": FusedAdamW(experts + rep, lr=cfg.lr, betas=cfg.betas, eps=cfg.eps,
+                                  weight_decay=cfg.weight_decay),
+            "dense": self.dense_shards})
 
     # ------------------------------------------------------------------ utils
     def lr_at(self, step: int) -> float:
@@ -152,16 +190,20 @@ class Trainer:
             if self.pstate.dense_bucket is not None:
                 grads.append(self.pstate.dense_bucket.flat)
                 weights.append(1.0)
+            if self.dense_shards is not None:  # disjoint slices: each counted once over the ranks
+                grads.append(self.dense_shards.grad_shard)
+                weights.append(1.0)
             self._norm_table = kn.sq_norm_build_table(grads, weights)
         out = torch.zeros((), device=self.device, dtype=torch.float32)
         kn.sq_norm(self._norm_table[0], self._norm_table[1], out)
         if self.world > 1:
-            # dense part is replicated (counted once per rank) -> subtract (world-1) copies
-            dense = self.pstate.dense_bucket.flat
-            dsq = dense.float().pow(2).sum()
-            out = out - dsq
+            # the replicated dense part is counted once per rank -> keep one copy
+            dsq = self.pstate.dense_bucket.flat.float().pow(2).sum() if self.pstate.dense_bucket is not None else None
+            if dsq is not None:
+                out = out - dsq
             dist.all_reduce(out)
-            out = out + dsq
+            if dsq is not None:
+                out = out + dsq
         return out
 
     # ------------------------------------------------------------------- step
@@ -217,10 +259,13 @@ class Trainer:
         if self.replica_sync is not None:
             self.replica_sync.wait()  # replicas were reduced over peer memory during the backward
         moe_ops.settle_stale_grads(self.model.expert_parameters())
-        if self.replica_sync is None and self.world > 1:
-            sync_replica_gradients(self.model, self.pstate.placements)
+        if self.world > 1:
+            if self.replica_sync is None:  # else reduced over peer memory during the backward
+                sync_replica_gradients(self.model, self.pstate.placements)
             if self.pstate.dense_bucket is not None:
                 self.pstate.dense_bucket.reduce()
+            if self.dense_shards is not None and self.device.type == "cuda":
+                self.dense_shards.reduce_scatter()
         if self.device.type == "cuda":
             sq = self._grad_sq_norm()
             norm = sq.sqrt() / nmb
@@ -234,14 +279,27 @@ class Trainer:
             for p in self.model.parameters():
                 if p.grad is not None:
                     p.grad.div_(nmb)
+            sharded = set()
+            dense_sq = torch.zeros((), dtype=torch.float64)
+            if self.dense_shards is not None:
+                # local gradients into the flat bucket, reduce-scatter, norm of the owned slices
+                for p in self.dense_shards.params:
+                    sharded.add(id(p))
+                    if p.grad is not None:
+                        p.main_grad.copy_(p.grad)
+                    else:
+                        p.main_grad.zero_()
+                self.dense_shards.reduce_scatter()
+                dense_sq = self.dense_shards.grad_shard.double().pow(2).sum()
+                dist.all_reduce(dense_sq)
             if self.world > 1:
                 for n, p in self.model.named_parameters():
-                    if p.grad is not None and not is_expert_param(n):
+                    if p.grad is not None and not is_expert_param(n) and id(p) not in sharded:
                         dist.all_reduce(p.grad)
             if cfg.max_grad_norm > 0:
                 # global norm: dense once, each logical expert once (owner copies)
-                dense_sq = sum(p.grad.double().pow(2).sum() for n, p in self.model.named_parameters()
-                               if p.grad is not None and not is_expert_param(n))
+                dense_sq = dense_sq + sum(p.grad.double().pow(2).sum() for n, p in self.model.named_parameters()
+                                          if p.grad is not None and not is_expert_param(n) and id(p) not in sharded)
                 exp_sq = torch.zeros((), dtype=torch.float64)
                 for blk in self.model.moe_blocks():
                     w = redundant_slot_weights(blk, blk.placement)
@@ -258,6 +316,8 @@ class Trainer:
                     for p in self.model.parameters():
                         if p.grad is not None:
                             p.grad.mul_(coef)
+                if self.dense_shards is not None:
+                    self.dense_shards.grad_scale = torch.tensor(coef, dtype=torch.float32)
         mult = self.lr_schedule.multiplier(self.global_step)
         for g in self.optimizer.param_groups:
             g.setdefault("initial_lr", g["lr"])
@@ -282,6 +342,8 @@ class Trainer:
                 g.zero_()
         if self.pstate.dense_bucket is not None:
             self.pstate.dense_bucket.zero()
+        if self.dense_shards is not None:
+            self.dense_shards.zero_grad()
         # expert gradients (the bulk) are overwritten by the step's first weight-gradient GEMM
         moe_ops.mark_grads_stale(self.model.expert_parameters())
 

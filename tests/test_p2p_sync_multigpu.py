@@ -107,3 +107,71 @@ def test_p2p_replica_sync_and_migration_match_nccl():
     for r, (e1, e2) in res.items():
         assert e1 < 1e-5, (r, e1)
         assert e2 == 0.0, (r, e2)
+
+
+def _trainer_worker(rank, world, port, out_q):
+    import torch.distributed as dist
+
+    os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
+                       "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank), "NCCL_NVLS_ENABLE": "0"})
+    torch.cuda.set_device(rank)
+    from datetime import timedelta
+
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from placemoe_b200.trainer.base import TrainConfig, Trainer
+
+        losses, diffs = {}, []
+        for mode in ("off", "auto"):  # replicated dense AdamW, then sharded dense (peer-memory RS / AG)
+            cfg = TrainConfig(model="small_qwen3_moe", seq_len=256, batch_per_rank=2, micro_batch_size=1, lr=1e-3,
+                              redundant_slots_per_rank=1, ep_transport="p2p", seed=0, dense_sharding=mode)
+            tr = Trainer(cfg)
+            assert (tr.dense_shards is not None) == (mode == "auto")
+            g = torch.Generator().manual_seed(100 + rank)  # different data per rank
+            losses[mode] = [tr.train_step(torch.randint(0, tr.model_cfg.vocab_size, (2, 256), generator=g))
+                            for _ in range(3)]
+            sync = getattr(tr.optimizer, "sync_params", None)
+            if sync is not None:
+                sync()
+            torch.cuda.synchronize()
+            # dense parameters must stay identical replicas across ranks
+            for name, p in tr.model.named_parameters():
+                if name.endswith(("gate_up_proj", "down_proj")):
+                    continue
+                ps = [torch.empty_like(p.data) for _ in range(world)]
+                dist.all_gather(ps, p.data.contiguous())
+                diffs.append((ps[0] - ps[1]).abs().max().item())
+            del tr
+        loss_gap = max(abs(a - b) / abs(a) for a, b in zip(losses["off"], losses["auto"]))
+        out_q.put((rank, max(diffs), loss_gap))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dense_replicas_stay_identical_with_peer_memory_ep():
+    """Different data per rank, peer-memory EP, replicated and sharded dense optimizer: dense weights must be
+    the same on every rank after steps, and both modes must train alike."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = free_port()
+    procs = [ctx.Process(target=_trainer_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    res = {}
+    while not q.empty():
+        r, d, gap = q.get()
+        res[r] = (d, gap)
+    assert len(res) == 2, res
+    for d, gap in res.values():
+        assert d == 0.0 and gap < 1e-3, res
