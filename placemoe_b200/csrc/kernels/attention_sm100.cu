@@ -599,8 +599,9 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 //   warps 2-9   two warpgroups; warp w owns TMEM lane quarter w % 4 (32 key rows, or
 //               32 query rows of dQ) and column group (w - 2) / 4 (64 queries, D / 2
 //               head dims), with packed f32x2 arithmetic:
-//               P^T = 2^(S^T c - lse) written bf16 into its own S^T columns (TMEM),
-//               dS^T = P^T (dP^T - delta) scale written to swizzled shared memory,
+//               per tile i: dS_i^T = P_i^T (dP_i^T - delta) scale to swizzled shared memory
+//               (P_i kept in registers as bf16 pairs), then P_{i+1}^T = 2^(S^T c - lse)
+//               written bf16 into its own S^T columns (TMEM) while dK_i / dQ_i run,
 //               dQ_i read from TMEM into fp32 staging boxes [128 queries x 32 dims]
 //               (128B-swizzled) that one thread per warpgroup adds to the fp32 dQ
 //               buffer with TMA reduce-adds.  Boxes 0-1 have their own 32 KB; boxes
@@ -622,11 +623,10 @@ constexpr int bwd_smem() {
 }
 
 // P = 2^(S c - lse) for 32 queries of one key row (column offset `rel` = key row - first
-// query, masked queries < key when MASK): bf16 pairs for TMEM and P * scale in f32x2 pairs.
+// query, masked queries < key when MASK), as bf16 pairs.
 template <bool MASK>
-PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, float scale, int rel,
-                         uint32_t* pk, uint64_t* ps) {
-  const uint64_t c2 = f2_pack(c, c), sc2 = f2_pack(scale, scale);
+PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, int rel, uint32_t* pk) {
+  const uint64_t c2 = f2_pack(c, c);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float4 l = lse4[j];
@@ -644,8 +644,6 @@ PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, 
     }
     pk[2 * j] = pack_bf16(e[0], e[1]);
     pk[2 * j + 1] = pack_bf16(e[2], e[3]);
-    ps[2 * j] = mul_f2(f2_pack(e[0], e[1]), sc2);
-    ps[2 * j + 1] = mul_f2(f2_pack(e[2], e[3]), sc2);
   }
 }
 
@@ -806,35 +804,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // A failed (bounded) wait only skips work: every thread still reaches the named barriers,
     // and the decision to stop is taken uniformly by all compute threads (bar.red.and).
     bool ok = true;
+    // P of tile j (64 queries of this group, bf16 pairs) -> TMEM (A operand of dV) and `pk`
+    // (kept for dS, since the next S^T MMA overwrites the TMEM copy).
+    uint32_t pk[32];
+    auto probs = [&](int j) {
+      const int st = j & 1;
+      const bool diag = kt + j % nqt == kt;
+      ok = ok && mbar_wait_abortable(&q_full[st], (j >> 1) & 1, s_abort) &&  // LSE rows visible
+           mbar_wait_abortable(s_full, j & 1, s_abort);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) return;
+      tc_fence_after();
+      const float4* lse4 = reinterpret_cast<const float4*>(sLse + st * 128 + cg * 64);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t sv[32];
+        const int q0 = cg * 64 + half * 32;
+        tmem_ld32(tA + lrow + q0, sv);
+        tmem_ld_wait();
+        if (diag) bwd_probs<true>(sv, lse4 + half * 8, c, r - q0, pk + half * 16);
+        else bwd_probs<false>(sv, lse4 + half * 8, c, 0, pk + half * 16);
+        // P^T bf16 over the group's own S^T columns (already read)
+        tmem_st16(tA + lrow + cg * 64 + half * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + half * 16));
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(p_done);
+    };
+    probs(0);
+    const uint64_t sc2 = f2_pack(a.scale, a.scale);
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / nqt;
       const int qt = kt + it % nqt;
       const int tq0 = b * a.S + qt * kTile;
       const int st = it & 1;
-      const float4* lse4 = reinterpret_cast<const float4*>(sLse + st * 128 + cg * 64);
       const float4* dl4 = reinterpret_cast<const float4*>(sDelta + st * 128 + cg * 64);
-      // q_full makes the LSE / delta rows of this stage visible to these threads
-      ok = ok && mbar_wait_abortable(&q_full[st], (it >> 1) & 1, s_abort) &&
-           mbar_wait_abortable(s_full, it & 1, s_abort);
-      ok = __all_sync(0xffffffffu, ok);
-      uint64_t ps[32];  // P * scale, pairs of queries
-      if (ok) {
-        tc_fence_after();
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t sv[32], pk[16];
-          const int q0 = cg * 64 + half * 32;
-          tmem_ld32(tA + lrow + q0, sv);
-          tmem_ld_wait();
-          if (qt == kt) bwd_probs<true>(sv, lse4 + half * 8, c, a.scale, r - q0, pk, ps + half * 16);
-          else bwd_probs<false>(sv, lse4 + half * 8, c, a.scale, 0, pk, ps + half * 16);
-          // P^T bf16 over the group's own S^T columns (already read)
-          tmem_st16(tA + lrow + cg * 64 + half * 16, pk);
-        }
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(p_done);
-      }
       // dS^T = P^T (dP^T - delta) * scale -> swizzled shared memory
       ok = ok && mbar_wait_abortable(dp_full, it & 1, s_abort);
       ok = __all_sync(0xffffffffu, ok);
@@ -853,13 +857,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const float4 d = dl4[half * 8 + j];
+            const uint32_t p01 = pk[half * 16 + 2 * j], p23 = pk[half * 16 + 2 * j + 1];
             const uint64_t t0 = add_f2(f2_pack(__uint_as_float(pv[4 * j]), __uint_as_float(pv[4 * j + 1])),
                                        f2_pack(-d.x, -d.y));
             const uint64_t t1 = add_f2(f2_pack(__uint_as_float(pv[4 * j + 2]), __uint_as_float(pv[4 * j + 3])),
                                        f2_pack(-d.z, -d.w));
             float u0, u1, u2, u3;
-            f2_unpack(mul_f2(ps[half * 16 + 2 * j], t0), u0, u1);
-            f2_unpack(mul_f2(ps[half * 16 + 2 * j + 1], t1), u2, u3);
+            f2_unpack(mul_f2(mul_f2(f2_pack(bf16_lo(p01), bf16_hi(p01)), sc2), t0), u0, u1);
+            f2_unpack(mul_f2(mul_f2(f2_pack(bf16_lo(p23), bf16_hi(p23)), sc2), t1), u2, u3);
             dsk[2 * j] = pack_bf16(u0, u1);
             dsk[2 * j + 1] = pack_bf16(u2, u3);
           }
@@ -874,6 +879,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_before();
         mbar_arrive(ds_done);
       }
+      // P of the next tile while the tensor pipe runs dK_i and dQ_i (S_{i+1} was issued after dV_i)
+      if (it + 1 < n_it) probs(it + 1);
       // dQ_i (rows = queries): TMEM -> registers (B released) -> staging boxes -> TMA reduce-add
       ok = ok && mbar_wait_abortable(dq_full, it & 1, s_abort);
       ok = __all_sync(0xffffffffu, ok);
