@@ -29,8 +29,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sq_norm_build_table", &pm::sq_norm_build_table);
   m.def("sq_norm", &pm::sq_norm);
   // attention
-  m.def("attn_fwd", &pm::attn_fwd);
-  m.def("attn_bwd", &pm::attn_bwd);
+  m.def("attn_fwd", &pm::attn_fwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("S"),
+        py::arg("doc_lo") = py::none());
+  m.def("attn_bwd", &pm::attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("dout"), py::arg("S"), py::arg("doc_hi") = py::none());
   // loss
   m.def("ce_fwd_bwd", &pm::ce_fwd_bwd);
   // peer-to-peer data plane

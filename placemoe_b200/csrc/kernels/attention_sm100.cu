@@ -1,7 +1,9 @@
 // Causal GQA flash attention on tcgen05 (sm_100a), forward and backward.
 //
 // Layout: q [T, Hq, D], k/v [T, Hkv, D], T = batch * seq_len, seq_len % 128 == 0,
-// D in {64, 128}.  Tiles are 128 queries x 128 keys.
+// D in {64, 128}.  Tiles are 128 queries x 128 keys.  Optionally each row of seq_len
+// tokens packs several documents: per-token document bounds mask keys of earlier
+// documents (forward: the query's document start; backward: the key's document end).
 //
 // Forward, one CTA per (batch, q head, 128-query tile), 192 threads:
 //   warp 0  TMA producer (Q once, K/V double-buffered)
@@ -62,6 +64,10 @@ struct AttnArgs {
   __nv_bfloat16* dk;   // [T, Hkv, D]
   __nv_bfloat16* dv;
   const float* lse_in;
+  // packed documents (optional): per token, the first position of its document and the
+  // position after its last token, both relative to the start of its row of seq_len tokens
+  const int* doc_lo;
+  const int* doc_hi;
 };
 
 // ---------------------------------------------------------------- forward
@@ -292,9 +298,9 @@ PM_DEVICE float exp2_poly(float x) {
 constexpr int kFwd2Threads = 320;
 constexpr int kPolyPer32 = 8;  // exponentials per 32 evaluated by exp2_poly
 
-// Row max of the raw scores of one 128-key S row in TMEM (keys > r masked when MASK).
+// Row max of the raw scores of one 128-key S row in TMEM (keys outside [lo, hi] masked when MASK).
 template <bool MASK>
-PM_DEVICE float srow_max(uint32_t t_s, int r) {
+PM_DEVICE float srow_max(uint32_t t_s, int lo, int hi) {
   float mraw = -INFINITY;
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
@@ -305,8 +311,8 @@ PM_DEVICE float srow_max(uint32_t t_s, int r) {
     if (MASK) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (half * 64 + i > r) v0[i] = __float_as_uint(-INFINITY);
-        if (half * 64 + 32 + i > r) v1[i] = __float_as_uint(-INFINITY);
+        if (half * 64 + i > hi || half * 64 + i < lo) v0[i] = __float_as_uint(-INFINITY);
+        if (half * 64 + 32 + i > hi || half * 64 + 32 + i < lo) v1[i] = __float_as_uint(-INFINITY);
       }
     }
 #pragma unroll
@@ -317,9 +323,10 @@ PM_DEVICE float srow_max(uint32_t t_s, int r) {
   return mraw;
 }
 
-// P = 2^(s c - m) of one S row -> bf16 into the swizzled P buffer; returns the row sum.
+// P = 2^(s c - m) of one S row -> bf16 into the swizzled P buffer (keys outside [lo, hi]
+// masked when MASK); returns the row sum.
 template <bool MASK>
-PM_DEVICE float srow_exp_store(uint32_t t_s, int r, float c, float m, uint8_t* myP) {
+PM_DEVICE float srow_exp_store(uint32_t t_s, int r, int lo, int hi, float c, float m, uint8_t* myP) {
   const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-m, -m);
   uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
@@ -333,8 +340,8 @@ PM_DEVICE float srow_exp_store(uint32_t t_s, int r, float c, float m, uint8_t* m
       float x0, x1;
       f2_unpack(fma_f2(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), c2, nm2), x0, x1);
       if (MASK) {
-        if (cc * 32 + i > r) x0 = -INFINITY;
-        if (cc * 32 + i + 1 > r) x1 = -INFINITY;
+        if (cc * 32 + i > hi || cc * 32 + i < lo) x0 = -INFINITY;
+        if (cc * 32 + i + 1 > hi || cc * 32 + i + 1 < lo) x1 = -INFINITY;
       }
       const float p0 = ((i >> 1) % (16 / kPolyPer32) == 0) ? exp2_poly(x0) : fast_exp2(x0);
       const float p1 = fast_exp2(x1);
@@ -491,12 +498,17 @@ __global__ void __launch_bounds__(kFwd2Threads, 1)
     const float c = a.scale * kLog2e;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
+    // first key of this row's document (packed sequences); 0 = the whole causal prefix
+    const int qlo = a.doc_lo ? a.doc_lo[tq0 + g * kTile + r] : 0;
     for (int j = 0; j < ng; ++j) {
       if (!mbar_wait_abortable(&s_full[g], j & 1, s_abort)) { ok = false; break; }
       tc_fence_after();
-      const bool masked = j == diag;
+      const int lo = qlo - j * kTile, hi = j == diag ? r : kTile - 1;
+      // warp-uniform choice: the row helpers issue warp-collective TMEM loads (a fully masked row
+      // keeps m = -inf and adds 0; rows without masking have lo <= 0 and hi = 127)
+      const bool masked = __any_sync(0xffffffffu, j == diag || lo > 0);
       // pass 1: row max (raw scores; the scale is positive)
-      const float mraw = masked ? srow_max<true>(t_s, r) : srow_max<false>(t_s, r);
+      const float mraw = masked ? srow_max<true>(t_s, lo, hi) : srow_max<false>(t_s, 0, kTile - 1);
       const float mx = mraw * c;
       float alpha = 1.0f;
       if (mx > m + 8.0f) {  // move the exponent base only when the max grew a lot
@@ -528,7 +540,8 @@ __global__ void __launch_bounds__(kFwd2Threads, 1)
         }
       }
       // pass 2: P = 2^(s c - m) -> bf16, swizzled into the A operand buffer
-      l += masked ? srow_exp_store<true>(t_s, r, c, m, myP) : srow_exp_store<false>(t_s, r, c, m, myP);
+      l += masked ? srow_exp_store<true>(t_s, r, lo, hi, c, m, myP)
+                  : srow_exp_store<false>(t_s, r, 0, kTile - 1, c, m, myP);
       fence_proxy_async_smem();
       tc_fence_before();
       mbar_arrive(&p_full[g]);
@@ -622,10 +635,11 @@ constexpr int bwd_smem() {
   return 5 * (D / 64) * 16384 + 32768 + 32768 + 2048 + 128;
 }
 
-// P = 2^(S c - lse) for 32 queries of one key row (column offset `rel` = key row - first
-// query, masked queries < key when MASK), as bf16 pairs.
+// P = 2^(S c - lse) for 32 queries of one key row, as bf16 pairs.  When MASK, query columns
+// outside [rel, rhi) are masked: rel = key - first query (causal), rhi = end of the key's
+// document - first query (packed sequences).
 template <bool MASK>
-PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, int rel, uint32_t* pk) {
+PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, int rel, int rhi, uint32_t* pk) {
   const uint64_t c2 = f2_pack(c, c);
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -640,7 +654,7 @@ PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, 
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       e[k] = fast_exp2(e[k]);
-      if (MASK && 4 * j + k < rel) e[k] = 0.f;
+      if (MASK && (4 * j + k < rel || 4 * j + k >= rhi)) e[k] = 0.f;
     }
     pk[2 * j] = pack_bf16(e[0], e[1]);
     pk[2 * j + 1] = pack_bf16(e[2], e[3]);
@@ -807,9 +821,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // P of tile j (64 queries of this group, bf16 pairs) -> TMEM (A operand of dV) and `pk`
     // (kept for dS, since the next S^T MMA overwrites the TMEM copy).
     uint32_t pk[32];
+    // end of this key's document (packed sequences), relative to the row of seq_len tokens
+    const int khi = a.doc_hi ? a.doc_hi[tk0 + r] : a.S;
     auto probs = [&](int j) {
       const int st = j & 1;
-      const bool diag = kt + j % nqt == kt;
+      const int qt_j = kt + j % nqt;
+      const bool diag = qt_j == kt;
       ok = ok && mbar_wait_abortable(&q_full[st], (j >> 1) & 1, s_abort) &&  // LSE rows visible
            mbar_wait_abortable(s_full, j & 1, s_abort);
       ok = __all_sync(0xffffffffu, ok);
@@ -822,8 +839,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         const int q0 = cg * 64 + half * 32;
         tmem_ld32(tA + lrow + q0, sv);
         tmem_ld_wait();
-        if (diag) bwd_probs<true>(sv, lse4 + half * 8, c, r - q0, pk + half * 16);
-        else bwd_probs<false>(sv, lse4 + half * 8, c, 0, pk + half * 16);
+        const int rhi = khi - (qt_j * kTile + q0);
+        if (diag || rhi < 32) bwd_probs<true>(sv, lse4 + half * 8, c, diag ? r - q0 : 0, rhi, pk + half * 16);
+        else bwd_probs<false>(sv, lse4 + half * 8, c, 0, 32, pk + half * 16);
         // P^T bf16 over the group's own S^T columns (already read)
         tmem_st16(tA + lrow + cg * 64 + half * 16, *reinterpret_cast<uint32_t(*)[16]>(pk + half * 16));
       }
@@ -1005,8 +1023,19 @@ static void check_qkv(const torch::Tensor& q, const torch::Tensor& k, const torc
 template <int D>
 static int fwd_smem() { return 1024 + (5 * (D / 64) * 16384) + 32768 + 256; }
 
-std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S) {
+// Per-token int32 positions of packed documents (see AttnArgs::doc_lo / doc_hi).
+static const int* doc_ptr(const c10::optional<torch::Tensor>& t, const torch::Tensor& q, const char* name) {
+  if (!t.has_value()) return nullptr;
+  TORCH_CHECK(t->is_cuda() && t->device() == q.device() && t->scalar_type() == torch::kInt32 &&
+                  t->is_contiguous() && t->numel() == q.size(0),
+              name, " must be a contiguous int32 CUDA tensor with one entry per token");
+  return t->data_ptr<int>();
+}
+
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S,
+                                    c10::optional<torch::Tensor> doc_lo) {
   check_qkv(q, k, v, S);
+  TORCH_CHECK(!doc_lo.has_value() || S % 256 == 0, "packed documents need seq_len % 256 == 0");
   c10::cuda::CUDAGuard guard(q.device());
   const int T = (int)q.size(0), Hq = (int)q.size(1), Hkv = (int)k.size(1), D = (int)q.size(2);
   auto o = torch::empty_like(q);
@@ -1018,6 +1047,7 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   a.scale = 1.f / sqrtf((float)D);
   a.o = (__nv_bfloat16*)o.data_ptr();
   a.lse = lse.data_ptr<float>();
+  a.doc_lo = doc_ptr(doc_lo, q, "doc_lo");
   CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v);
   auto stream = at::cuda::getCurrentCUDAStream();
   if (S % 256 == 0) {  // two query tiles per CTA
@@ -1049,7 +1079,8 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
 }
 
 std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dout, int64_t S) {
+                                    torch::Tensor lse, torch::Tensor dout, int64_t S,
+                                    c10::optional<torch::Tensor> doc_hi) {
   check_qkv(q, k, v, S);
   TORCH_CHECK(dout.is_contiguous() && dout.sizes() == q.sizes() && o.sizes() == q.sizes(), "dout / o layout");
   PM_CHECK_CUDA(o); PM_CHECK_CUDA(lse); PM_CHECK_CUDA(dout);
@@ -1074,6 +1105,7 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   a.dq_acc = dq_acc.data_ptr<float>();
   a.dk = (__nv_bfloat16*)dk.data_ptr();
   a.dv = (__nv_bfloat16*)dv.data_ptr();
+  a.doc_hi = doc_ptr(doc_hi, q, "doc_hi");
   // the kernel consumes the LSE in log2 units
   auto lse2 = (lse * kLog2e).contiguous();
   a.lse_in = lse2.data_ptr<float>();

@@ -50,9 +50,10 @@ std::vector<torch::Tensor> sq_norm_build_table(std::vector<torch::Tensor> grads,
 void sq_norm(torch::Tensor table, torch::Tensor meta, torch::Tensor out);
 
 // attention_sm100.cu
-std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S);
+std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S,
+                                    c10::optional<torch::Tensor> doc_lo);
 std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
-                                    torch::Tensor lse, torch::Tensor dout, int64_t S);
+                                    torch::Tensor lse, torch::Tensor dout, int64_t S, c10::optional<torch::Tensor> doc_hi);
 
 // loss.cu
 void ce_fwd_bwd(torch::Tensor logits, torch::Tensor labels, int64_t ignore_index, double grad_scale,

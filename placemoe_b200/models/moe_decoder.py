@@ -66,13 +66,13 @@ class Attention(nn.Module):
             self.q_group = self.k_group = 0
         self.register_buffer("inv_freq", norm_ops.rope_inv_freq(d, cfg.rope_theta), persistent=False)
 
-    def forward(self, x, pos, seq_len):
-        # x: [T, H] (T = batch * seq_len, packed by sequence)
+    def forward(self, x, pos, seq_len, docs=None):
+        # x: [T, H] (T = batch * seq_len, packed by sequence); docs: per-token document bounds
         qkv = mp_ops.linear(x, self.qkv_proj)
         q, k, v = norm_ops.qkv_norm_rope(qkv, self.q_norm, self.k_norm, pos, self.inv_freq, self.hq, self.hkv,
                                          self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps,
                                          max_pos=seq_len)
-        o = attn_ops.causal_attention(q, k, v, seq_len)  # [T, Hq, D]
+        o = attn_ops.causal_attention(q, k, v, seq_len, docs)  # [T, Hq, D]
         o = o.reshape(o.shape[0], -1)
         return mp_ops.linear(o, self.o_proj)
 
@@ -184,8 +184,8 @@ class DecoderLayer(nn.Module):
         self.post_attention_layernorm = RMSNorm(cfg.hidden_size, cfg.rms_norm_eps)
         self.mlp = DenseMLP(cfg) if cfg.is_dense else MoEBlock(cfg, layer_idx, num_local_slots)
 
-    def forward(self, x, pos, seq_len):
-        x = x + self.self_attn(self.input_layernorm(x), pos, seq_len)
+    def forward(self, x, pos, seq_len, docs=None):
+        x = x + self.self_attn(self.input_layernorm(x), pos, seq_len, docs)
         x = x + self.mlp(self.post_attention_layernorm(x))
         return x
 
@@ -254,27 +254,40 @@ class MoEForCausalLM(nn.Module):
             self._grad_anchor = a
         return a
 
-    def hidden_states(self, input_ids: torch.Tensor) -> torch.Tensor:
+    def hidden_states(self, input_ids: torch.Tensor, cu_seqlens: torch.Tensor | None = None) -> torch.Tensor:
+        """``cu_seqlens``: cumulative document boundaries over the flattened tokens when rows pack
+        several documents (positions restart and attention stays inside each document)."""
         b, s = input_ids.shape
         ids = input_ids.reshape(-1)
         x = mp_ops.embedding(ids, self.embed_tokens, self._anchor(ids.device))
-        pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)
+        docs = None
+        if cu_seqlens is None:
+            pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)
+        else:
+            docs = attn_ops.doc_bounds(cu_seqlens.to(ids.device), b * s, s)
+            pos = (torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b) - docs[0]).to(torch.int32)
         for layer in self.layers:
             if self.gradient_checkpointing and self.training:
-                x = torch.utils.checkpoint.checkpoint(layer, x, pos, s, use_reentrant=False)
+                x = torch.utils.checkpoint.checkpoint(layer, x, pos, s, docs, use_reentrant=False)
             else:
-                x = layer(x, pos, s)
+                x = layer(x, pos, s, docs)
         return self.norm(x)
 
-    def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, loss_denom=None):
-        """Returns (loss, aux_loss) with labels, else logits [B, S, V]."""
-        h = self.hidden_states(input_ids)
+    def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, loss_denom=None,
+                cu_seqlens: torch.Tensor | None = None):
+        """Returns (loss, aux_loss) with labels, else logits [B, S, V].  With ``cu_seqlens`` the last
+        token of a document predicts nothing (no loss across document boundaries)."""
+        h = self.hidden_states(input_ids, cu_seqlens)
         w = self.embed_tokens if self.lm_head is None else self.lm_head
         if labels is None:
             logits = mp_ops.linear(h, w)
             return logits.reshape(*input_ids.shape, -1)
         shifted = torch.full_like(labels, loss_ops.IGNORE_INDEX)
         shifted[:, :-1] = labels[:, 1:]
+        if cu_seqlens is not None:
+            ends = cu_seqlens.to(labels.device).long()[1:] - 1  # last token of every document
+            flat = shifted.view(-1)
+            flat[ends] = loss_ops.IGNORE_INDEX
         loss = loss_ops.fused_linear_cross_entropy(h, w, shifted, denom=loss_denom)
         aux = None
         for blk in self.moe_blocks():

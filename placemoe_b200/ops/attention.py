@@ -1,4 +1,4 @@
-"""Causal GQA attention over packed fixed-length sequences.
+"""Causal GQA attention over packed fixed-length sequences, optionally with several documents per row.
 
 q: [T, Hq, D], k/v: [T, Hkv, D] with T = batch * seq_len (token-major, as
 produced by the fused QKV-norm-RoPE kernel).  Returns [T, Hq, D].
@@ -21,7 +21,28 @@ import torch.nn.functional as F
 from ._ext import kernels
 
 
-def attention_reference(q, k, v, seq_len):
+def doc_bounds(cu_seqlens: torch.Tensor, num_tokens: int, seq_len: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-token (first position, end position) of its document, relative to its row of seq_len tokens.
+
+    ``cu_seqlens`` holds the cumulative document boundaries over the flattened tokens
+    (first entry 0, last entry ``num_tokens``); every row boundary must also be a document
+    boundary.  Returns two int32 tensors of ``num_tokens`` entries.
+    """
+    cu = cu_seqlens.to(torch.int64)
+    if cu[0].item() != 0 or cu[-1].item() != num_tokens:
+        raise ValueError("cu_seqlens must start at 0 and end at the token count")
+    lens = cu[1:] - cu[:-1]
+    if (lens <= 0).any():
+        raise ValueError("documents must be non-empty")
+    starts = torch.repeat_interleave(cu[:-1], lens)
+    ends = torch.repeat_interleave(cu[1:], lens)
+    row0 = torch.arange(num_tokens, device=cu.device) // seq_len * seq_len
+    if ((ends - 1) // seq_len != starts // seq_len).any():
+        raise ValueError("a document crosses a row of seq_len tokens")
+    return (starts - row0).to(torch.int32), (ends - row0).to(torch.int32)
+
+
+def attention_reference(q, k, v, seq_len, docs=None):
     t, hq, d = q.shape
     hkv = k.shape[1]
     b = t // seq_len
@@ -33,6 +54,11 @@ def attention_reference(q, k, v, seq_len):
         vf = vf.repeat_interleave(hq // hkv, dim=1)
     s = (qf @ kf.transpose(-1, -2)) / math.sqrt(d)
     mask = torch.ones(seq_len, seq_len, dtype=torch.bool, device=q.device).tril()
+    if docs is not None:  # keys of earlier documents are masked: key >= first position of the query's document
+        lo = docs[0].to(q.device).long().reshape(b, seq_len)
+        keys = torch.arange(seq_len, device=q.device)
+        mask = mask[None] & (keys[None, None, :] >= lo[:, :, None])  # [b, q, k]
+        mask = mask[:, None]
     s = s.masked_fill(~mask, float("-inf"))
     o = torch.softmax(s, dim=-1) @ vf
     return o.transpose(1, 2).reshape(t, hq, d).to(q.dtype)
@@ -44,24 +70,30 @@ def _has_kernel() -> bool:
 
 class _FlashAttn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, seq_len):
-        o, lse = kernels().attn_fwd(q, k, v, seq_len)
+    def forward(ctx, q, k, v, seq_len, doc_lo, doc_hi):
+        o, lse = kernels().attn_fwd(q, k, v, seq_len, doc_lo)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.seq_len = seq_len
+        ctx.doc_hi = doc_hi
         return o
 
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = kernels().attn_bwd(q, k, v, o, lse, do.contiguous(), ctx.seq_len)
-        return dq, dk, dv, None
+        dq, dk, dv = kernels().attn_bwd(q, k, v, o, lse, do.contiguous(), ctx.seq_len, ctx.doc_hi)
+        return dq, dk, dv, None, None, None
 
 
-def causal_attention(q, k, v, seq_len: int):
+def causal_attention(q, k, v, seq_len: int, docs=None):
+    """``docs``: optional (doc_lo, doc_hi) int32 per-token document bounds (:func:`doc_bounds`)
+    for rows that pack several documents; attention then stays inside each document."""
     if not q.is_cuda:
-        return attention_reference(q, k, v, seq_len)
+        return attention_reference(q, k, v, seq_len, docs)
     if _has_kernel():
-        return _FlashAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), seq_len)
+        lo, hi = (None, None) if docs is None else (docs[0].contiguous(), docs[1].contiguous())
+        return _FlashAttn.apply(q.contiguous(), k.contiguous(), v.contiguous(), seq_len, lo, hi)
+    if docs is not None:
+        raise RuntimeError("packed documents need the attention kernel")
     # Interim path until the tcgen05 attention kernel is part of the build.
     t, hq, d = q.shape
     hkv = k.shape[1]

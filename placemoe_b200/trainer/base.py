@@ -67,6 +67,7 @@ class TrainConfig:
     ep_transport: str = "auto"
     recompute_expert_rows: bool = False  # drop dispatched expert inputs after forward, re-gather in backward  # "auto" | "p2p" | "nccl"
     gradient_checkpointing: bool = False
+    activation_offload: bool = False  # saved activations to pinned host memory (utils/offload.py)
     device: str = "cuda"
     log_interval: int = 10
     output_dir: str = ""
@@ -207,20 +208,38 @@ class Trainer:
         return out
 
     # ------------------------------------------------------------------- step
-    def forward_backward(self, input_ids: torch.Tensor) -> torch.Tensor:
-        loss, aux = self.model(input_ids, labels=input_ids)
+    def forward_backward(self, input_ids: torch.Tensor, cu_seqlens: torch.Tensor | None = None) -> torch.Tensor:
+        from ..utils.offload import ActivationOffload
+
+        with ActivationOffload(enabled=self.cfg.activation_offload and self.device.type == "cuda"):
+            if cu_seqlens is None:
+                loss, aux = self.model(input_ids, labels=input_ids)
+            else:
+                loss, aux = self.model(input_ids, labels=input_ids, cu_seqlens=cu_seqlens)
         total = loss / self.world
         if aux is not None:
             total = total + aux / self.world
         total.backward()
         return loss.detach()
 
-    def train_step(self, input_ids: torch.Tensor, *, read_loss: bool = True):
-        """One optimizer step over ``input_ids`` [batch_per_rank, seq] (host or device tensor)."""
+    def train_step(self, input_ids: torch.Tensor, *, read_loss: bool = True, cu_seqlens: torch.Tensor | None = None):
+        """One optimizer step over ``input_ids`` [batch_per_rank, seq] (host or device tensor).
+
+        ``cu_seqlens`` (packed rows): cumulative document boundaries over the flattened tokens;
+        every row boundary is a document boundary (``data.pack_documents``).
+        """
         cfg = self.cfg
         ids = input_ids.to(self.device, non_blocking=True)
         mb = max(1, cfg.micro_batch_size)
         n_micro = max(1, ids.shape[0] // mb)
+        cus = [None] * n_micro
+        if cu_seqlens is not None:  # split the document boundaries by micro-batch
+            cu = cu_seqlens.to(torch.int64).cpu()
+            seq = ids.shape[1]
+            for i in range(n_micro):
+                lo, hi = i * mb * seq, (i + 1) * mb * seq
+                part = cu[(cu >= lo) & (cu <= hi)] - lo
+                cus[i] = part.to(torch.int32).to(self.device)
         ep = self.pstate.ep
         rsync = self.replica_sync
         for attempt in range(4):
@@ -228,7 +247,10 @@ class Trainer:
             for i in range(n_micro):
                 if rsync is not None:  # replicas are reduced during the last micro-batch's backward
                     rsync.armed = i == n_micro - 1
-                losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+                if cus[i] is None:
+                    losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb]))
+                else:
+                    losses.append(self.forward_backward(ids[i * mb:(i + 1) * mb], cus[i]))
             if rsync is not None:
                 rsync.armed = False
             if not hasattr(ep, "check_capacity"):

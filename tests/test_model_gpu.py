@@ -80,3 +80,27 @@ def test_dense_model_matches_cpu_reference():
         gg = dict(gpu.named_parameters())[name].main_grad.float().cpu()
         rel = ((gg - gc).norm() / (gc.norm() + 1e-12)).item()
         assert rel < 0.08, f"{name}: relative grad error {rel:.3f}"
+
+
+def test_activation_offload_is_transparent():
+    """Saved activations through pinned host memory: same loss and gradients as keeping them on the GPU."""
+    from placemoe_b200.models.config import get_preset
+    from placemoe_b200.models.moe_decoder import build_model
+    from placemoe_b200.utils.offload import ActivationOffload
+
+    cfg = get_preset("small_qwen3_moe")
+    torch.manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (2, 256), device="cuda")
+    grads = []
+    for offload in (False, True):
+        model = build_model(cfg, device="cuda", seed=3)
+        with ActivationOffload(min_bytes=1 << 16, enabled=offload) as ctx:
+            loss, aux = model(ids, labels=ids)
+        (loss + aux).backward()
+        if offload:
+            assert ctx.offloaded_bytes > 0
+        grads.append((loss.item(), model.layers[0].self_attn.qkv_proj.main_grad.clone()))
+    assert abs(grads[0][0] - grads[1][0]) < 1e-4 * abs(grads[0][0])
+    # dQ accumulates with unordered fp32 reduce-adds: runs agree to rounding, not bit for bit
+    diff = (grads[0][1] - grads[1][1]).norm() / grads[0][1].norm()
+    assert diff.item() < 1e-3
