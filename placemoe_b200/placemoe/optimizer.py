@@ -4,9 +4,9 @@
 
     for every replica-allocation candidate (grouped / greedy / top-demand):
         instance statistics <- uniform split of the logical statistics
-        for round in rounds:
+        for each layout/mapping alternation:
             placement candidates (partition of instances onto GPUs)
-            for each placement: fresh mapping (greedy init) and, from round 2,
+            for each placement: fresh mapping (greedy init) and, from the second alternation on,
                 the carried mapping of the incumbent, each refined by the
                 coordinate-descent core
             every candidate is scored by the exact route-replay evaluator;
