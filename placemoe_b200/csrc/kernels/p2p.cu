@@ -10,8 +10,9 @@
 //   p2p_put_words  scatter 32-bit words (int32 / fp32 metadata) to peers
 //   p2p_barrier    one CTA: release-store this rank's epoch into every peer's flag
 //                  word, then acquire-wait until every peer's epoch reached ours.
-//                  Bounded: after the budget the kernel records kErrPeerTimeout and
-//                  returns (the host raises); it never traps or spins forever.
+//                  Bounded (wall-clock budget): on timeout it records kErrPeerTimeout
+//                  in the sticky status block and returns; later waits then return
+//                  at once and the host raises at the step's status read.
 //   p2p_sum_f32    sum fp32 buffers read from several peers (replica-gradient reduction)
 //   p2p_pull       bulk copy from one peer's buffer (expert-state migration)
 //
@@ -27,19 +28,11 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "peer.cuh"
 
 namespace pm {
 
 constexpr int kMaxPeers = 64;
-
-PM_DEVICE void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-PM_DEVICE unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // rows: warp per item, H multiple of 8 (16-byte vectors)
 __global__ void __launch_bounds__(256) p2p_put_rows_kernel(const __nv_bfloat16* __restrict__ src, int H,
@@ -88,24 +81,8 @@ __global__ void p2p_allgather_words_kernel(const unsigned* __restrict__ vals, in
 }
 
 __global__ void p2p_barrier_kernel(const long long* __restrict__ peers, long long flags_off, int my_rank, int world,
-                                   unsigned epoch, long long budget) {
-  const int r = threadIdx.x;
-  if (r < world) {
-    __threadfence_system();
-    unsigned* remote = reinterpret_cast<unsigned*>(peers[r] + flags_off) + my_rank;
-    st_release_sys(remote, epoch);
-  }
-  __syncthreads();
-  if (r < world) {
-    const unsigned* mine = reinterpret_cast<const unsigned*>(peers[my_rank] + flags_off) + r;
-    const long long start = clock64();
-    while ((int)(ld_acquire_sys(mine) - epoch) < 0) {
-      if (clock64() - start > budget) {
-        set_error(kErrPeerTimeout);
-        break;
-      }
-    }
-  }
+                                   unsigned epoch, long long budget_ns, int* __restrict__ st) {
+  peer_barrier_threads(peers, flags_off, my_rank, world, epoch, budget_ns, st, kWaitBarrier);
   __syncthreads();
 }
 
@@ -213,14 +190,15 @@ void p2p_allgather_words(torch::Tensor vals, torch::Tensor peers, int64_t region
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s) {
-  PM_CHECK_CUDA(peers);
+void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s,
+                 torch::Tensor status) {
+  PM_CHECK_CUDA(peers); PM_CHECK_CUDA(status);
   TORCH_CHECK(peers.numel() <= kMaxPeers && my_rank < peers.numel(), "peer table");
+  TORCH_CHECK(status.scalar_type() == torch::kInt32 && status.numel() >= 4, "status: int32[4]");
   c10::cuda::CUDAGuard guard(peers.device());
-  const long long budget = (long long)(timeout_s * 2.0e9);  // cycles at ~2 GHz
   p2p_barrier_kernel<<<1, 64, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const long long*>(peers.data_ptr<int64_t>()), flags_off, (int)my_rank, (int)peers.numel(),
-      (unsigned)epoch, budget);
+      (unsigned)epoch, (long long)(timeout_s * 1e9), status.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -66,7 +66,8 @@ void p2p_put_rows(torch::Tensor src, c10::optional<torch::Tensor> src_row, torch
 void p2p_put_words(torch::Tensor vals, torch::Tensor dst_rank, torch::Tensor dst_idx, c10::optional<torch::Tensor> n_dev,
                    int64_t n_host, torch::Tensor peers, int64_t region_off);
 void p2p_allgather_words(torch::Tensor vals, torch::Tensor peers, int64_t region_off, int64_t my_rank);
-void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s);
+void p2p_barrier(torch::Tensor peers, int64_t flags_off, int64_t my_rank, int64_t epoch, double timeout_s,
+                 torch::Tensor status);
 void p2p_reduce_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor ranks, int64_t region_off);
 void p2p_sum_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor src_rank, torch::Tensor src_off);
 void p2p_pull(torch::Tensor dst, torch::Tensor peers, int64_t src_rank, int64_t region_off);

@@ -58,13 +58,53 @@ def available() -> bool:
         return False
 
 
+_P2P_STATUS: dict = {}
+
+# identifiers of the wait that gave up first (status word 1, see csrc/kernels/peer.cuh)
+_WAIT_NAMES = {1: "p2p barrier", 2: "grid barrier", 3: "dispatch count exchange", 4: "dispatch rows",
+               5: "combine partial sums", 6: "backward scatter"}
+_ERROR_NAMES = {1: "mbarrier wait timed out", 2: "peer wait timed out", 3: "bounds check failed", 4: "bad arguments"}
+
+
+def p2p_status(device) -> "torch.Tensor":
+    """Sticky status block (int32[4]) shared by every peer-memory kernel on ``device``.
+
+    Word 0 is the first error code (0 = ok), word 1 the wait that gave up, word 2
+    the largest received row count seen.  Once word 0 is set, every later peer
+    wait returns at once, so a missing peer costs one time budget per process.
+    """
+    import torch
+
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    st = _P2P_STATUS.get(dev)
+    if st is None:
+        st = torch.zeros(4, dtype=torch.int32, device=dev)
+        _P2P_STATUS[dev] = st
+    return st
+
+
 def device_error(reset: bool = True) -> int:
     """Error word written by bounded device waits / checks (0 = no error)."""
-    return int(kernels().device_error(reset))
+    code = int(kernels().device_error(reset))
+    for st in _P2P_STATUS.values():
+        v = int(st[0].item())
+        if v and not code:
+            code = v
+        if reset and v:
+            st[:2].zero_()
+    return code
 
 
 def check_device_error() -> None:
+    """Raise if any kernel recorded an error since the last check (one small device read per source)."""
+    where = ""
+    for st in _P2P_STATUS.values():
+        w = st[:2].tolist()
+        if w[0]:
+            where = f" (first failed wait: {_WAIT_NAMES.get(w[1], w[1])})"
+            break
     code = device_error(reset=True)
     if code:
-        names = {1: "mbarrier wait timed out", 2: "peer wait timed out", 3: "bounds check failed", 4: "bad arguments"}
-        raise RuntimeError(f"placemoe_b200 kernel reported error {code}: {names.get(code, 'unknown')}")
+        raise RuntimeError(f"placemoe_b200 kernel reported error {code}: {_ERROR_NAMES.get(code, 'unknown')}{where}")

@@ -39,6 +39,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from ..ops import moe as moe_ops
+from ..ops import p2p_status
 
 BARRIER_TIMEOUT_S = 30.0
 
@@ -108,7 +109,8 @@ class SymmetricArena:
 
     def barrier(self):
         self.epoch += 1
-        moe_ops.kernels().p2p_barrier(self.peers, self.layout["flags"], self.rank, self.epoch, BARRIER_TIMEOUT_S)
+        moe_ops.kernels().p2p_barrier(self.peers, self.layout["flags"], self.rank, self.epoch, BARRIER_TIMEOUT_S,
+                                      p2p_status(self.buf.device))
 
     def fits(self, tokens: int, k: int, hidden: int) -> bool:
         return tokens <= self.tokens and k == self.k and hidden == self.hidden

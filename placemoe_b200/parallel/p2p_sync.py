@@ -31,9 +31,10 @@ import torch
 import torch.distributed as dist
 
 from ..ops import moe as moe_ops
+from ..ops import p2p_status
 
 FLAGS_BYTES = 256
-BARRIER_TIMEOUT_S = 60.0
+BARRIER_TIMEOUT_S = 20.0
 
 
 def _align(n: int, a: int = 256) -> int:
@@ -78,13 +79,22 @@ class PeerExchange:
         return self.buf[FLAGS_BYTES:].view(dtype)
 
     def barrier(self) -> None:
+        """Bounded device barrier over every rank of the group (each rank must call it equally often)."""
         self.epoch += 1
-        moe_ops.kernels().p2p_barrier(self.peers, 0, self.rank, self.epoch, BARRIER_TIMEOUT_S)
+        moe_ops.kernels().p2p_barrier(self.peers, 0, self.rank, self.epoch, BARRIER_TIMEOUT_S,
+                                      p2p_status(self.device))
 
 
 # ---------------------------------------------------------------- replica gradients
 class _LayerSyncPlan:
-    """Static per-layer schedule: which local slots to stage, which sums to compute."""
+    """Static per-layer schedule: which local slots to stage, which sums to compute.
+
+    ``active`` is a property of the layer, the same on every rank: a layer with
+    any replicated expert runs the exchange (and both of its barriers) on every
+    rank of the group, also on a rank that holds none of the copies.  Barriers
+    count arrivals over the whole group, so a rank that skipped one would leave
+    its peers waiting.
+    """
 
     def __init__(self, placement, device):
         spr = placement.slots_per_rank
@@ -92,7 +102,9 @@ class _LayerSyncPlan:
         self.version = placement.version
         self.stage: list[int] = []
         self.sums: list[tuple[int, torch.Tensor, torch.Tensor]] = []  # (local slot, src ranks, src slot ids)
-        for slots in placement.replica_groups():
+        groups = placement.replica_groups()
+        self.active = len(groups) > 0
+        for slots in groups:
             members = [(int(s) // spr, int(s) % spr) for s in slots.tolist()]
             mine = [j for (r, j) in members if r == rank]
             if not mine:
@@ -129,7 +141,7 @@ class ReplicaGradSync:
         if not self.armed:
             return
         plan = self._plan(blk)
-        if not plan.sums:
+        if not plan.active:  # no replicated expert in this layer on any rank
             return
         ready = torch.cuda.Event()
         ready.record()

@@ -29,6 +29,7 @@ import torch.distributed as dist
 
 from ..models.config import MoEModelConfig, get_preset
 from ..models.moe_decoder import build_model
+from ..ops import check_device_error
 from ..ops import moe as moe_ops
 from ..ops import mp as mp_ops
 from ..optim import build_lr_scheduler, build_optimizer
@@ -257,6 +258,10 @@ class Trainer:
                 break
             try:
                 ep.check_capacity()  # one host read per step: did any rank overflow its expert buffers?
+                if self.device.type == "cuda":
+                    # a peer wait that ran out (sticky status) or a kernel check: raise now, not
+                    # after further steps on stale data
+                    check_device_error()
                 break
             except EPCapacityExceeded:
                 if attempt == 3:
@@ -272,7 +277,12 @@ class Trainer:
         self.global_step += 1
         if self.hot_update is not None:
             self.hot_update.on_step_end(self)
-        return float(loss.item()) if read_loss else loss
+        if not read_loss:
+            return loss
+        value = float(loss.item())
+        if self.device.type == "cuda" and not hasattr(ep, "check_capacity"):
+            check_device_error()  # the loss read already synchronised: one more small read
+        return value
 
     def optimizer_step(self):
         cfg = self.cfg

@@ -275,3 +275,36 @@ def test_attention_packed_documents(d, hq, hkv):
 
     torch.cuda.synchronize()
     check_device_error()
+
+
+@pytest.mark.gpu
+def test_peer_barrier_times_out_and_status_is_sticky():
+    """A bounded peer wait that runs out: one GPU, a two-entry peer table whose second flag is never
+    written.  The kernel returns an error status (no trap); a later wait returns at once; the host raises."""
+    import time
+
+    from placemoe_b200.ops import check_device_error, kernels, p2p_status
+
+    kn = kernels()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    st = p2p_status(dev)
+    check_device_error()  # start clean
+    flags = torch.zeros(64, dtype=torch.int32, device=dev)
+    peers = torch.tensor([flags.data_ptr(), flags.data_ptr()], dtype=torch.int64, device=dev)
+    t0 = time.perf_counter()
+    kn.p2p_barrier(peers, 0, 0, 1, 0.3, st)
+    torch.cuda.synchronize()
+    first = time.perf_counter() - t0
+    assert st.tolist()[:2] == [2, 1]  # peer wait timed out, in the p2p barrier
+    t1 = time.perf_counter()
+    kn.p2p_barrier(peers, 0, 0, 2, 5.0, st)  # sticky: returns without waiting out its budget
+    torch.cuda.synchronize()
+    second = time.perf_counter() - t1
+    assert 0.25 < first < 5.0, first
+    assert second < 1.0, second
+    with pytest.raises(RuntimeError, match="peer wait timed out"):
+        check_device_error()
+    assert st.tolist()[0] == 0
+    # the context stays usable
+    x = torch.ones(1024, device=dev)
+    assert float(x.sum()) == 1024.0

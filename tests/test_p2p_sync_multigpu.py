@@ -1,6 +1,9 @@
-"""Peer-memory replica-gradient reduction and migration transfers vs their NCCL counterparts (2 GPUs).
+"""Peer-memory replica-gradient reduction and migration transfers vs their NCCL counterparts (2 and 4 GPUs).
 
-Runs as 2 child processes, one per GPU, with NVLS disabled; skipped on fewer than 2 GPUs.
+Runs as child processes, one per GPU, with NVLS disabled; each case is skipped when the
+machine has fewer GPUs than it needs.  The 4-rank trainer case uses a placement in which
+only ranks 0 and 1 hold replicated experts: ranks 2 and 3 still take part in every
+replica-gradient barrier.
 """
 
 import os
@@ -109,7 +112,31 @@ def test_p2p_replica_sync_and_migration_match_nccl():
         assert e2 == 0.0, (r, e2)
 
 
-def _trainer_worker(rank, world, port, out_q):
+def partial_replica_artifact(path, cfg, world):
+    """Artifact for every layer: fixed EP plus one replica on rank 1 (of rank 0's first expert) and one on
+    rank 0 (of rank 1's first expert); the extra slots of the other ranks stay empty."""
+    import numpy as np
+
+    from placemoe_b200.parallel.data_parallel import expert_topology
+    from placemoe_b200.placemoe.artifacts import build_placemoe_artifact, write_artifact
+    from placemoe_b200.placemoe.types import LayerPlan, identity_plan
+
+    topo = expert_topology(cfg.num_experts, world, 1)
+    base = identity_plan(topo)
+    spr = topo.slots_per_rank
+    per = -(-cfg.num_experts // world)
+    layout = np.array(base.slot_to_logical)
+    mapping = np.array(base.source_logical_to_physical)
+    layout[2 * spr - 1] = 0  # rank 1's extra slot: expert 0 (owned by rank 0)
+    layout[spr - 1] = per  # rank 0's extra slot: expert `per` (owned by rank 1)
+    mapping[1, 0] = 2 * spr - 1
+    mapping[0, per] = spr - 1
+    plan = LayerPlan(layout, mapping, np.array(base.owner_slots))
+    plans = {f"model.layers.{i}.mlp.experts": plan for i in range(cfg.num_hidden_layers)}
+    write_artifact(build_placemoe_artifact(plans, topo), path)
+
+
+def _trainer_worker(rank, world, port, out_q, artifact=""):
     import torch.distributed as dist
 
     os.environ.update({"MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port), "RANK": str(rank),
@@ -125,12 +152,22 @@ def _trainer_worker(rank, world, port, out_q):
         losses, diffs = {}, []
         for mode in ("off", "auto"):  # replicated dense AdamW, then sharded dense (peer-memory RS / AG)
             cfg = TrainConfig(model="small_qwen3_moe", seq_len=256, batch_per_rank=2, micro_batch_size=1, lr=1e-3,
-                              redundant_slots_per_rank=1, ep_transport="p2p", seed=0, dense_sharding=mode)
+                              redundant_slots_per_rank=1, ep_transport="p2p", seed=0, dense_sharding=mode,
+                              placemoe_artifact=artifact)
             tr = Trainer(cfg)
+            if artifact:  # replicas on ranks 0 and 1 only: every rank still runs the layer's sync
+                assert tr.replica_sync is not None
             assert (tr.dense_shards is not None) == (mode == "auto")
             g = torch.Generator().manual_seed(100 + rank)  # different data per rank
             losses[mode] = [tr.train_step(torch.randint(0, tr.model_cfg.vocab_size, (2, 256), generator=g))
                             for _ in range(3)]
+            if artifact:  # copies of one expert on ranks 0 and 1 must have stayed identical
+                w = tr.model.moe_blocks()[0].gate_up_proj.data.contiguous()
+                ws = [torch.empty_like(w) for _ in range(world)]
+                dist.all_gather(ws, w)
+                spr = w.shape[0]
+                diffs.append((ws[0][spr - 1] - ws[1][0]).abs().max().item())
+                diffs.append((ws[1][spr - 1] - ws[0][0]).abs().max().item())
             sync = getattr(tr.optimizer, "sync_params", None)
             if sync is not None:
                 sync()
@@ -141,7 +178,7 @@ def _trainer_worker(rank, world, port, out_q):
                     continue
                 ps = [torch.empty_like(p.data) for _ in range(world)]
                 dist.all_gather(ps, p.data.contiguous())
-                diffs.append((ps[0] - ps[1]).abs().max().item())
+                diffs.append(max((ps[0] - q).abs().max().item() for q in ps[1:]))
             del tr
         loss_gap = max(abs(a - b) / abs(a) for a, b in zip(losses["off"], losses["auto"]))
         out_q.put((rank, max(diffs), loss_gap))
@@ -149,17 +186,13 @@ def _trainer_worker(rank, world, port, out_q):
         dist.destroy_process_group()
 
 
-def test_dense_replicas_stay_identical_with_peer_memory_ep():
-    """Different data per rank, peer-memory EP, replicated and sharded dense optimizer: dense weights must be
-    the same on every rank after steps, and both modes must train alike."""
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_trainer_case(world, artifact=""):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
     port = free_port()
-    procs = [ctx.Process(target=_trainer_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_trainer_worker, args=(r, world, port, q, artifact)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -172,6 +205,26 @@ def test_dense_replicas_stay_identical_with_peer_memory_ep():
     while not q.empty():
         r, d, gap = q.get()
         res[r] = (d, gap)
-    assert len(res) == 2, res
+    assert len(res) == world, res
     for d, gap in res.values():
         assert d == 0.0 and gap < 1e-3, res
+
+
+def test_dense_replicas_stay_identical_with_peer_memory_ep():
+    """Different data per rank, peer-memory EP, replicated and sharded dense optimizer: dense weights must be
+    the same on every rank after steps, and both modes must train alike."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    _run_trainer_case(2)
+
+
+def test_four_ranks_uneven_replica_membership(tmp_path):
+    """4 ranks, replicas held by ranks 0 and 1 only, dense sharding on and off: training completes (no
+    barrier waits out), dense replicas stay identical and both dense modes agree."""
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    from placemoe_b200.models.config import get_preset
+
+    path = str(tmp_path / "partial_replicas.json")
+    partial_replica_artifact(path, get_preset("small_qwen3_moe"), 4)
+    _run_trainer_case(4, path)
