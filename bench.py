@@ -42,9 +42,14 @@ def parse():
     p.add_argument("--model", default="olmoe_1b_7b")
     p.add_argument("--seq", type=int, default=4096)
     p.add_argument("--batch-per-gpu", type=int, default=8)
-    p.add_argument("--micro-batch", type=int, default=4)
+    p.add_argument("--micro-batch", type=int, default=0,
+                   help="sequences per micro-batch (default 4; 2 for qwen3_30b_a3b)")
     p.add_argument("--redundant-slots", type=int, default=-1,
-                   help="extra expert slots per GPU for replicas (default: 1 when N > 1, else 0)")
+                   help="extra expert slots per GPU for replicas (default when N > 1: 4 for qwen3_30b_a3b, "
+                        "else 1; 0 on one GPU)")
+    p.add_argument("--placement", default="placemoe", choices=("placemoe", "fixed_ep", "eplb"),
+                   help="N > 1: PlaceMoE L,M planned from captured routes, plain EP, or EPLB-style replication "
+                        "from the captured demand")
     p.add_argument("--plan-steps", type=int, default=-1,
                    help="steps of captured routes the PlaceMoE planner uses before timing (default: 20 when N > 1)")
     p.add_argument("--artifact", default="")
@@ -136,6 +141,7 @@ def plan_placement(trainer, pool, args, rank, world):
     cfg = trainer.model_cfg
     t0 = time.perf_counter()
     payload = [None]
+    report = [None]
     if rank == 0:
         out = os.path.join(root, "layout.json")
         plan_placemoe.main([
@@ -144,7 +150,10 @@ def plan_placement(trainer, pool, args, rank, world):
             "--redundant-slots-per-rank", str(args.redundant_slots), "--hidden-size", str(cfg.hidden_size),
             "--layers", str(cfg.num_hidden_layers), "--workers", str(min(8, os.cpu_count() or 1)),
             "--output-layout", out, "--output-report", os.path.join(root, "report.json"),
+            "--emit", "eplb" if args.placement == "eplb" else "placemoe",
         ])
+        with open(os.path.join(root, "report.json")) as f:
+            report[0] = json.load(f)["aggregate"]
         with open(out) as f:
             payload[0] = json.load(f)
     dist.broadcast_object_list(payload, src=0)
@@ -157,8 +166,13 @@ def plan_placement(trainer, pool, args, rank, world):
     trainer._norm_table = None
     trainer.optimizer.reset_tables()
     dist.barrier()
+    agg = report[0] or {}
     return {"plan_steps": args.plan_steps, "planner_ms": round(planner_ms, 1),
-            "install_ms": round((time.perf_counter() - t1) * 1e3, 1), "moved_slots": moved}
+            "install_ms": round((time.perf_counter() - t1) * 1e3, 1), "moved_slots": moved,
+            "emitted": args.placement,
+            "modelled_speedup_vs_fixed_ep": (round(agg["validation_speedup"], 3)
+                                             if agg.get("validation_speedup") else None),
+            "mean_dedup_ratio": round(agg.get("mean_dedup_ratio", 0.0), 3)}
 
 
 def run_reference(args):
@@ -189,10 +203,15 @@ def main():
     rank, world = init_distributed()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    big = args.model == "qwen3_30b_a3b"
+    if args.micro_batch <= 0:
+        args.micro_batch = 2 if big else 4
+    if args.placement == "fixed_ep":
+        args.redundant_slots = 0
     if args.redundant_slots < 0:
-        args.redundant_slots = 1 if world > 1 else 0
+        args.redundant_slots = (4 if big else 1) if world > 1 else 0
     if args.plan_steps < 0:
-        args.plan_steps = 20 if world > 1 and not args.artifact else 0
+        args.plan_steps = 20 if world > 1 and not args.artifact and args.placement != "fixed_ep" else 0
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     overrides = {"num_hidden_layers": args.layers} if args.layers else {}
@@ -248,10 +267,25 @@ def main():
     barrier()
     ms_e2e = s2.elapsed_time(e2) / args.steps
 
-    t = torch.tensor([ms, ms_e2e], device="cuda")
+    # ---- exposed all-to-all: one more step with CUDA events around every EP communication kernel.
+    # Those kernels run on the compute stream, so their summed time is the exposed a2a time per step.
+    a2a = {}
+    from placemoe_b200.parallel import p2p_ep
+
+    if world > 1 and isinstance(trainer.pstate.ep, p2p_ep.P2PExpertParallel):
+        barrier()
+        p2p_ep.TIMER = p2p_ep.PhaseTimer()
+        trainer.train_step(dev_batches[0], read_loss=False)
+        barrier()
+        a2a = p2p_ep.TIMER.phases()
+        p2p_ep.TIMER = None
+    names = ["dispatch", "combine", "scatter", "combine_bwd"]
+    t = torch.tensor([ms, ms_e2e, sum(a2a.values())] + [a2a.get(n, 0.0) for n in names], device="cuda")
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e2e = t.tolist()
+    vals = t.tolist()
+    ms, ms_e2e, a2a_ms = vals[:3]
+    a2a_phases = dict(zip(names, (round(v, 3) for v in vals[3:])))
     tokens = args.batch_per_gpu * args.seq * world
     value = tokens / (ms / 1e3)
     e2e = tokens / (ms_e2e / 1e3)
@@ -278,8 +312,10 @@ def main():
                 "micro_batch": args.micro_batch,
                 "parallelism": f"dp{world}+ep{world}" + ("+dense-shard" if trainer.dense_shards is not None else ""),
                 "ep_transport": args.ep_transport if world > 1 else "none",
-                "placement": (f"PlaceMoE static L,M planned from {args.plan_steps} captured steps, "
-                              f"{args.redundant_slots} replica slot(s)/GPU" if plan_info else
+                "placement": ((f"PlaceMoE static L,M planned from {args.plan_steps} captured steps, "
+                               if args.placement == "placemoe" else
+                               f"EPLB-style replication from {args.plan_steps} captured steps, ")
+                              + f"{args.redundant_slots} replica slot(s)/GPU" if plan_info else
                               ("artifact " + args.artifact if args.artifact else
                                ("fixed EP" if world > 1 else "single GPU"))),
                 "router_bias": f"{mcfg.router_bias_scale} * log Zipf(s={mcfg.router_bias_zipf_s})",
@@ -289,6 +325,8 @@ def main():
             "clocks": clocks,
             "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": pool.bytes_per_batch,
                     "d2h_bytes_per_step": 4, "ms_per_step": round(ms_e2e, 3), "last_loss": last},
+            "exposed_a2a_ms_per_step": round(a2a_ms, 3) if world > 1 and a2a else None,
+            "a2a_phases_ms_per_step": a2a_phases if world > 1 and a2a else None,
             "gpu_launches": launches,
             "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 2**30, 1),
             "planner": plan_info,

@@ -43,5 +43,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_reduce_f32", &pm::p2p_reduce_f32);
   m.def("p2p_sum_f32", &pm::p2p_sum_f32);
   m.def("p2p_pull", &pm::p2p_pull);
+  // fused expert-parallel dispatch / combine (one cooperative kernel per phase)
+  m.def("ep_scratch_ints", &pm::ep_scratch_ints);
+  m.def("ep_dispatch", &pm::ep_dispatch);
+  m.def("ep_combine", &pm::ep_combine);
+  m.def("ep_scatter", &pm::ep_scatter);
   m.def("device_error", &pm::device_error, "read (and optionally clear) the kernels' error words");
 }

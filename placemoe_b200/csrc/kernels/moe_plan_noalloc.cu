@@ -13,15 +13,15 @@
 // this one writes into buffers the caller already owns and keeps its scratch
 // in a fixed device array compiled into the library.
 //
-//   int pm_moe_plan_noalloc(const int* idx, const int* lut, const float* weights,
-//                           int n, int k, int num_slots, int capacity, int align,
-//                           int* offsets, int* counts, int* row_of, int* row_token,
-//                           float* row_scale, cudaStream_t stream);
+//   The exported prototypes and return codes are declared in csrc/pm_noalloc.h.
 //
 // Inputs and outputs have the meaning and shapes of `moe_plan`:
 //   idx [n] int32 (n = tokens * k, top-k expert ids), lut optional (logical ->
 //   slot), weights optional fp32 [n]; outputs offsets [num_slots + 1],
 //   counts [num_slots], row_of [n], row_token [capacity], row_scale [capacity].
+//   The padded segments end at offsets[num_slots] <= n + num_slots * (align - 1), and
+//   the kernels write row_token / row_scale up to that row, so a capacity below that
+//   bound is rejected with PM_NOALLOC_BAD_ARGS before anything is launched.
 // Returns 0 on success, otherwise a nonzero code (see pm_moe_plan_noalloc_error).
 //
 // Limits: the scratch array holds kNoAllocScratchInts = 262144 int32 (1 MiB) of
@@ -31,9 +31,13 @@
 //
 // Set-up: the first call on a device looks up the device address of the
 // scratch array with cudaGetSymbolAddress (with that device current) and
-// caches it per device.  Make that first call before any stream capture on the
-// device.  Every device that loads the library holds the 1 MiB array until the
-// process exits.
+// caches it per device ordinal.  Make that first call before any stream capture
+// on the device.  Every device that loads the library holds the 1 MiB array
+// until the process exits.  The address belongs to the device's primary
+// context (the one the CUDA runtime uses): use the entry point from the
+// runtime's primary context only, and not after cudaDeviceReset() on that
+// device, which destroys the context the cached address refers to.  The
+// first-call look-up is serialised by a mutex, so threads may race to make it.
 //
 // Sharing: all calls on one device share the one scratch array, and the array
 // keeps the contents of the last call.  The count kernel writes every scratch
@@ -44,7 +48,10 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "common.cuh"
+#include "pm_noalloc.h"
 
 namespace pm {
 // Kernels of the allocating entry point (moe_route.cu), reused unchanged.
@@ -73,14 +80,7 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchInts];
 
 int* g_scratch_ptr[kMaxDevices] = {nullptr};
-
-enum : int {
-  PM_NOALLOC_OK = 0,
-  PM_NOALLOC_BAD_ARGS = 1,
-  PM_NOALLOC_TOO_LARGE = 2,
-  PM_NOALLOC_SYMBOL = 3,
-  PM_NOALLOC_LAUNCH = 4,
-};
+std::mutex g_scratch_mu;
 
 thread_local const char* g_last_error = "ok";
 
@@ -117,16 +117,23 @@ int pm_moe_plan_noalloc(const int* idx, const int* lut, const float* weights, in
   if ((long long)nblocks * num_slots > kNoAllocScratchInts)
     return fail(PM_NOALLOC_TOO_LARGE,
                 "request exceeds the fixed scratch: ceil(n / 2048) * num_slots must be <= 262144");
+  // the padded plan ends at offsets[num_slots] <= n + num_slots * (align - 1)
+  if ((long long)capacity < (long long)n + (long long)num_slots * (align - 1))
+    return fail(PM_NOALLOC_BAD_ARGS, "capacity below n + num_slots * (align - 1) rows");
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(PM_NOALLOC_SYMBOL, "cudaGetDevice failed or device index out of range");
-  if (g_scratch_ptr[dev] == nullptr) {
-    void* ptr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || ptr == nullptr) return fail(PM_NOALLOC_SYMBOL, "cudaGetSymbolAddress(scratch) failed");
-    g_scratch_ptr[dev] = static_cast<int*>(ptr);
+  int* block_counts = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+      if (e != cudaSuccess || ptr == nullptr) return fail(PM_NOALLOC_SYMBOL, "cudaGetSymbolAddress(scratch) failed");
+      g_scratch_ptr[dev] = static_cast<int*>(ptr);
+    }
+    block_counts = g_scratch_ptr[dev];
   }
-  int* block_counts = g_scratch_ptr[dev];
   // cudaLaunchKernel reports the status of each launch itself, independent of any
   // error state left in the runtime by earlier, unrelated calls of the process.
   {

@@ -72,6 +72,20 @@ void p2p_reduce_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor ranks,
 void p2p_sum_f32(torch::Tensor out, torch::Tensor peers, torch::Tensor src_rank, torch::Tensor src_off);
 void p2p_pull(torch::Tensor dst, torch::Tensor peers, int64_t src_rank, int64_t region_off);
 
+// fused expert-parallel dispatch / combine over peer memory (ep_fused.cu)
+int64_t ep_scratch_ints(int64_t world, int64_t slots);
+void ep_dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w, torch::Tensor dest_tab, torch::Tensor slot_tab,
+                 torch::Tensor peers, std::vector<int64_t> geo, torch::Tensor scratch, torch::Tensor status,
+                 int64_t epoch, double timeout_s, torch::Tensor pos, torch::Tensor dst, torch::Tensor offsets,
+                 torch::Tensor row_scale);
+void ep_combine(torch::Tensor rows, c10::optional<torch::Tensor> dscale, torch::Tensor pos, torch::Tensor dst,
+                torch::Tensor offsets, torch::Tensor peers, std::vector<int64_t> geo, torch::Tensor scratch,
+                torch::Tensor status, int64_t epoch, double timeout_s, torch::Tensor out,
+                c10::optional<torch::Tensor> dw_out);
+void ep_scatter(torch::Tensor dy, torch::Tensor pos, torch::Tensor dst, torch::Tensor offsets, torch::Tensor peers,
+                std::vector<int64_t> geo, torch::Tensor scratch, torch::Tensor status, int64_t epoch,
+                double timeout_s);
+
 int device_error(bool reset);
 }  // namespace pm
 

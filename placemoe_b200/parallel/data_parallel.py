@@ -145,7 +145,10 @@ def parallelize_model(model, *, plans=None, topology: PlaceMoETopology | None = 
             ep = P2PExpertParallel(group, capture_routes=capture_routes)
         else:
             ep = ExpertParallel(group, capture_routes=capture_routes)
-    for blk in model.moe_blocks():
+    if ep is not None and hasattr(ep, "num_layers"):
+        ep.num_layers = len(keys)  # one receive slab per MoE layer in the peer-memory arena
+    for i, blk in enumerate(model.moe_blocks()):
+        blk.ep_slab = i
         if blk.num_local_slots != topology.slots_per_rank:
             raise ValueError(f"{blk.layer_key} holds {blk.num_local_slots} slots, topology needs "
                              f"{topology.slots_per_rank}")

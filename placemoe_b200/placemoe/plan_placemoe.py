@@ -64,6 +64,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--compute-ms-per-assignment", type=float, default=None)
     p.add_argument("--compute-phase-multiplier", type=float, default=None)
     p.add_argument("--comparison-layout", default="fixed-ep", help="'none', 'fixed-ep', 'eplb' or an artifact path")
+    p.add_argument("--emit", choices=("placemoe", "eplb"), default="placemoe",
+                   help="'eplb': write the EPLB-style replication seed instead of the optimised plan "
+                        "(comparison runs)")
     p.add_argument("--rounds", type=int, default=2)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--output-layout", required=True)
@@ -115,15 +118,23 @@ def plan_layer(job: dict) -> dict:
     ev_opt = RouteReplayEvaluator(opt, topo, hidden_size=job["hidden"], bytes_per_element=job["bpe"], calibration=cal)
     ev_val = RouteReplayEvaluator(val, topo, hidden_size=job["hidden"], bytes_per_element=job["bpe"], calibration=cal)
     cfg = OptimizerConfig(rounds=job["rounds"], seed=job["seed"])
-    if job["mode"] == "mapping":
-        current = LayerPlan.from_runtime_payload(job["input_plan"])
-        res = optimize_fixed_layout_mapping(stats, topo, current, ev_opt, cfg)
+    if job.get("emit") == "eplb":
+        from .optimizer import OptimizerCandidate as Candidate
+
+        plan = eplb_plan(topo, stats.demand)
+        best = Candidate(plan, ev_opt.evaluate(plan), "eplb")
+        vcost, n_cand = ev_val.evaluate(plan), 1
     else:
-        res = optimize_replica_allocation(stats, topo, ev_opt, cfg)
-    # held-out selection among the candidates (best few by optimisation cost)
-    ranked = sorted(res.candidates, key=lambda c: c.cost.total_ms)[:8]
-    scored = [(ev_val.evaluate(c.plan), c) for c in ranked]
-    vcost, best = min(scored, key=lambda r: (r[0].total_ms, r[1].label))
+        if job["mode"] == "mapping":
+            current = LayerPlan.from_runtime_payload(job["input_plan"])
+            res = optimize_fixed_layout_mapping(stats, topo, current, ev_opt, cfg)
+        else:
+            res = optimize_replica_allocation(stats, topo, ev_opt, cfg)
+        # held-out selection among the candidates (best few by optimisation cost)
+        ranked = sorted(res.candidates, key=lambda c: c.cost.total_ms)[:8]
+        scored = [(ev_val.evaluate(c.plan), c) for c in ranked]
+        vcost, best = min(scored, key=lambda r: (r[0].total_ms, r[1].label))
+        n_cand = len(res.candidates)
     comparison = None
     if job["comparison"] == "fixed-ep":
         try:
@@ -139,7 +150,7 @@ def plan_layer(job: dict) -> dict:
         "optimize_cost_ms": best.cost.total_ms, "validation_cost_ms": vcost.total_ms,
         "validation_comm_ms": vcost.comm_ms, "validation_compute_ms": vcost.compute_ms,
         "dedup_ratio": vcost.dedup_ratio, "comparison_cost_ms": comparison,
-        "candidates": len(res.candidates), "wall_ms": (time.perf_counter() - t0) * 1e3,
+        "candidates": n_cand, "wall_ms": (time.perf_counter() - t0) * 1e3,
     }
 
 
@@ -179,7 +190,7 @@ def main(argv=None) -> int:
             "hidden": args.hidden_size, "bpe": args.bytes_per_element, "rounds": args.rounds, "seed": args.seed,
             "mode": args.update_mode, "threads": args.worker_threads,
             "input_plan": input_plans[key].to_runtime_payload() if key in input_plans else None,
-            "comparison": args.comparison_layout,
+            "comparison": args.comparison_layout, "emit": args.emit,
             "comparison_plan": comparison_plans[key].to_runtime_payload() if key in comparison_plans else None,
         })
         if args.update_mode == "mapping" and key not in input_plans:

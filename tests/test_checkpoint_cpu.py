@@ -84,3 +84,35 @@ def test_hf_export_load_roundtrip_single_process(tmp_path):
     load_hf_weights(tr2, out)
     for (n, a), (_, b) in zip(tr.model.named_parameters(), tr2.model.named_parameters()):
         assert torch.allclose(a.bfloat16().float(), b, atol=0, rtol=0), n
+
+
+def _digest_worker(rank, world, workdir):
+    """Rank 1's placement digest is replaced by a fake that disagrees: every rank must refuse the load
+    before any tensor is read, and the model must keep its pre-load values."""
+    import pytest
+
+    from placemoe_b200.checkpoint import checkpointer, load_checkpoint, save_checkpoint
+
+    torch.manual_seed(0)
+    b = torch.randint(0, 1024, (2, 64), generator=torch.Generator().manual_seed(rank))
+    tr = _trainer()
+    tr.train_step(b)
+    path = save_checkpoint(tr, os.path.join(workdir, "ckpt"))
+    tr2 = _trainer()
+    before = {n: p.detach().clone() for n, p in tr2.model.named_parameters()}
+    if rank == 1:
+        real = checkpointer.placement_digest
+        checkpointer.placement_digest = lambda trainer: real(trainer) + 1
+    try:
+        with pytest.raises(RuntimeError, match="differs across ranks"):
+            load_checkpoint(tr2, path)
+    finally:
+        if rank == 1:
+            checkpointer.placement_digest = real
+    for n, p in tr2.model.named_parameters():
+        assert torch.equal(p.detach(), before[n]), n
+    assert tr2.global_step == 0
+
+
+def test_checkpoint_digest_mismatch_refused_on_every_rank(tmp_path):
+    run_distributed(_digest_worker, 2, str(tmp_path))

@@ -80,3 +80,23 @@ def test_noalloc_rejects_requests_beyond_scratch():
                                  _ptr(dummy), _ptr(dummy), _ptr(dummy), ctypes.c_void_p(0))
     assert rc == 2
     assert b"scratch" in lib.pm_moe_plan_noalloc_error()
+
+
+def test_noalloc_rejects_too_small_capacity():
+    """The padded plan can end at n + num_slots * (align - 1) rows: a smaller capacity is refused before
+    any launch, and the caller's buffers stay untouched."""
+    lib = _lib()
+    t, k, slots, align = 300, 4, 16, 128
+    n = t * k
+    cap = n + slots * (align - 1) - 1
+    idx = torch.randint(0, slots, (t, k), device="cuda", dtype=torch.int32)
+    outs = (torch.full((slots + 1,), -7, dtype=torch.int32, device="cuda"),
+            torch.full((slots,), -7, dtype=torch.int32, device="cuda"),
+            torch.full((n,), -7, dtype=torch.int32, device="cuda"),
+            torch.full((cap,), -7, dtype=torch.int32, device="cuda"),
+            torch.full((cap,), -7.0, dtype=torch.float32, device="cuda"))
+    rc = _call(lib, idx, None, None, slots, cap, align, outs)
+    torch.cuda.synchronize()
+    assert rc == 1
+    assert b"capacity" in lib.pm_moe_plan_noalloc_error()
+    assert all(bool((o == -7).all()) for o in outs)
