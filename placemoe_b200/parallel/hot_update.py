@@ -38,10 +38,9 @@ import torch.distributed as dist
 
 from ..placemoe.artifacts import build_placemoe_artifact, validate_placemoe_artifact, write_artifact
 from ..placemoe.runtime.config import PlaceMoERuntimeConfig
-from ..placemoe.runtime.controller import HotUpdateController
 from ..placemoe.runtime.planner_process import (HotUpdateJob, PlannerCommandSpec, build_planner_command,
                                                 default_planner_path, planner_environment, python_executable)
-from ..placemoe.runtime.scheduler import UpdateKind
+from ..placemoe.runtime.scheduler import HotUpdateController, UpdateKind
 from ..placemoe.types import EMPTY_EXPERT, LayerPlan
 from .migration import migrate_layer
 from .route_capture import RouteRecorder

@@ -26,30 +26,36 @@ PLACEMOE_ARTIFACT_SCHEMA_VERSION = 2
 ALGORITHM = "placemoe-v1"
 
 
+class ArtifactError(ValueError):
+    """A schema-v2 artifact that cannot be installed."""
+
+
+def _require(ok: bool, problem: str) -> None:
+    if not ok:
+        raise ArtifactError(f"PlaceMoE artifact rejected: {problem}")
+
+
+def _topology_row(topology: PlaceMoETopology) -> dict[str, int]:
+    return {"ep_size": topology.ep_size, "ranks_per_node": topology.ranks_per_node,
+            "num_experts": topology.num_experts, "num_physical_slots": topology.total_slots,
+            "slots_per_rank": topology.slots_per_rank}
+
+
 def build_placemoe_artifact(plans: Mapping[str, LayerPlan], topology: PlaceMoETopology, *,
                             source: Mapping[str, Any] | None = None) -> dict[str, Any]:
-    if not plans:
-        raise ValueError("A PlaceMoE artifact must contain at least one layer plan.")
-    layers = {}
-    for name, plan in plans.items():
-        if not name:
-            raise ValueError("Layer names must be non-empty.")
+    """The artifact for ``plans`` (every plan checked against ``topology``) -- validated before it is returned."""
+    _require(bool(plans), "no layer plans")
+    _require(all(isinstance(k, str) and k for k in plans), "every layer needs a non-empty name")
+    for plan in plans.values():
         plan.validate(topology)
-        layers[name] = plan.to_runtime_payload()
-    src = dict(source or {})
-    src.update({"algorithm": ALGORITHM, "initial_layout": "preloaded", "requires_static_preload": True})
+    provenance = {**dict(source or {}), "algorithm": ALGORITHM, "initial_layout": "preloaded",
+                  "requires_static_preload": True}
     payload = {
         "schema_version": PLACEMOE_ARTIFACT_SCHEMA_VERSION,
-        "source": src,
-        "topology": {
-            "ep_size": topology.ep_size,
-            "ranks_per_node": topology.ranks_per_node,
-            "num_experts": topology.num_experts,
-            "num_physical_slots": topology.total_slots,
-            "slots_per_rank": topology.slots_per_rank,
-        },
+        "source": provenance,
+        "topology": _topology_row(topology),
         "replay": {"actions_by_step": {"1": []}},
-        "layers": layers,
+        "layers": {name: plan.to_runtime_payload() for name, plan in plans.items()},
     }
     validate_placemoe_artifact(payload)
     return payload
@@ -57,36 +63,35 @@ def build_placemoe_artifact(plans: Mapping[str, LayerPlan], topology: PlaceMoETo
 
 def artifact_topology(payload: Mapping[str, Any]) -> PlaceMoETopology:
     row = payload.get("topology")
-    if not isinstance(row, Mapping):
-        raise ValueError("PlaceMoE artifact is missing its topology.")
-    topo = PlaceMoETopology(
-        ep_size=int(row["ep_size"]),
-        ranks_per_node=int(row.get("ranks_per_node", row["ep_size"])),
-        num_experts=int(row["num_experts"]),
-        slots_per_rank=int(row["slots_per_rank"]),
-    )
-    if int(row.get("num_physical_slots", -1)) != topo.total_slots:
-        raise ValueError("Artifact physical-slot count does not match its topology.")
+    _require(isinstance(row, Mapping), "no topology object")
+    try:
+        topo = PlaceMoETopology(ep_size=int(row["ep_size"]),
+                                ranks_per_node=int(row.get("ranks_per_node", row["ep_size"])),
+                                num_experts=int(row["num_experts"]), slots_per_rank=int(row["slots_per_rank"]))
+    except KeyError as missing:
+        raise ArtifactError(f"PlaceMoE artifact rejected: topology lacks {missing}") from None
+    declared = int(row.get("num_physical_slots", -1))
+    _require(declared == topo.total_slots,
+             f"topology declares {declared} physical slots, its sizes give {topo.total_slots}")
     return topo
 
 
 def validate_placemoe_artifact(payload: Mapping[str, Any]) -> dict[str, LayerPlan]:
-    if int(payload.get("schema_version", -1)) != PLACEMOE_ARTIFACT_SCHEMA_VERSION:
-        raise ValueError("Unsupported PlaceMoE artifact schema version.")
-    src = payload.get("source")
-    if not isinstance(src, Mapping) or src.get("algorithm") != ALGORITHM:
-        raise ValueError("Artifact was not produced by the PlaceMoE optimizer.")
+    """Every layer plan of a schema-v2 artifact, each checked against the artifact's topology."""
+    version = payload.get("schema_version")
+    _require(version == PLACEMOE_ARTIFACT_SCHEMA_VERSION,
+             f"schema_version {version!r}, this reader understands {PLACEMOE_ARTIFACT_SCHEMA_VERSION}")
+    provenance = payload.get("source")
+    _require(isinstance(provenance, Mapping) and provenance.get("algorithm") == ALGORITHM,
+             f"source.algorithm must be {ALGORITHM!r}")
     topo = artifact_topology(payload)
-    rows = payload.get("layers")
-    if not isinstance(rows, Mapping) or not rows:
-        raise ValueError("PlaceMoE artifact must contain a non-empty layer table.")
+    layers = payload.get("layers")
+    _require(isinstance(layers, Mapping) and len(layers) > 0, "empty or missing layer table")
     plans = {}
-    for name, row in rows.items():
-        if not isinstance(name, str) or not isinstance(row, Mapping):
-            raise ValueError("PlaceMoE layer entries must map names to plan objects.")
-        plan = LayerPlan.from_runtime_payload(dict(row))
-        plan.validate(topo)
-        plans[name] = plan
+    for name, row in layers.items():
+        _require(isinstance(name, str) and isinstance(row, Mapping), f"layer entry {name!r} is not a plan object")
+        plans[name] = LayerPlan.from_runtime_payload(dict(row))
+        plans[name].validate(topo)
     return plans
 
 

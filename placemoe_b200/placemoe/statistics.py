@@ -25,69 +25,68 @@ from .types import EMPTY_EXPERT, ProfileStatistics
 
 
 def profile_route_statistics(samples: Sequence[Sequence], *, num_experts: int) -> ProfileStatistics:
-    if not samples or not samples[0]:
-        raise ValueError("At least one routing sample and source rank are required.")
-    if num_experts <= 0:
-        raise ValueError("num_experts must be positive.")
-    ep = len(samples[0])
-    demand = torch.zeros(ep, num_experts, dtype=torch.float64)
-    affinity = torch.zeros(ep, num_experts, num_experts, dtype=torch.float64)
+    if num_experts < 1:
+        raise ValueError(f"num_experts must be >= 1, got {num_experts}")
+    if len(samples) == 0 or len(samples[0]) == 0:
+        raise ValueError("route statistics need at least one step with at least one source GPU")
+    gpus = len(samples[0])
+    demand = torch.zeros(gpus, num_experts, dtype=torch.float64)
+    affinity = torch.zeros(gpus, num_experts, num_experts, dtype=torch.float64)
     core = load_planner()
-    for sample in samples:
-        if len(sample) != ep:
-            raise ValueError("All routing samples must contain the same source ranks.")
-        for s, route in enumerate(sample):
-            r = torch.as_tensor(route)
-            if r.ndim != 2 or r.shape[1] <= 0:
-                raise ValueError("Each route tensor must have shape [tokens, top_k].")
-            core.accumulate_route_stats(r.detach().cpu().to(torch.int64).contiguous(), s, demand, affinity)
+    for step, sample in enumerate(samples):
+        if len(sample) != gpus:
+            raise ValueError(f"step {step} has routes of {len(sample)} GPUs, step 0 of {gpus}")
+        for src, route in enumerate(sample):
+            ids = torch.as_tensor(route)
+            if ids.dim() != 2 or ids.shape[1] == 0:
+                raise ValueError(f"step {step}, GPU {src}: routes are [tokens, top_k], got {tuple(ids.shape)}")
+            core.accumulate_route_stats(ids.detach().to("cpu", torch.int64).contiguous(), src, demand, affinity)
     return ProfileStatistics(demand=demand.numpy(), affinity=affinity.numpy())
 
 
-def _copy_counts(copy_to_expert: np.ndarray, num_experts: int) -> np.ndarray:
-    if (copy_to_expert < EMPTY_EXPERT).any() or (copy_to_expert >= num_experts).any():
-        raise ValueError("copy_to_expert contains an invalid logical expert ID.")
-    counts = np.bincount(copy_to_expert[copy_to_expert >= 0], minlength=num_experts)
-    if (counts < 1).any():
-        raise ValueError("Every logical expert must retain at least one physical copy.")
+def _copies_per_expert(copy_to_expert: np.ndarray, num_experts: int) -> np.ndarray:
+    """Copies of each expert in a copy -> expert table (-1 = empty copy); every expert needs one."""
+    bad = (copy_to_expert < EMPTY_EXPERT) | (copy_to_expert >= num_experts)
+    if bad.any():
+        raise ValueError(f"copy table holds ids outside [-1, {num_experts}): {copy_to_expert[bad][:4].tolist()}")
+    counts = np.bincount(copy_to_expert[copy_to_expert != EMPTY_EXPERT], minlength=num_experts)
+    if counts.min(initial=1) == 0:
+        raise ValueError(f"experts without a copy: {np.flatnonzero(counts == 0)[:8].tolist()}")
     return counts
 
 
 def uniform_copy_statistics(stats: ProfileStatistics, copy_to_expert) -> tuple[np.ndarray, np.ndarray]:
+    """Statistics per copy when every copy of an expert takes an equal share (no mapping yet)."""
     c2e = np.asarray(copy_to_expert, dtype=np.int64)
-    counts = _copy_counts(c2e, stats.num_experts)
-    n = len(c2e)
-    act = np.flatnonzero(c2e >= 0)
-    demand = np.zeros((stats.ep_size, n))
-    demand[:, act] = stats.demand[:, c2e[act]] / counts[c2e[act]][None, :]
-    affinity = np.zeros((stats.ep_size, n, n))
-    ea = c2e[act]
-    sub = stats.affinity[:, ea][:, :, ea] / (counts[ea][:, None] * counts[ea][None, :])[None]
-    same = ea[:, None] == ea[None, :]
-    sub[:, same] = 0.0
-    affinity[np.ix_(np.arange(stats.ep_size), act, act)] = sub
+    counts = _copies_per_expert(c2e, stats.num_experts)
+    live = np.flatnonzero(c2e != EMPTY_EXPERT)
+    experts = c2e[live]
+    share = 1.0 / counts[experts]
+    demand = np.zeros((stats.ep_size, len(c2e)))
+    demand[:, live] = stats.demand[:, experts] * share[None, :]
+    pair = stats.affinity[:, experts[:, None], experts[None, :]] * np.outer(share, share)[None]
+    pair[:, experts[:, None] == experts[None, :]] = 0.0  # copies of one expert are never co-selected
+    affinity = np.zeros((stats.ep_size, len(c2e), len(c2e)))
+    affinity[:, live[:, None], live[None, :]] = pair
     return demand, affinity
 
 
 def project_statistics_to_copies(stats: ProfileStatistics, copy_to_expert, mapping) -> tuple[np.ndarray, np.ndarray]:
+    """Statistics per copy when GPU r sends expert e's tokens to copy ``mapping[r, e]``."""
     c2e = np.asarray(copy_to_expert, dtype=np.int64)
     m = np.asarray(mapping, dtype=np.int64)
-    _copy_counts(c2e, stats.num_experts)
+    _copies_per_expert(c2e, stats.num_experts)
     if m.shape != (stats.ep_size, stats.num_experts):
-        raise ValueError("mapping must have shape [source_rank, logical_expert].")
-    if (m < 0).any() or (m >= len(c2e)).any():
-        raise ValueError("mapping references an unavailable physical copy.")
-    if not np.array_equal(c2e[m], np.broadcast_to(np.arange(stats.num_experts), m.shape)):
-        raise ValueError("mapping references a copy of the wrong logical expert.")
+        raise ValueError(f"mapping is [gpu, expert] = {(stats.ep_size, stats.num_experts)}, got {m.shape}")
+    if ((m < 0) | (m >= len(c2e))).any() or not (c2e[m] == np.arange(stats.num_experts)[None, :]).all():
+        raise ValueError("mapping must point every (gpu, expert) at a copy of that expert")
     n = len(c2e)
     demand = np.zeros((stats.ep_size, n))
     affinity = np.zeros((stats.ep_size, n, n))
-    for s in range(stats.ep_size):
-        sel = m[s]
-        np.add.at(demand[s], sel, stats.demand[s])
-        # affinity between the copies chosen for (i, j); P^T A P with P the selection matrix
-        p = np.zeros((stats.num_experts, n))
-        p[np.arange(stats.num_experts), sel] = 1.0
-        affinity[s] = p.T @ stats.affinity[s] @ p
-        np.fill_diagonal(affinity[s], 0.0)
+    for src in range(stats.ep_size):
+        chosen = m[src]
+        np.add.at(demand[src], chosen, stats.demand[src])
+        # co-selection moves with the chosen copies: scatter-add the expert pair matrix onto copy pairs
+        np.add.at(affinity[src], (chosen[:, None], chosen[None, :]), stats.affinity[src])
+        np.fill_diagonal(affinity[src], 0.0)
     return demand, affinity

@@ -1,20 +1,33 @@
-"""PlaceMoE data model: topology, profile statistics and a per-layer plan (L, M).
+"""PlaceMoE data model: the slot topology, profile statistics and a per-layer plan (L, M).
 
-* ``Topology(ep_size, ranks_per_node, num_experts, slots_per_rank)`` -- the
-  physical slot capacity of one expert-parallel MoE layer.  On one NVSwitch
-  domain (8xB200) ``ranks_per_node == ep_size``: one level.
-* ``ProfileStatistics(demand[S, E], affinity[S, E, E])`` -- source-conditioned
-  assignment demand and symmetric, zero-diagonal co-selection affinity.
-* ``LayerPlan(slot_to_logical, source_logical_to_physical, owner_slots)`` --
-  layout ``L`` (logical expert of every physical slot, -1 = empty), mapping
-  ``M`` (copy that source rank r uses for logical expert e) and the runtime
-  owner copy of every expert.  ``validate`` enforces: >= 1 copy per expert,
-  optional exact extra-copy budget, M points at a copy of the right expert,
-  owners hold their expert.
+A placement problem lives on ``PlaceMoETopology``: ``ep_size`` GPUs grouped
+into nodes of ``ranks_per_node``, each GPU holding ``slots_per_rank`` physical
+expert slots, for ``num_experts`` logical experts.  Slot ``s`` sits on GPU
+``s // slots_per_rank``.  On one NVSwitch domain (8xB200) there is one node.
 
-Semantics and the JSON payload keys are the same as
-veomni/distributed/moe/hiermoe/placemoe/types.py:25-177 so that artifacts are
-interchangeable.
+``LayerPlan`` is the answer for one MoE layer:
+
+* ``slot_to_logical`` (layout L): the logical expert held by every slot, or
+  ``EMPTY_EXPERT`` (-1);
+* ``source_logical_to_physical`` (mapping M): ``M[r, e]`` is the slot whose
+  copy of expert ``e`` serves tokens routed on GPU ``r``;
+* ``owner_slots``: the copy of every expert that owns its optimizer state and
+  counts it once in the gradient norm.
+
+A plan is consistent when every expert has a copy, every ``M[r, e]`` and
+``owner_slots[e]`` points at a slot holding ``e``, and (optionally) the layout
+spends exactly the requested number of extra copies.  ``LayerPlan.problems``
+lists every violated rule; ``validate`` raises on the first.
+
+``ProfileStatistics`` carries what the planner optimises against: the
+source-conditioned demand ``demand[r, e]`` (assignments of expert ``e`` made
+on GPU ``r``) and the co-selection ``affinity[r, e, f]`` (tokens of GPU ``r``
+that chose both ``e`` and ``f``; symmetric, zero diagonal).
+
+The three arrays of a plan and their JSON keys are the interchange format of
+the schema-v2 artifact; their meaning matches
+veomni/distributed/moe/hiermoe/placemoe/types.py:25-177, so artifacts written
+by either implementation load in the other.
 """
 
 from __future__ import annotations
@@ -26,11 +39,13 @@ import numpy as np
 
 EMPTY_EXPERT = -1
 
+_PLAN_KEYS = ("slot_to_logical", "owner_slots", "source_logical_to_physical")
 
-def _frozen(a, dtype) -> np.ndarray:
-    out = np.array(a, dtype=dtype, copy=True)
-    out.setflags(write=False)
-    return out
+
+def _readonly(values, dtype) -> np.ndarray:
+    arr = np.array(values, dtype=dtype, copy=True)
+    arr.flags.writeable = False
+    return arr
 
 
 @dataclass(frozen=True)
@@ -41,13 +56,14 @@ class PlaceMoETopology:
     slots_per_rank: int
 
     def __post_init__(self) -> None:
-        for k in ("ep_size", "ranks_per_node", "num_experts", "slots_per_rank"):
-            if int(getattr(self, k)) <= 0:
-                raise ValueError(f"{k} must be positive.")
-        if self.ep_size % self.ranks_per_node != 0:
-            raise ValueError("ep_size must be divisible by ranks_per_node.")
+        bad = [name for name in ("ep_size", "ranks_per_node", "num_experts", "slots_per_rank")
+               if int(getattr(self, name)) < 1]
+        if bad:
+            raise ValueError(f"topology sizes must be >= 1: {', '.join(bad)}")
+        if self.ep_size % self.ranks_per_node:
+            raise ValueError(f"{self.ep_size} GPUs do not split into nodes of {self.ranks_per_node}")
         if self.total_slots < self.num_experts:
-            raise ValueError("Physical capacity cannot hold one copy of every expert.")
+            raise ValueError(f"{self.total_slots} slots cannot hold {self.num_experts} experts once each")
 
     @property
     def num_nodes(self) -> int:
@@ -59,15 +75,17 @@ class PlaceMoETopology:
 
     @property
     def extra_copies(self) -> int:
+        """Slots beyond one copy per expert: the replica budget."""
         return self.total_slots - self.num_experts
 
     def rank_of_slot(self, slot: int) -> int:
-        if slot < 0 or slot >= self.total_slots:
-            raise ValueError(f"Physical slot {slot} is outside the topology.")
+        if not 0 <= slot < self.total_slots:
+            raise ValueError(f"slot {slot} is not in [0, {self.total_slots})")
         return slot // self.slots_per_rank
 
     def slot_ranks(self) -> np.ndarray:
-        return np.arange(self.total_slots, dtype=np.int64) // self.slots_per_rank
+        """GPU of every slot, [total_slots]."""
+        return np.repeat(np.arange(self.ep_size, dtype=np.int64), self.slots_per_rank)
 
 
 @dataclass(frozen=True)
@@ -76,37 +94,39 @@ class ProfileStatistics:
     affinity: np.ndarray
 
     def __post_init__(self) -> None:
-        d = _frozen(self.demand, np.float64)
-        a = _frozen(self.affinity, np.float64)
-        if d.ndim != 2:
-            raise ValueError("demand must have shape [source_rank, expert].")
-        s, e = d.shape
-        if a.shape != (s, e, e):
-            raise ValueError("affinity must have shape [source_rank, expert, expert].")
-        if (d < 0).any() or (a < 0).any():
-            raise ValueError("Profile statistics must be non-negative.")
-        if not np.allclose(a, np.swapaxes(a, 1, 2)):
-            raise ValueError("Expert affinity must be symmetric for every source rank.")
-        if not np.allclose(np.diagonal(a, axis1=1, axis2=2), 0.0):
-            raise ValueError("Expert affinity diagonal must be zero.")
-        object.__setattr__(self, "demand", d)
-        object.__setattr__(self, "affinity", a)
+        demand = _readonly(self.demand, np.float64)
+        affinity = _readonly(self.affinity, np.float64)
+        if demand.ndim != 2:
+            raise ValueError(f"demand is [gpu, expert]; got shape {demand.shape}")
+        gpus, experts = demand.shape
+        if affinity.shape != (gpus, experts, experts):
+            raise ValueError(f"affinity is [gpu, expert, expert] = {(gpus, experts, experts)}; got {affinity.shape}")
+        if min(demand.min(initial=0.0), affinity.min(initial=0.0)) < 0:
+            raise ValueError("demand and affinity are counts: no negative entries")
+        if not np.allclose(affinity, affinity.transpose(0, 2, 1)):
+            raise ValueError("affinity[r] must be a symmetric matrix for every GPU r")
+        if np.abs(np.einsum("rii->ri", affinity)).max(initial=0.0) > 1e-9:
+            raise ValueError("affinity[r, e, e] must be 0 (an expert is not co-selected with itself)")
+        object.__setattr__(self, "demand", demand)
+        object.__setattr__(self, "affinity", affinity)
 
     @property
     def ep_size(self) -> int:
-        return self.demand.shape[0]
+        return int(self.demand.shape[0])
 
     @property
     def num_experts(self) -> int:
-        return self.demand.shape[1]
+        return int(self.demand.shape[1])
 
     @property
     def expert_demand(self) -> np.ndarray:
-        return self.demand.sum(0)
+        """Demand per expert over all source GPUs, [E]."""
+        return self.demand.sum(axis=0)
 
     @property
     def expert_affinity(self) -> np.ndarray:
-        return self.affinity.sum(0)
+        """Co-selection over all source GPUs, [E, E]."""
+        return self.affinity.sum(axis=0)
 
 
 @dataclass(frozen=True)
@@ -116,61 +136,62 @@ class LayerPlan:
     owner_slots: np.ndarray
 
     def __post_init__(self) -> None:
-        object.__setattr__(self, "slot_to_logical", _frozen(self.slot_to_logical, np.int64))
-        object.__setattr__(self, "source_logical_to_physical", _frozen(self.source_logical_to_physical, np.int64))
-        object.__setattr__(self, "owner_slots", _frozen(self.owner_slots, np.int64))
+        for name in _PLAN_KEYS:
+            object.__setattr__(self, name, _readonly(getattr(self, name), np.int64))
 
     @property
     def copy_counts(self) -> np.ndarray:
-        used = self.slot_to_logical[self.slot_to_logical != EMPTY_EXPERT]
-        return np.bincount(used, minlength=len(self.owner_slots))
+        """Copies of every logical expert in the layout, [E]."""
+        held = self.slot_to_logical[self.slot_to_logical >= 0]
+        return np.bincount(held, minlength=len(self.owner_slots))
+
+    def problems(self, topology: PlaceMoETopology, additional_copies: int | None = None) -> list[str]:
+        """Every rule of a consistent plan that this plan breaks (empty when it is consistent)."""
+        e, n, r = topology.num_experts, topology.total_slots, topology.ep_size
+        layout, mapping, owners = self.slot_to_logical, self.source_logical_to_physical, self.owner_slots
+        shapes = [("layout", layout.shape, (n,)), ("mapping", mapping.shape, (r, e)), ("owners", owners.shape, (e,))]
+        found = [f"{what} has shape {got}, the topology needs {want}" for what, got, want in shapes if got != want]
+        if found:
+            return found  # the element checks below need the right shapes
+        if ((layout < EMPTY_EXPERT) | (layout >= e)).any():
+            found.append(f"layout entries must be -1 (empty) or an expert id below {e}")
+            return found
+        copies = self.copy_counts
+        missing = np.flatnonzero(copies[:e] == 0)
+        if missing.size:
+            found.append(f"experts without any copy: {missing[:8].tolist()}")
+        if additional_copies is not None and int(copies.sum()) - e != additional_copies:
+            found.append(f"layout spends {int(copies.sum()) - e} extra copies, the budget is {additional_copies}")
+        for what, slots, expect in (("mapping", mapping, np.broadcast_to(np.arange(e), mapping.shape)),
+                                    ("owner", owners, np.arange(e))):
+            if ((slots < 0) | (slots >= n)).any():
+                found.append(f"{what} points outside the {n} slots")
+            elif not np.array_equal(layout[slots], expect):
+                found.append(f"{what} points at a slot that holds another expert")
+        return found
 
     def validate(self, topology: PlaceMoETopology, *, additional_copies: int | None = None) -> None:
-        e, n = topology.num_experts, topology.total_slots
-        layout, mapping, owners = self.slot_to_logical, self.source_logical_to_physical, self.owner_slots
-        if layout.shape != (n,):
-            raise ValueError("Layout length does not match the physical slot capacity.")
-        if mapping.shape != (topology.ep_size, e):
-            raise ValueError("Mapping shape does not match [source_rank, logical_expert].")
-        if owners.shape != (e,):
-            raise ValueError("owner_slots must contain one runtime owner per logical expert.")
-        if (layout < EMPTY_EXPERT).any() or (layout >= e).any():
-            raise ValueError("Layout contains an invalid logical expert ID.")
-        counts = self.copy_counts
-        if (counts[:e] < 1).any():
-            raise ValueError("Every logical expert must retain at least one physical copy.")
-        if additional_copies is not None and int(counts.sum()) - e != additional_copies:
-            raise ValueError("Layout does not use the requested additional-copy budget.")
-        if (mapping < 0).any() or (mapping >= n).any():
-            raise ValueError("Mapping references a slot outside the topology.")
-        if not np.array_equal(layout[mapping], np.broadcast_to(np.arange(e), mapping.shape)):
-            raise ValueError("Mapping references a copy of the wrong logical expert.")
-        if (owners < 0).any() or (owners >= n).any():
-            raise ValueError("Runtime owner references a slot outside the topology.")
-        if not np.array_equal(layout[owners], np.arange(e)):
-            raise ValueError("Runtime owner slots do not match their logical experts.")
+        found = self.problems(topology, additional_copies)
+        if found:
+            raise ValueError("inconsistent layer plan: " + "; ".join(found))
 
     def to_runtime_payload(self) -> dict[str, Any]:
-        return {
-            "slot_to_logical": self.slot_to_logical.tolist(),
-            "owner_slots": self.owner_slots.tolist(),
-            "source_logical_to_physical": self.source_logical_to_physical.tolist(),
-        }
+        """The artifact's per-layer JSON object."""
+        return {name: getattr(self, name).tolist() for name in _PLAN_KEYS}
 
     @classmethod
     def from_runtime_payload(cls, payload: dict[str, Any]) -> "LayerPlan":
-        return cls(
-            slot_to_logical=payload["slot_to_logical"],
-            owner_slots=payload["owner_slots"],
-            source_logical_to_physical=payload["source_logical_to_physical"],
-        )
+        return cls(**{name: payload[name] for name in _PLAN_KEYS})
 
     def replica_groups(self) -> list[np.ndarray]:
-        """Physical slots of every logical expert (owner first)."""
+        """Slots of every logical expert, owner first (one group per expert)."""
+        order = np.argsort(self.slot_to_logical, kind="stable")
+        held = self.slot_to_logical[order]
         groups = []
         for e, owner in enumerate(self.owner_slots.tolist()):
-            slots = np.flatnonzero(self.slot_to_logical == e)
-            groups.append(np.concatenate([[owner], slots[slots != owner]]).astype(np.int64))
+            lo, hi = np.searchsorted(held, [e, e + 1])
+            others = order[lo:hi]
+            groups.append(np.concatenate(([owner], others[others != owner])).astype(np.int64))
         return groups
 
 
@@ -179,18 +200,14 @@ def identity_plan(topology: PlaceMoETopology) -> LayerPlan:
 
     Extra slots (if any) are left empty.
     """
-    n, e = topology.total_slots, topology.num_experts
+    e, spr = topology.num_experts, topology.slots_per_rank
     per_rank = -(-e // topology.ep_size)
-    if per_rank > topology.slots_per_rank:
-        raise ValueError("identity plan needs ceil(E / ep) <= slots_per_rank")
-    layout = np.full(n, EMPTY_EXPERT, dtype=np.int64)
-    owners = np.zeros(e, dtype=np.int64)
-    for x in range(e):
-        r, j = divmod(x, per_rank)
-        slot = r * topology.slots_per_rank + j
-        layout[slot] = x
-        owners[x] = slot
-    mapping = np.broadcast_to(owners, (topology.ep_size, e)).copy()
-    plan = LayerPlan(layout, mapping, owners)
+    if per_rank > spr:
+        raise ValueError(f"fixed EP needs ceil({e} / {topology.ep_size}) = {per_rank} slots per GPU, have {spr}")
+    experts = np.arange(e)
+    owners = (experts // per_rank) * spr + experts % per_rank
+    layout = np.full(topology.total_slots, EMPTY_EXPERT, dtype=np.int64)
+    layout[owners] = experts
+    plan = LayerPlan(layout, np.tile(owners, (topology.ep_size, 1)), owners)
     plan.validate(topology)
     return plan
