@@ -9,4 +9,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("evaluate_routes", &pmp::evaluate_routes, "exact one-level route replay");
   m.def("optimize_mapping", &pmp::optimize_mapping, "mapping coordinate descent (in place)");
   m.def("refine_partition", &pmp::refine_partition, "capacity-constrained pairwise exchange (in place)");
+  m.def("optimize_mapping_normalized", &pmp::optimize_mapping_normalized,
+        "scale-normalised mapping proposal (in place); returns [peak load, sweeps, changes]");
+  m.def("community_intersection_hits", &pmp::community_intersection_hits, "tokens whose community mask meets X");
+  m.def("community_mask_histogram", &pmp::community_mask_histogram, "tokens per (source unit, community mask)");
+  m.def("optimize_community_mapping", &pmp::optimize_community_mapping,
+        "block mapping of (source unit, community) -> destination unit");
 }

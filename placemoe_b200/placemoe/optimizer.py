@@ -9,6 +9,10 @@
             for each placement: fresh mapping (greedy init) and, from the second alternation on,
                 the carried mapping of the incumbent, each refined by the
                 coordinate-descent core
+            plus proposals from the fresh seed: scale-normalised mappings (one
+                per assignment weight) and a community block mapping (experts with
+                the same copy GPUs move as one block, rows counted exactly from
+                the token community masks)
             every candidate is scored by the exact route-replay evaluator;
             the incumbent only changes on strict improvement (monotone)
             instance statistics <- projection through the incumbent mapping
@@ -27,7 +31,8 @@ import numpy as np
 
 from .allocation import candidate_allocations, instances_from_allocation
 from .evaluator import PlanCost, RouteReplayEvaluator
-from .mapping import initialize_mapping, optimize_mapping
+from .mapping import (community_mask_histogram, copy_set_communities, initialize_mapping, optimize_community_mapping,
+                      optimize_mapping, optimize_mapping_normalized)
 from .materialize import layout_from_ranks, materialize_plan
 from .partition import expert_groups_for_allocation
 from .placement import PlacementConfig, place_instances
@@ -46,6 +51,9 @@ class OptimizerConfig:
     exchange_limit: int = 256
     seed: int = 0
     include_baselines: bool = True
+    # scale-normalised mapping proposals (one per assignment weight) and the community block proposal
+    normalized_weights: tuple = (0.5, 2.0)
+    community_mapping: bool = True
 
     def __post_init__(self):
         if self.rounds <= 0 or self.placement_candidates <= 0 or self.allocation_candidates <= 0:
@@ -144,6 +152,9 @@ def optimize_replica_allocation(stats: ProfileStatistics, topology: PlaceMoETopo
                                             gamma=gamma, local_weight=local_w, sweeps=cfg.mapping_sweeps)
                     plan = materialize_plan(layout, m, stats.demand, topology)
                     consider(plan, f"alloc{ai}/round{rnd}/place{pi}:{place.seed_name}/map{si}")
+                tag = f"alloc{ai}/round{rnd}/place{pi}:{place.seed_name}"
+                for label, m in _mapping_proposals(stats, layout, slot_rank, seeds[0], topology, evaluator, cfg):
+                    consider(materialize_plan(layout, m, stats.demand, topology), f"{tag}/{label}")
             if incumbent is not None and incumbent.label.startswith(f"alloc{ai}/"):
                 p = incumbent.plan
                 carried = p.source_logical_to_physical.copy()
@@ -154,6 +165,37 @@ def optimize_replica_allocation(stats: ProfileStatistics, topology: PlaceMoETopo
                 inst_of_slot[order] = np.arange(len(order))
                 mapping_inst = inst_of_slot[carried]
     return res
+
+
+def _mapping_proposals(stats: ProfileStatistics, layout: np.ndarray, slot_rank: np.ndarray, seed: np.ndarray,
+                       topology: PlaceMoETopology, evaluator: RouteReplayEvaluator, cfg: OptimizerConfig):
+    """(label, mapping) proposals beyond the calibrated descent, for the exact evaluator to judge."""
+    out = []
+    seen = set()
+    for w in cfg.normalized_weights:
+        m, _ = optimize_mapping_normalized(stats.demand, stats.affinity, layout, slot_rank, seed,
+                                           ranks_per_node=topology.ranks_per_node, assignment_weight=w,
+                                           sweeps=cfg.mapping_sweeps)
+        if m.tobytes() not in seen:
+            seen.add(m.tobytes())
+            out.append((f"normalized{w:g}", m))
+    if cfg.community_mapping and topology.extra_copies > 0:
+        comm = copy_set_communities(layout, slot_rank, topology.num_experts)
+        if comm is not None:
+            c = int(comm.max()) + 1
+            hist = None
+            for step in evaluator.samples:
+                h = community_mask_histogram(step, comm, ranks_per_unit=1, num_communities=c)
+                hist = h if hist is None else hist + h
+            asg = np.zeros((topology.ep_size, c))
+            for k in range(c):
+                asg[:, k] = stats.demand[:, comm == k].sum(axis=1)
+            omega, gamma, _ = evaluator.coefficients()
+            res = optimize_community_mapping(layout, slot_rank, comm, asg, hist, ranks_per_unit=1,
+                                             comm_ms_per_token=omega, ms_per_assignment=gamma)
+            if res.mapping.tobytes() not in seen:
+                out.append(("community", res.mapping))
+    return out
 
 
 def optimize_fixed_layout_mapping(stats: ProfileStatistics, topology: PlaceMoETopology, layout_plan: LayerPlan,
@@ -174,4 +216,9 @@ def optimize_fixed_layout_mapping(stats: ProfileStatistics, topology: PlaceMoETo
         plan.validate(topology)
         cand = OptimizerCandidate(plan, evaluator.evaluate(plan), f"mapping{si}")
         res.candidates.append(cand)
+    seed = initialize_mapping(stats.demand, layout, slot_rank, topology.ep_size)
+    for label, m in _mapping_proposals(stats, layout, slot_rank, seed, topology, evaluator, cfg):
+        plan = LayerPlan(layout, m, layout_plan.owner_slots)
+        plan.validate(topology)
+        res.candidates.append(OptimizerCandidate(plan, evaluator.evaluate(plan), label))
     return res
