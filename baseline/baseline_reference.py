@@ -11,7 +11,9 @@ micro-batch, ``veomni_clip_grad_norm`` and ``optimizer.step``.
 Model: the reference has no expert-parallel OLMoE implementation, so its
 Qwen3-MoE implementation is configured at the OLMoE-1B-7B shape (16 layers,
 hidden 2048, 16 MHA heads x 128, 64 experts top-8, moe_intermediate 1024,
-vocab 50304); MoE kernels ``fused_triton`` (its default), attention through
+vocab 50304), or at the Qwen3-30B-A3B shape (``--model qwen3_30b_a3b``: 48
+layers, 32 q / 4 kv heads, 128 experts top-8, moe_intermediate 768, vocab
+151936); MoE kernels ``fused_triton`` (its default), attention through
 PyTorch SDPA, other ops eager (liger_kernel is not installed here).  The
 reference exposes no router-bias hook, so its routing is not skewed.
 
@@ -32,7 +34,6 @@ import json
 import os
 import sys
 import tempfile
-import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(HERE, "_ref")
@@ -43,15 +44,24 @@ def _unavailable(reason: str) -> int:
     return 0
 
 
-def _config_dir(vocab=50304, hidden=2048, layers=16, heads=16, kv=16, hd=128, experts=64, k=8, inter=1024):
-    d = tempfile.mkdtemp(prefix="ref_olmoe_shape_")
+# The two benchmark shapes, as Qwen3-MoE configurations of the reference's own model implementation.
+SHAPES = {
+    "olmoe_1b_7b": dict(vocab=50304, hidden=2048, layers=16, heads=16, kv=16, hd=128, experts=64, k=8, inter=1024,
+                        norm_topk=False, theta=10000.0, eps=1e-5, aux=0.01),
+    "qwen3_30b_a3b": dict(vocab=151936, hidden=2048, layers=48, heads=32, kv=4, hd=128, experts=128, k=8,
+                          inter=768, norm_topk=True, theta=1000000.0, eps=1e-6, aux=0.001),
+}
+
+
+def _config_dir(vocab, hidden, layers, heads, kv, hd, experts, k, inter, norm_topk, theta, eps, aux):
+    d = tempfile.mkdtemp(prefix="ref_moe_shape_")
     cfg = {
         "architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe", "vocab_size": vocab,
         "hidden_size": hidden, "intermediate_size": inter, "moe_intermediate_size": inter,
         "num_hidden_layers": layers, "num_attention_heads": heads, "num_key_value_heads": kv, "head_dim": hd,
-        "num_experts": experts, "num_experts_per_tok": k, "norm_topk_prob": False, "decoder_sparse_step": 1,
-        "mlp_only_layers": [], "rope_theta": 10000.0, "rms_norm_eps": 1e-5, "max_position_embeddings": 4096,
-        "tie_word_embeddings": False, "router_aux_loss_coef": 0.01, "output_router_logits": True,
+        "num_experts": experts, "num_experts_per_tok": k, "norm_topk_prob": norm_topk, "decoder_sparse_step": 1,
+        "mlp_only_layers": [], "rope_theta": theta, "rms_norm_eps": eps, "max_position_embeddings": 4096,
+        "tie_word_embeddings": False, "router_aux_loss_coef": aux, "output_router_logits": True,
         "attention_bias": False, "attention_dropout": 0.0, "hidden_act": "silu", "initializer_range": 0.02,
         "torch_dtype": "bfloat16", "use_cache": False,
     }
@@ -63,8 +73,9 @@ def _config_dir(vocab=50304, hidden=2048, layers=16, heads=16, kv=16, hd=128, ex
 def main(args) -> int:
     if not os.path.isdir(os.path.join(REF, "veomni")):
         return _unavailable("reference not installed in baseline/_ref")
-    if args.model != "olmoe_1b_7b":
-        return _unavailable(f"reference arm is defined for olmoe_1b_7b only (got {args.model})")
+    if args.model not in SHAPES:
+        return _unavailable(f"reference arm is defined for {sorted(SHAPES)} (got {args.model})")
+    shape = SHAPES[args.model]
     sys.path.insert(0, REF)
     import torch
     import torch.distributed as dist
@@ -103,7 +114,7 @@ def main(args) -> int:
     ops = OpsImplementationConfig(attn_implementation="sdpa", moe_implementation="fused_triton",
                                   cross_entropy_loss_implementation="eager", rms_norm_implementation="eager",
                                   swiglu_mlp_implementation="eager", rotary_pos_emb_implementation="eager")
-    cfg_dir = _config_dir()
+    cfg_dir = _config_dir(**shape)
     # its parallelizer accepts meta init only when FSDP is on (world size > 1)
     init_device = "meta" if world > 1 else "cuda"
     # Without FSDP its mixed-precision switch only upcasts the model to fp32, which its fused
@@ -123,7 +134,7 @@ def main(args) -> int:
 
     seq, bpg, mb = args.seq, args.batch_per_gpu, args.micro_batch
     g = torch.Generator().manual_seed(rank)
-    pool = [torch.randint(0, 50304, (bpg, seq), generator=g).pin_memory() for _ in range(2)]
+    pool = [torch.randint(0, shape["vocab"], (bpg, seq), generator=g).pin_memory() for _ in range(2)]
     dev = [p.cuda() for p in pool]
 
     def step(ids, read_loss):
@@ -174,8 +185,10 @@ def main(args) -> int:
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic uniform token ids (seeded), random-init weights",
-            "config": {"model": "reference Qwen3-MoE implementation at the olmoe_1b_7b shape (16L, H2048, 64E top8, "
-                                "I1024, V50304); no router bias", "global_batch": bpg * world, "seq_len": seq,
+            "config": {"model": (f"reference Qwen3-MoE implementation at the {args.model} shape "
+                                 f"({shape['layers']}L, H{shape['hidden']}, {shape['heads']}q/{shape['kv']}kv heads, "
+                                 f"{shape['experts']}E top{shape['k']}, I{shape['inter']}, V{shape['vocab']}); "
+                                 "no router bias"), "global_batch": bpg * world, "seq_len": seq,
                        "precision": "fsdp2 mixed precision (fp32 masters, bf16 compute)" if mp_on
                        else "bf16 parameters and optimizer states (no FSDP on one GPU)",
                        "micro_batch": mb, "parallelism": f"fsdp{world}+ep{world}",
@@ -189,4 +202,3 @@ def main(args) -> int:
     return 0
 
 
-__all__ = ["main", "time"]

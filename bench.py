@@ -59,7 +59,10 @@ def parse():
                    help="shard dense masters/moments/gradients over the ranks (peer-memory RS/AG); auto = N > 1")
     p.add_argument("--recompute-expert-rows", action="store_true",
                    help="re-gather dispatched expert inputs in the backward instead of keeping them (memory)")
-    return p.parse_args()
+    args = p.parse_args()
+    if args.micro_batch <= 0:
+        args.micro_batch = 2 if args.model == "qwen3_30b_a3b" else 4
+    return args
 
 
 class ClockSampler:
@@ -204,8 +207,6 @@ def main():
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     big = args.model == "qwen3_30b_a3b"
-    if args.micro_batch <= 0:
-        args.micro_batch = 2 if big else 4
     if args.placement == "fixed_ep":
         args.redundant_slots = 0
     if args.redundant_slots < 0:

@@ -1,11 +1,17 @@
 """In-tree build of the native extensions.
 
-Two extension modules are produced under ``placemoe_b200/_build/``:
+Three extension modules are produced under ``placemoe_b200/_build/``:
 
 * ``pm_kernels``  -- the sm_100a CUDA kernels (tcgen05 GEMMs, attention, norms,
   router, dispatch/combine, optimizer, P2P kernels) with their pybind11 bindings;
+* ``pm_kernels_dbg`` -- the same kernels compiled with ``-DPLACEMOE_DEBUG_BOUNDS``:
+  indices read from data (row tables, dispatch positions, peer ranks) are
+  checked; a bad one records error 3 ("bounds check failed") and the access
+  is skipped instead of faulting.  ``PLACEMOE_DEBUG_BOUNDS=1`` in the
+  environment makes :func:`load_kernels` return this module;
 * ``pm_planner``  -- the CPU C++ cores of the PlaceMoE planner (route statistics,
-  mapping coordinate descent, partition exchange refinement, exact route replay).
+  mapping coordinate descent and proposals, partition exchange refinement,
+  exact route replay).
 
 Only :func:`build` compiles.  :func:`load_kernels` / :func:`load_planner` import
 an already built module and never invoke the compiler, so a GPU machine that
@@ -26,7 +32,9 @@ _CSRC = os.path.join(_PKG_DIR, "csrc")
 BUILD_DIR = os.path.join(_PKG_DIR, "_build")
 
 KERNELS_NAME = "pm_kernels"
+DEBUG_KERNELS_NAME = "pm_kernels_dbg"
 PLANNER_NAME = "pm_planner"
+DEBUG_ENV = "PLACEMOE_DEBUG_BOUNDS"
 
 CUDA_FLAGS = [
     "-gencode",
@@ -56,16 +64,18 @@ def _so_path(name: str) -> str:
     return os.path.join(BUILD_DIR, name, f"{name}.so")
 
 
-def build_kernels(verbose: bool = False) -> ModuleType:
+def build_kernels(verbose: bool = False, debug_bounds: bool = False) -> ModuleType:
     from torch.utils import cpp_extension
 
-    out = os.path.join(BUILD_DIR, KERNELS_NAME)
+    name = DEBUG_KERNELS_NAME if debug_bounds else KERNELS_NAME
+    defs = ["-DPLACEMOE_DEBUG_BOUNDS"] if debug_bounds else []
+    out = os.path.join(BUILD_DIR, name)
     os.makedirs(out, exist_ok=True)
     return cpp_extension.load(
-        name=KERNELS_NAME,
+        name=name,
         sources=kernel_sources(),
-        extra_cflags=CXX_FLAGS,
-        extra_cuda_cflags=CUDA_FLAGS,
+        extra_cflags=CXX_FLAGS + defs,
+        extra_cuda_cflags=CUDA_FLAGS + defs,
         extra_include_paths=[os.path.join(_CSRC), os.path.join(_CSRC, "kernels")],
         build_directory=out,
         verbose=verbose,
@@ -88,10 +98,12 @@ def build_planner(verbose: bool = False) -> ModuleType:
     )
 
 
-def build(verbose: bool = False) -> None:
+def build(verbose: bool = False, debug_bounds: bool = True) -> None:
     os.environ.setdefault("MAX_JOBS", str(os.cpu_count() or 8))
     build_planner(verbose)
     build_kernels(verbose)
+    if debug_bounds:
+        build_kernels(verbose, debug_bounds=True)
 
 
 def _import_so(name: str) -> ModuleType:
@@ -111,7 +123,14 @@ def _import_so(name: str) -> ModuleType:
 
 
 def load_kernels() -> ModuleType:
+    """The kernel module: the bounds-checked build when ``PLACEMOE_DEBUG_BOUNDS=1``."""
+    if os.environ.get(DEBUG_ENV, "0") not in ("", "0"):
+        return _import_so(DEBUG_KERNELS_NAME)
     return _import_so(KERNELS_NAME)
+
+
+def load_debug_kernels() -> ModuleType:
+    return _import_so(DEBUG_KERNELS_NAME)
 
 
 def load_planner(auto_build: bool = True) -> ModuleType:
@@ -125,5 +144,5 @@ def load_planner(auto_build: bool = True) -> ModuleType:
 
 
 if __name__ == "__main__":
-    build(verbose="-v" in sys.argv)
-    print("built", _so_path(KERNELS_NAME), _so_path(PLANNER_NAME))
+    build(verbose="-v" in sys.argv, debug_bounds="--no-debug" not in sys.argv)
+    print("built", _so_path(KERNELS_NAME), _so_path(DEBUG_KERNELS_NAME), _so_path(PLANNER_NAME))

@@ -16,7 +16,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 
 import torch
@@ -150,6 +149,53 @@ def bench_attn(batch, seq, heads, kv_heads, dim, iters):
     report("attn_bwd", time_fn(lambda: kernels().attn_bwd(q, kk, v, o, lse, do, seq), iters), 2.5 * f)
 
 
+def bench_attn_compare(batch, seq, heads, kv_heads, dim, iters):
+    """Same-box comparison of the tcgen05 attention kernels with PyTorch SDPA backends (causal).
+
+    SDPA runs in its own [B, H, S, D] layout; its backward time is (forward + backward) - forward.
+    FLOPs count the causal half: forward 4*B*S^2/2*H*D, backward 2.5x that.
+    """
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from placemoe_b200.ops import kernels
+
+    t = batch * seq
+    f = 4.0 * batch * seq * seq / 2 * heads * dim
+    tag = f"B{batch} S{seq} H{heads}/{kv_heads} D{dim}"
+    q = torch.randn(t, heads, dim, device="cuda", dtype=torch.bfloat16)
+    kk = torch.randn(t, kv_heads, dim, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(t, kv_heads, dim, device="cuda", dtype=torch.bfloat16)
+    o, lse = kernels().attn_fwd(q, kk, v, seq)
+    do = torch.randn_like(o)
+    report(f"ours attn_fwd[{tag}]", time_fn(lambda: kernels().attn_fwd(q, kk, v, seq), iters), f)
+    report(f"ours attn_bwd[{tag}]", time_fn(lambda: kernels().attn_bwd(q, kk, v, o, lse, do, seq), iters), 2.5 * f)
+    qb = q.view(batch, seq, heads, dim).transpose(1, 2).contiguous().requires_grad_()
+    kb = kk.view(batch, seq, kv_heads, dim).transpose(1, 2).contiguous().requires_grad_()
+    vb = v.view(batch, seq, kv_heads, dim).transpose(1, 2).contiguous().requires_grad_()
+    dob = do.view(batch, seq, heads, dim).transpose(1, 2).contiguous()
+    gqa = heads != kv_heads
+    for name, backend in (("cudnn", SDPBackend.CUDNN_ATTENTION), ("flash", SDPBackend.FLASH_ATTENTION),
+                          ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        try:
+            with sdpa_kernel(backend):
+                def fwd():
+                    with torch.no_grad():
+                        return F.scaled_dot_product_attention(qb, kb, vb, is_causal=True, enable_gqa=gqa)
+
+                def fwd_bwd():
+                    out = F.scaled_dot_product_attention(qb, kb, vb, is_causal=True, enable_gqa=gqa)
+                    out.backward(dob)
+                    qb.grad = kb.grad = vb.grad = None
+
+                tf = time_fn(fwd, iters)
+                tfb = time_fn(fwd_bwd, iters)
+            report(f"sdpa-{name} fwd[{tag}]", tf, f)
+            report(f"sdpa-{name} bwd[{tag}]", max(tfb - tf, 1e-6), 2.5 * f)
+        except RuntimeError as e:  # backend not available for this shape / GPU
+            print(json.dumps({"op": f"sdpa-{name}[{tag}]", "unavailable": str(e).splitlines()[0][:200]}), flush=True)
+
+
 def bench_memory(tokens, hidden, iters):
     from placemoe_b200.ops import kernels
 
@@ -161,7 +207,7 @@ def bench_memory(tokens, hidden, iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="all", choices=("all", "gemm", "moe", "attn", "memory"))
+    ap.add_argument("--op", default="all", choices=("all", "gemm", "moe", "attn", "attn_compare", "memory"))
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=2048)
     ap.add_argument("--k", type=int, default=2048)
@@ -189,6 +235,8 @@ def main():
             bench_moe(a.tokens, a.experts, a.topk, a.hidden, a.inter, a.iters, a.skew, al)
     if a.op in ("all", "attn"):
         bench_attn(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
+    if a.op == "attn_compare":
+        bench_attn_compare(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
     if a.op in ("all", "memory"):
         bench_memory(a.tokens, a.hidden, a.iters)
     from placemoe_b200.ops import check_device_error
@@ -201,4 +249,3 @@ if __name__ == "__main__":
     main()
 
 
-__all__ = ["math"]

@@ -29,7 +29,6 @@ from __future__ import annotations
 import json
 import os
 
-import numpy as np
 import torch
 import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
@@ -340,4 +339,4 @@ def load_hf_weights(trainer, hf_dir: str) -> None:
     _reload_params(trainer)
 
 
-__all__ = ["save_checkpoint", "load_checkpoint", "export_hf", "load_hf_weights", "placement_digest", "np"]
+__all__ = ["save_checkpoint", "load_checkpoint", "export_hf", "load_hf_weights", "placement_digest"]

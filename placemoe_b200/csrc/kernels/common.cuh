@@ -39,6 +39,20 @@ enum : int {
 
 PM_DEVICE void set_error(int code) { atomicCAS(&g_pm_error, 0, code); }
 
+// Index checks of the bounds-checked debug build (compiled with -DPLACEMOE_DEBUG_BOUNDS):
+// PM_INDEX_OK(cond) records kErrBounds and yields false when an index read from data is out
+// of range, so the caller skips the access instead of faulting; in the normal build it is
+// `true` and costs nothing.
+#ifdef PLACEMOE_DEBUG_BOUNDS
+PM_DEVICE bool index_ok(bool cond) {
+  if (!cond) set_error(kErrBounds);
+  return cond;
+}
+#define PM_INDEX_OK(cond) (::pm::index_ok(cond))
+#else
+#define PM_INDEX_OK(cond) (true)
+#endif
+
 // ~2^31 cycles is about one second at the B200 boost clock.
 constexpr long long kWaitBudgetCycles = 1LL << 32;
 

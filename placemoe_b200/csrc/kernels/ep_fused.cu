@@ -65,6 +65,7 @@ constexpr int kEpMaxPeers = 64;
 struct EpGeo {
   const long long* peers;  // [W] base addresses of the arena on every rank
   int W, rank, S, K, H, T, cap, align, kpad, parity;
+  int E, t_cap;       // logical experts (dispatch tables), tokens the return buffers hold
   long long off_flags, off_counts, off_x, off_meta, off_tab, off_back, off_dw, off_dy;
   unsigned epoch;     // first barrier epoch used by this launch
   long long budget_ns;
@@ -129,6 +130,18 @@ PM_DEVICE int first_same_dest(int d, int p, int K) {
   return first;
 }
 
+// Bucket (destination GPU, local slot) of assignment a, or -1 when a checked index is out of range
+// (the checks exist only in the bounds-checked debug build).
+PM_DEVICE int bucket_of(const EpGeo& g, const int* __restrict__ idx, const int* __restrict__ dest_tab,
+                        const int* __restrict__ slot_tab, int a, int* dest) {
+  const int e = idx[a];
+  if (!PM_PEER_INDEX_OK(g.st, e >= 0 && e < g.E)) return -1;
+  const int d = dest_tab[e], s = slot_tab[e];
+  if (!PM_PEER_INDEX_OK(g.st, d >= 0 && d < g.W && s >= 0 && s < g.S)) return -1;
+  *dest = d;
+  return d * g.S + s;
+}
+
 // ----------------------------------------------------------------------------------- dispatch
 __global__ void __launch_bounds__(kEpThreads, 2)
     ep_dispatch_kernel(EpGeo g, const __nv_bfloat16* __restrict__ x, const int* __restrict__ idx,
@@ -156,8 +169,9 @@ __global__ void __launch_bounds__(kEpThreads, 2)
 
   // ---- A: per-warp histograms over the warp's tokens
   for (int a = wt0 * K + lane; a < wt1 * K; a += 32) {
-    const int e = idx[a];
-    atomicAdd(&wrun[warp * B + dest_tab[e] * S + slot_tab[e]], 1);
+    int d;
+    const int b = bucket_of(g, idx, dest_tab, slot_tab, a, &d);
+    if (b >= 0) atomicAdd(&wrun[warp * B + b], 1);
   }
   __syncthreads();
   for (int b = tid; b < B; b += kEpThreads) {
@@ -226,20 +240,16 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   for (int a0 = wt0 * K; a0 < wt1 * K; a0 += 32) {
     const int a = a0 + lane;
     const bool valid = a < wt1 * K;
-    int b = -1, d = -1;
-    if (valid) {
-      const int e = idx[a];
-      d = dest_tab[e];
-      b = d * S + slot_tab[e];
-    }
+    int b = -1, d = 0;
+    if (valid) b = bucket_of(g, idx, dest_tab, slot_tab, a, &d);
     const unsigned same = __match_any_sync(0xffffffffu, b);
     const int rnk = __popc(same & (unsigned)lanemask_lt());
-    const int p = valid ? wrun[warp * B + b] + rnk : -1;
+    const int p = b >= 0 ? wrun[warp * B + b] + rnk : -1;
     __syncwarp();
-    if (valid && rnk == 0) wrun[warp * B + b] += __popc(same);
+    if (b >= 0 && rnk == 0) wrun[warp * B + b] += __popc(same);
     __syncwarp();
     if (valid) {
-      pos_out[a] = p < g.cap ? p : -1;
+      pos_out[a] = p < g.cap ? p : -1;  // -1: dropped (beyond the slab) or a bad index
       dst_out[a] = d;
     }
   }
@@ -316,8 +326,9 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     const int n = min(n_rows, g.cap);
     for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
       const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
-      if (lane == 0) row_scale[q] = m.x >= 0 ? __int_as_float(m.y) : 0.f;
-      if (m.x >= 0 && m.x != q)
+      const bool ok = m.x < 0 || PM_PEER_INDEX_OK(g.st, m.x < n);
+      if (lane == 0) row_scale[q] = (m.x >= 0 && ok) ? __int_as_float(m.y) : 0.f;
+      if (m.x >= 0 && m.x != q && ok)
         warp_copy_row(reinterpret_cast<uint4*>(me + g.off_x + (size_t)q * g.H * 2),
                       reinterpret_cast<const uint4*>(me + g.off_x + (size_t)m.x * g.H * 2), n16, lane);
     }
@@ -342,6 +353,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
     const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
     if (m.x < 0) continue;
+    if (!PM_PEER_INDEX_OK(g.st, m.z >= 0 && m.z < W && m.w >= 0 && m.w < g.t_cap * K)) continue;
     if (dscale != nullptr && lane == 0)
       reinterpret_cast<float*>(s_peers[m.z] + g.off_dw)[m.w] = dscale[q];
     if (m.x != q) continue;
@@ -350,7 +362,8 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     int cnt = 0;
 #pragma unroll
     for (int i = 0; i < kEpMaxK; ++i) {
-      const int v = i < g.kpad ? __ldcg(tab + i) : -1;
+      int v = i < g.kpad ? __ldcg(tab + i) : -1;
+      if (v >= 0 && !PM_PEER_INDEX_OK(g.st, v < n)) v = -1;
       list[i] = v;
       cnt += (v >= 0 && cnt == i) ? 1 : 0;
     }
@@ -383,6 +396,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     if (lane < K) {
       d = dst[t * K + lane];
       p = pos[t * K + lane];
+      if (p >= 0 && !PM_PEER_INDEX_OK(g.st, d >= 0 && d < W)) p = -1;
     }
     const unsigned dmask = __reduce_or_sync(0xffffffffu, (lane < K && p >= 0) ? (1u << d) : 0u);
     if (dw_out != nullptr && lane < K)
@@ -428,6 +442,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     if (lane < K) {
       d = dst[t * K + lane];
       p = pos[t * K + lane];
+      if (p >= 0 && !PM_PEER_INDEX_OK(g.st, d >= 0 && d < g.W && p < g.cap)) p = -1;
     }
     const int first = first_same_dest(d, p, K);
     unsigned prims = __ballot_sync(0xffffffffu, lane < K && p >= 0 && first == lane);
@@ -450,7 +465,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   // ---- B: local copies for the token's other assignments on this GPU
   for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
     const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
-    if (m.x >= 0 && m.x != q)
+    if (m.x >= 0 && m.x != q && PM_PEER_INDEX_OK(g.st, m.x < n))
       warp_copy_row(reinterpret_cast<uint4*>(me + g.off_dy + (size_t)q * g.H * 2),
                     reinterpret_cast<const uint4*>(me + g.off_dy + (size_t)m.x * g.H * 2), n16, lane);
   }
@@ -470,6 +485,7 @@ static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers,
   g.peers = reinterpret_cast<const long long*>(peers.data_ptr<int64_t>());
   g.W = (int)v[0]; g.rank = (int)v[1]; g.S = (int)v[2]; g.K = (int)v[3]; g.H = (int)v[4];
   g.T = T; g.cap = (int)v[6]; g.align = (int)v[7]; g.kpad = (int)v[8]; g.parity = (int)v[9];
+  g.E = 0; g.t_cap = (int)v[5];
   g.off_flags = v[10]; g.off_counts = v[11]; g.off_x = v[12]; g.off_meta = v[13]; g.off_tab = v[14];
   g.off_back = v[15]; g.off_dw = v[16]; g.off_dy = v[17];
   TORCH_CHECK(T <= v[5], "more tokens than the arena holds");
@@ -524,6 +540,7 @@ void ep_dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w, torch::Ten
               dst.scalar_type() == torch::kInt32, "pos / dst: int32 [T, K]");
   TORCH_CHECK(offsets.numel() == g.S + 1 && offsets.scalar_type() == torch::kInt32, "offsets: int32 [S+1]");
   TORCH_CHECK(row_scale.numel() >= g.cap && row_scale.scalar_type() == torch::kFloat32, "row_scale: fp32 [cap]");
+  g.E = (int)dest_tab.numel();
   const int B = g.W * g.S;
   const size_t smem = (size_t)(kEpWarps + 3) * B * sizeof(int);
   const void* fn = reinterpret_cast<const void*>(&ep_dispatch_kernel);

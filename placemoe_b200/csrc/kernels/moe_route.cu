@@ -390,7 +390,7 @@ std::vector<torch::Tensor> moe_plan(torch::Tensor idx, c10::optional<torch::Tens
 // Row movement
 // ----------------------------------------------------------------------------
 // out[r] = src[row_token[r]] for r < offsets[S] (zero rows where row_token < 0)
-__global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* __restrict__ src,
+__global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int nsrc,
                                                           const int* __restrict__ row_token,
                                                           const int* __restrict__ end_ptr, int cap, int H,
                                                           __nv_bfloat16* __restrict__ out) {
@@ -399,7 +399,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* _
   for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < end; r += gridDim.x * 8) {
     const int t = row_token[r];
     uint4* o = reinterpret_cast<uint4*>(out + (size_t)r * H);
-    if (t < 0) {
+    if (t < 0 || !PM_INDEX_OK(t < nsrc)) {
       for (int i = threadIdx.x & 31; i < vec; i += 32) o[i] = make_uint4(0, 0, 0, 0);
     } else {
       const uint4* s = reinterpret_cast<const uint4*>(src + (size_t)t * H);
@@ -409,7 +409,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(const __nv_bfloat16* _
 }
 
 // out[t] = sum_k src[row_of[t*K + k]]  (rows < 0 skipped), fp32 accumulation
-__global__ void __launch_bounds__(256) sum_rows_kernel(const __nv_bfloat16* __restrict__ src,
+__global__ void __launch_bounds__(256) sum_rows_kernel(const __nv_bfloat16* __restrict__ src, int nsrc,
                                                        const int* __restrict__ row_of, int T, int K, int H,
                                                        __nv_bfloat16* __restrict__ out) {
   const int vec = H / 8;
@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(256) sum_rows_kernel(const __nv_bfloat16* __re
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int k = 0; k < K; ++k) {
         const int r = row_of[(size_t)t * K + k];
-        if (r < 0) continue;
+        if (r < 0 || !PM_INDEX_OK(r < nsrc)) continue;
         const uint4 q = reinterpret_cast<const uint4*>(src + (size_t)r * H)[i];
         const uint32_t u[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -435,12 +435,12 @@ __global__ void __launch_bounds__(256) sum_rows_kernel(const __nv_bfloat16* __re
 }
 
 // out[a] = vals[row_of[a]] (0 where row_of < 0): per-assignment values from per-row values
-__global__ void gather_scalar_kernel(const float* __restrict__ vals, const int* __restrict__ row_of, int n,
+__global__ void gather_scalar_kernel(const float* __restrict__ vals, int nvals, const int* __restrict__ row_of, int n,
                                      float* __restrict__ out) {
   const int a = blockIdx.x * blockDim.x + threadIdx.x;
   if (a < n) {
     const int r = row_of[a];
-    out[a] = r >= 0 ? vals[r] : 0.f;
+    out[a] = (r >= 0 && PM_INDEX_OK(r < nvals)) ? vals[r] : 0.f;
   }
 }
 
@@ -463,7 +463,8 @@ void gather_rows(torch::Tensor src, torch::Tensor row_token, c10::optional<torch
   const int* ep = end.has_value() ? end->data_ptr<int>() : nullptr;
   const int grid = std::max(1, std::min((cap + 7) / 8, sms() * 8));
   gather_rows_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)src.data_ptr(), row_token.data_ptr<int>(), ep, cap, H, (__nv_bfloat16*)out.data_ptr());
+      (const __nv_bfloat16*)src.data_ptr(), (int)src.size(0), row_token.data_ptr<int>(), ep, cap, H,
+      (__nv_bfloat16*)out.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -478,7 +479,8 @@ void sum_rows(torch::Tensor src, torch::Tensor row_of, torch::Tensor out) {
   if (T == 0) return;
   const int grid = std::max(1, std::min((T + 7) / 8, sms() * 8));
   sum_rows_kernel<<<grid, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)src.data_ptr(), row_of.data_ptr<int>(), T, K, H, (__nv_bfloat16*)out.data_ptr());
+      (const __nv_bfloat16*)src.data_ptr(), (int)src.size(0), row_of.data_ptr<int>(), T, K, H,
+      (__nv_bfloat16*)out.data_ptr());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -489,7 +491,7 @@ torch::Tensor gather_scalar(torch::Tensor vals, torch::Tensor row_of) {
   auto out = torch::empty(row_of.sizes(), vals.options());
   if (n == 0) return out;
   gather_scalar_kernel<<<(n + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      vals.data_ptr<float>(), row_of.data_ptr<int>(), n, out.data_ptr<float>());
+      vals.data_ptr<float>(), (int)vals.numel(), row_of.data_ptr<int>(), n, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }

@@ -30,6 +30,7 @@ enum PeerWait : int {
   kWaitEpRows = 4,       // dispatch: rows stored
   kWaitEpCombine = 5,    // combine: partial sums stored
   kWaitEpScatter = 6,    // backward scatter: output gradients stored
+  kWhereIndexCheck = 7,  // an index read from data was out of range (bounds-checked debug build)
 };
 
 PM_DEVICE unsigned long long now_ns() {
@@ -58,6 +59,18 @@ PM_DEVICE bool status_failed(const int* st) { return ld_volatile_i32(st) != 0; }
 PM_DEVICE void status_fail(int* st, int code, int where) {
   if (atomicCAS(st, 0, code) == 0) atomicExch(st + 1, where);
 }
+
+// Index check of the bounds-checked debug build for the peer-memory kernels: a bad index
+// sets kErrBounds in the sticky status block and the caller skips the access.
+#ifdef PLACEMOE_DEBUG_BOUNDS
+PM_DEVICE bool peer_index_ok(int* st, bool cond) {
+  if (!cond) status_fail(st, kErrBounds, kWhereIndexCheck);
+  return cond;
+}
+#define PM_PEER_INDEX_OK(st, cond) (::pm::peer_index_ok((st), (cond)))
+#else
+#define PM_PEER_INDEX_OK(st, cond) (true)
+#endif
 
 // Threads 0..world-1 of the calling CTA take part (the caller syncs the CTA around it).
 // Returns false when the budget ran out or an earlier wait had already failed.

@@ -14,7 +14,6 @@ path identical and uses a minimal tower.
 
 from __future__ import annotations
 
-import os
 import time
 
 import torch
@@ -105,4 +104,4 @@ class VLMTrainer(TextTrainer):
         return tr
 
 
-__all__ = ["VLMTrainer", "VisionTower", "os"]
+__all__ = ["VLMTrainer", "VisionTower"]
