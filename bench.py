@@ -57,6 +57,16 @@ def parse():
     p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
     p.add_argument("--dense-sharding", default="auto", choices=["auto", "on", "off"],
                    help="shard dense masters/moments/gradients over the ranks (peer-memory RS/AG); auto = N > 1")
+    p.add_argument("--adaptive", type=int, default=0,
+                   help="N > 1: after the timed run, N steps with PlaceMoE hot updates while the router bias "
+                        "rotates, then N steps on the static placement for comparison")
+    p.add_argument("--rotate-every", type=int, default=50, help="adaptive run: rotate the bias every R steps")
+    p.add_argument("--rotate-by", type=int, default=16, help="adaptive run: experts per rotation")
+    p.add_argument("--mapping-every", type=int, default=20, help="adaptive run: mapping-only update interval")
+    p.add_argument("--layout-every", type=int, default=100, help="adaptive run: full (layout) update interval")
+    p.add_argument("--ulysses", type=int, default=1,
+                   help="Ulysses sequence-parallel group size (consecutive ranks share a batch; attention runs "
+                        "on whole sequences over head groups)")
     p.add_argument("--recompute-expert-rows", action="store_true",
                    help="re-gather dispatched expert inputs in the backward instead of keeping them (memory)")
     args = p.parse_args()
@@ -178,6 +188,73 @@ def plan_placement(trainer, pool, args, rank, world):
             "mean_dedup_ratio": round(agg.get("mean_dedup_ratio", 0.0), 3)}
 
 
+def adaptive_run(trainer, pool, args, rank, world):
+    """Hot-update run: ``args.adaptive`` steps with mapping-only updates every ``mapping_every`` steps and
+    full layout updates (expert weights + AdamW moments migrated peer to peer) every ``layout_every``
+    steps, planned asynchronously on rank 0's CPU from captured routes, while the router bias
+    permutation rotates by ``rotate_by`` experts every ``rotate_every`` steps.  Then the same number of
+    steps, same rotation, on the static placement (run first, before any update).  Device time is measured
+    with CUDA events around every step (max over ranks)."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    from placemoe_b200.parallel.hot_update import HotUpdateManager
+    from placemoe_b200.placemoe.runtime.config import HotUpdateConfig, PlaceMoEPlannerResources, PlaceMoERuntimeConfig
+
+    root = tempfile.mkdtemp(prefix="pm_hot_") if rank == 0 else ""
+    holder = [root]
+    dist.broadcast_object_list(holder, src=0)
+    cfg = PlaceMoERuntimeConfig(
+        hot_update=HotUpdateConfig(enabled=True, layout_interval_steps=args.layout_every,
+                                   mapping_interval_steps=args.mapping_every, work_root=holder[0]),
+        resources=PlaceMoEPlannerResources(workers=min(8, os.cpu_count() or 1), candidate_workers=1))
+    blocks = trainer.model.moe_blocks()
+    base = [blk.router_bias.clone() for blk in blocks]
+
+    def run(n, manager):
+        trainer.hot_update = manager
+        for blk, b in zip(blocks, base):
+            blk.router_bias.copy_(b)
+        times = []
+        for i in range(n):
+            if i and i % args.rotate_every == 0:
+                for blk in blocks:
+                    blk.router_bias.copy_(torch.roll(blk.router_bias, args.rotate_by))
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            trainer.train_step(next(pool), read_loss=False)
+            e.record()
+            times.append((s, e))
+        torch.cuda.synchronize()
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in times)], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        trainer.hot_update = None
+        return float(t.item())
+
+    t_static = run(args.adaptive, None)  # first: the static artifact as installed
+    mgr = HotUpdateManager(trainer, cfg)
+    t_adapt = run(args.adaptive, mgr)
+    tokens = args.batch_per_gpu * args.seq * world * args.adaptive
+    ev = mgr.events
+    applied = [e for e in ev if e["event"] == "applied"]
+    full = [e for e in applied if e["kind"] == "full"]
+    return {
+        "steps": args.adaptive, "rotate_every": args.rotate_every, "rotate_by": args.rotate_by,
+        "mapping_every": args.mapping_every, "layout_every": args.layout_every,
+        "tokens_per_s_adaptive": round(tokens / (t_adapt / 1e3), 1),
+        "tokens_per_s_static": round(tokens / (t_static / 1e3), 1),
+        "mapping_updates": sum(1 for e in applied if e["kind"] == "mapping"),
+        "layout_updates": len(full),
+        "migration_ms_per_layout_update": round(sum(e["migration_ms"] for e in full) / max(1, len(full)), 1),
+        "moved_slots_per_layout_update": round(sum(e["moved_slots"] for e in full) / max(1, len(full)), 1),
+        "planner_ms_mean": round(sum(e["planner_ms"] for e in applied) / max(1, len(applied)), 1),
+        "staleness_steps_mean": round(sum(e["staleness_steps"] for e in applied) / max(1, len(applied)), 2),
+        "failed_or_stale": sum(1 for e in ev if e["event"] in ("failed", "rejected_stale")),
+    }
+
+
 def run_reference(args):
     from baseline_reference import run as ref_run  # noqa: E402  (baseline/ helper)
 
@@ -221,9 +298,10 @@ def main():
                       micro_batch_size=args.micro_batch, redundant_slots_per_rank=args.redundant_slots,
                       placemoe_artifact=args.artifact, total_steps=args.warmup + 2 * args.steps + 1,
                       ep_transport=args.ep_transport, recompute_expert_rows=args.recompute_expert_rows,
-                      dense_sharding=args.dense_sharding)
+                      dense_sharding=args.dense_sharding, ulysses_size=args.ulysses)
     trainer = Trainer(cfg, mcfg)
-    pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank)
+    # ranks of one sequence-parallel group read the same sequences (each keeps its chunk of them)
+    pool = PinnedBatchPool(mcfg.vocab_size, args.batch_per_gpu, args.seq, n=2, seed=0, rank=rank // args.ulysses)
     dev_batches = [b.to("cuda") for b in pool.batches]
 
     def barrier():
@@ -280,6 +358,7 @@ def main():
         barrier()
         a2a = p2p_ep.TIMER.phases()
         p2p_ep.TIMER = None
+    adaptive = adaptive_run(trainer, pool, args, rank, world) if args.adaptive > 0 and world > 1 else None
     names = ["dispatch", "combine", "scatter", "combine_bwd"]
     t = torch.tensor([ms, ms_e2e, sum(a2a.values())] + [a2a.get(n, 0.0) for n in names], device="cuda")
     if world > 1:
@@ -287,7 +366,7 @@ def main():
     vals = t.tolist()
     ms, ms_e2e, a2a_ms = vals[:3]
     a2a_phases = dict(zip(names, (round(v, 3) for v in vals[3:])))
-    tokens = args.batch_per_gpu * args.seq * world
+    tokens = args.batch_per_gpu * args.seq * world // args.ulysses  # an SP group shares its sequences
     value = tokens / (ms / 1e3)
     e2e = tokens / (ms_e2e / 1e3)
     if rank == 0:
@@ -308,10 +387,12 @@ def main():
             "config": {
                 "model": f"{args.model} ({mcfg.num_hidden_layers}L, H{mcfg.hidden_size}, {mcfg.num_experts}E "
                          f"top{mcfg.num_experts_per_tok}, I{mcfg.moe_intermediate_size}, V{mcfg.vocab_size})",
-                "global_batch": args.batch_per_gpu * world,
+                "global_batch": args.batch_per_gpu * world // args.ulysses,
                 "seq_len": args.seq,
                 "micro_batch": args.micro_batch,
-                "parallelism": f"dp{world}+ep{world}" + ("+dense-shard" if trainer.dense_shards is not None else ""),
+                "parallelism": f"dp{world // args.ulysses}+ep{world}" +
+                               (f"+sp{args.ulysses}" if args.ulysses > 1 else "") +
+                               ("+dense-shard" if trainer.dense_shards is not None else ""),
                 "ep_transport": args.ep_transport if world > 1 else "none",
                 "placement": ((f"PlaceMoE static L,M planned from {args.plan_steps} captured steps, "
                                if args.placement == "placemoe" else
@@ -331,6 +412,7 @@ def main():
             "gpu_launches": launches,
             "peak_mem_gb": round(torch.cuda.max_memory_allocated() / 2**30, 1),
             "planner": plan_info,
+            "adaptive": adaptive,
             "model_tflops_per_gpu": round(flops / (ms / 1e3) / world / 1e12, 1),
         }
         print(json.dumps(line), flush=True)

@@ -48,6 +48,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &pm::ep_dispatch);
   m.def("ep_combine", &pm::ep_combine);
   m.def("ep_scatter", &pm::ep_scatter);
+  m.def("sp_exchange", &pm::sp_exchange);
   m.def("device_error", &pm::device_error, "read (and optionally clear) the kernels' error words");
 #ifdef PLACEMOE_DEBUG_BOUNDS
   m.def("debug_bounds", [] { return true; }, "built with the index checks of the debug build");

@@ -31,6 +31,7 @@ enum PeerWait : int {
   kWaitEpCombine = 5,    // combine: partial sums stored
   kWaitEpScatter = 6,    // backward scatter: output gradients stored
   kWhereIndexCheck = 7,  // an index read from data was out of range (bounds-checked debug build)
+  kWaitSpExchange = 8,   // Ulysses sequence-parallel exchange
 };
 
 PM_DEVICE unsigned long long now_ns() {

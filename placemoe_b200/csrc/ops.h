@@ -86,6 +86,10 @@ void ep_scatter(torch::Tensor dy, torch::Tensor pos, torch::Tensor dst, torch::T
                 std::vector<int64_t> geo, torch::Tensor scratch, torch::Tensor status, int64_t epoch,
                 double timeout_s);
 
+// Ulysses sequence-parallel exchange over peer memory (sp_exchange.cu)
+void sp_exchange(torch::Tensor in, torch::Tensor out, torch::Tensor peers, std::vector<int64_t> geo,
+                 torch::Tensor scratch, torch::Tensor status, int64_t epoch, double timeout_s);
+
 int device_error(bool reset);
 }  // namespace pm
 

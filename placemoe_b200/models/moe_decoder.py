@@ -67,13 +67,27 @@ class Attention(nn.Module):
         self.register_buffer("inv_freq", norm_ops.rope_inv_freq(d, cfg.rope_theta), persistent=False)
 
     def forward(self, x, pos, seq_len, docs=None):
-        # x: [T, H] (T = batch * seq_len, packed by sequence); docs: per-token document bounds
+        # x: [T, H] (T = batch * seq_len, packed by sequence); docs: per-token document bounds.
+        # With Ulysses sequence parallelism (self.sp) x holds this rank's chunk of seq_len tokens of
+        # every sequence; q, k, v are re-split by heads around the attention over whole sequences.
+        sp = getattr(self, "sp", None)
+        full = seq_len * (sp.size if sp is not None else 1)
         qkv = mp_ops.linear(x, self.qkv_proj)
         q, k, v = norm_ops.qkv_norm_rope(qkv, self.q_norm, self.k_norm, pos, self.inv_freq, self.hq, self.hkv,
                                          self.d, self.q_group, self.k_group, self.cfg.rms_norm_eps,
-                                         max_pos=seq_len)
-        o = attn_ops.causal_attention(q, k, v, seq_len, docs)  # [T, Hq, D]
-        o = o.reshape(o.shape[0], -1)
+                                         max_pos=full)
+        if sp is None:
+            o = attn_ops.causal_attention(q, k, v, seq_len, docs)  # [T, Hq, D]
+            o = o.reshape(o.shape[0], -1)
+        else:
+            if docs is not None:
+                raise NotImplementedError("packed documents with sequence parallelism")
+            from ..parallel.ulysses import heads_to_seq, seq_to_heads
+
+            b = x.shape[0] // seq_len
+            q, k, v = (seq_to_heads(t, sp, b, seq_len) for t in (q, k, v))
+            o = attn_ops.causal_attention(q, k, v, full)  # [B*S, Hq/P, D]
+            o = heads_to_seq(o, sp, b, seq_len)
         return mp_ops.linear(o, self.o_proj)
 
 
@@ -261,7 +275,12 @@ class MoEForCausalLM(nn.Module):
         ids = input_ids.reshape(-1)
         x = mp_ops.embedding(ids, self.embed_tokens, self._anchor(ids.device))
         docs = None
-        if cu_seqlens is None:
+        sp = getattr(self, "sp", None)
+        if sp is not None:  # this rank's chunk of every sequence starts at position rank * s
+            if cu_seqlens is not None:
+                raise NotImplementedError("packed documents with sequence parallelism")
+            pos = (torch.arange(s, device=ids.device, dtype=torch.int32) + sp.rank * s).repeat(b)
+        elif cu_seqlens is None:
             pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)
         else:
             docs = attn_ops.doc_bounds(cu_seqlens.to(ids.device), b * s, s)
@@ -273,21 +292,39 @@ class MoEForCausalLM(nn.Module):
                 x = layer(x, pos, s, docs)
         return self.norm(x)
 
+    def set_sequence_parallel(self, sp) -> None:
+        """Run attention with Ulysses sequence parallelism over ``sp`` (a parallel.ulysses.UlyssesGroup)."""
+        self.sp = sp
+        for layer in self.layers:
+            layer.self_attn.sp = sp
+
     def forward(self, input_ids: torch.Tensor, labels: torch.Tensor | None = None, loss_denom=None,
-                cu_seqlens: torch.Tensor | None = None):
+                cu_seqlens: torch.Tensor | None = None, shifted_labels: torch.Tensor | None = None):
         """Returns (loss, aux_loss) with labels, else logits [B, S, V].  With ``cu_seqlens`` the last
-        token of a document predicts nothing (no loss across document boundaries)."""
+        token of a document predicts nothing (no loss across document boundaries).  ``shifted_labels``
+        (the next-token targets, already shifted) replace ``labels`` -- sequence-parallel ranks pass
+        their chunk of the targets of the whole sequence."""
         h = self.hidden_states(input_ids, cu_seqlens)
         w = self.embed_tokens if self.lm_head is None else self.lm_head
-        if labels is None:
+        if labels is None and shifted_labels is None:
             logits = mp_ops.linear(h, w)
             return logits.reshape(*input_ids.shape, -1)
+        if shifted_labels is not None:
+            loss = loss_ops.fused_linear_cross_entropy(h, w, shifted_labels, denom=loss_denom)
+            aux = None
+            for blk in self.moe_blocks():
+                if blk.last_aux_loss is not None:
+                    aux = blk.last_aux_loss if aux is None else aux + blk.last_aux_loss
+            return loss, aux
         shifted = torch.full_like(labels, loss_ops.IGNORE_INDEX)
         shifted[:, :-1] = labels[:, 1:]
         if cu_seqlens is not None:
             ends = cu_seqlens.to(labels.device).long()[1:] - 1  # last token of every document
             flat = shifted.view(-1)
             flat[ends] = loss_ops.IGNORE_INDEX
+        if loss_denom is None:  # targets counted on the host: no device read in the middle of the step
+            b, s = labels.shape
+            loss_denom = max(b * s - (cu_seqlens.numel() - 1 if cu_seqlens is not None else b), 1)
         loss = loss_ops.fused_linear_cross_entropy(h, w, shifted, denom=loss_denom)
         aux = None
         for blk in self.moe_blocks():

@@ -62,7 +62,8 @@ _P2P_STATUS: dict = {}
 
 # identifiers of the wait that gave up first (status word 1, see csrc/kernels/peer.cuh)
 _WAIT_NAMES = {1: "p2p barrier", 2: "grid barrier", 3: "dispatch count exchange", 4: "dispatch rows",
-               5: "combine partial sums", 6: "backward scatter"}
+               5: "combine partial sums", 6: "backward scatter", 7: "index check (debug build)",
+               8: "sequence-parallel exchange"}
 _ERROR_NAMES = {1: "mbarrier wait timed out", 2: "peer wait timed out", 3: "bounds check failed", 4: "bad arguments"}
 
 

@@ -67,6 +67,7 @@ class TrainConfig:
     capture_routes: bool = False
     ep_transport: str = "auto"
     recompute_expert_rows: bool = False  # drop dispatched expert inputs after forward, re-gather in backward  # "auto" | "p2p" | "nccl"
+    ulysses_size: int = 1  # sequence-parallel ranks per group (consecutive ranks; they share one batch)
     gradient_checkpointing: bool = False
     activation_offload: bool = False  # saved activations to pinned host memory (utils/offload.py)
     device: str = "cuda"
@@ -133,6 +134,18 @@ class Trainer:
             self.peer_exchange = PeerExchange(None, self.device, nbytes)
             self.replica_sync = ReplicaGradSync(self.peer_exchange)
             self.pstate.ep.replica_sync = self.replica_sync
+        self.sp = None
+        if cfg.ulysses_size > 1:
+            from ..parallel.ulysses import build_ulysses_groups
+
+            mc = self.model_cfg
+            if mc.num_key_value_heads % cfg.ulysses_size or mc.num_attention_heads % cfg.ulysses_size:
+                raise ValueError("attention heads must split over the sequence-parallel ranks")
+            if cfg.seq_len % cfg.ulysses_size:
+                raise ValueError("seq_len must split over the sequence-parallel ranks")
+            widest = cfg.micro_batch_size * cfg.seq_len // cfg.ulysses_size * mc.q_size
+            self.sp = build_ulysses_groups(cfg.ulysses_size, self.device, widest)
+            self.model.set_sequence_parallel(self.sp)
         self.dense_shards = None
         if self._want_dense_sharding():
             self._setup_dense_shards()
@@ -213,7 +226,23 @@ class Trainer:
         from ..utils.offload import ActivationOffload
 
         with ActivationOffload(enabled=self.cfg.activation_offload and self.device.type == "cuda"):
-            if cu_seqlens is None:
+            if self.sp is not None:
+                if cu_seqlens is not None:
+                    raise NotImplementedError("packed documents with sequence parallelism")
+                # every rank of the SP group holds the same sequences: take this rank's chunk of the tokens and
+                # of the next-token targets of the whole sequence; the loss divisor is the group's target
+                # count over P, so the mean of the P chunk losses is the loss of the whole batch
+                from ..ops.loss import IGNORE_INDEX
+
+                b, s = input_ids.shape
+                p, r = self.sp.size, self.sp.rank
+                chunk = s // p
+                targets = torch.full_like(input_ids, IGNORE_INDEX)
+                targets[:, :-1] = input_ids[:, 1:]
+                sl = slice(r * chunk, (r + 1) * chunk)
+                loss, aux = self.model(input_ids[:, sl].contiguous(), shifted_labels=targets[:, sl].contiguous(),
+                                       loss_denom=b * (s - 1) / p)
+            elif cu_seqlens is None:
                 loss, aux = self.model(input_ids, labels=input_ids)
             else:
                 loss, aux = self.model(input_ids, labels=input_ids, cu_seqlens=cu_seqlens)
