@@ -24,9 +24,15 @@ rank plus 1.2 GB of expert weights), so no explicit flush is done.
 Roofline per rank (reported as the max over ranks):
   compute  = 18 * A_r * H * I flops (fc1 2I-wide + fc2; fwd, dgrad, wgrad) over the
              measured bf16 GEMM peak;
-  NVLink   = bytes leaving this GPU (dispatch + combine rows, both passes) over
-             770 GB/s per direction;
+  NVLink   = bytes leaving this GPU (dispatch + combine rows, both passes) over the
+             link bandwidth measured at start-up: a peer pull of 256 MiB from the next
+             rank (``p2p_pull``, CUDA events, best of 5, min over ranks); 770 GB/s per
+             direction when the probe is skipped;
   target   = max(compute, NVLink); frac = target / measured.
+Per fused communication kernel (peer-memory transport) the bench also reports its
+time (max over ranks), the NVLink bytes it moves and the achieved GB/s against the
+measured link: dispatch moves the deduplicated rows out, combine the pre-reduced
+partials back, scatter the output gradients out, combine_bwd the data gradients back.
 """
 
 from __future__ import annotations
@@ -40,7 +46,31 @@ import torch
 import torch.distributed as dist
 import torch.nn.functional as F
 
-LINK_GBS = 770.0
+LINK_GBS = 770.0  # per direction, the pool's measured peer copy; used when the probe is skipped
+
+
+def measure_link_gbs(world: int, rank: int, nbytes: int = 256 << 20) -> float:
+    """Peer pull bandwidth from rank+1 into this GPU (GB/s, best of 5; min over ranks)."""
+    from ..ops import kernels
+    from ..parallel.p2p_sync import FLAGS_BYTES, PeerExchange
+
+    x = PeerExchange(None, "cuda", nbytes)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    src = (rank + 1) % world
+    best = float("inf")
+    for i in range(6):
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        kernels().p2p_pull(dst, x.peers, src, FLAGS_BYTES)
+        e.record()
+        torch.cuda.synchronize()
+        if i:
+            best = min(best, s.elapsed_time(e))
+    gbs = torch.tensor([nbytes / (best * 1e-3) / 1e9], device="cuda")
+    dist.all_reduce(gbs, op=dist.ReduceOp.MIN)
+    del x
+    return float(gbs.item())
 
 
 def _peaks():
@@ -127,6 +157,8 @@ def run(args):
         os.environ.setdefault("RANK", "0")
         os.environ.setdefault("WORLD_SIZE", "1")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if world > 1 and not args.no_link_probe and not args.link_gbs:
+        args.link_gbs = measure_link_gbs(world, rank)
     cfg = get_preset("olmoe_1b_7b", hidden_size=args.hidden, moe_intermediate_size=args.inter,
                      num_experts=args.experts, num_experts_per_tok=args.topk, router_bias_zipf_s=args.skew,
                      router_bias_scale=1.0, router_aux_loss_coef=0.0, norm_topk_prob=False)
@@ -209,7 +241,8 @@ def run(args):
     gemm_ms = 18.0 * A_recv.max().item() * h * i / (peak_tf * 1e12) * 1e3
     # bytes leaving a GPU: dispatch rows out + combine partials back, in forward and backward
     link_bytes = 2 * (rows_out + rows_in).max().item() * h * 2
-    link_ms = link_bytes / (LINK_GBS * 1e9) * 1e3
+    link_gbs = args.link_gbs or LINK_GBS
+    link_ms = link_bytes / (link_gbs * 1e9) * 1e3
     t = torch.tensor([float(np.median(fwd_ms)), float(np.median(bwd_ms))], device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ph = torch.tensor([phases.get(kk, 0.0) for kk in sorted(phases)], device="cuda", dtype=torch.float64)
@@ -228,7 +261,19 @@ def run(args):
            "remote_rows_out_max": int(rows_out.max().item()),
            "tflops_per_rank": round(18.0 * A_recv.max().item() * h * i / ((f + b) * 1e-3) / 1e12, 1)}
     if ph.numel():
-        row["phases_ms_max_over_ranks"] = {kk: round(v, 3) for kk, v in zip(sorted(phases), ph.tolist())}
+        pm = dict(zip(sorted(phases), ph.tolist()))
+        row["phases_ms_max_over_ranks"] = {kk: round(v, 3) for kk, v in pm.items()}
+        # NVLink bytes per fused kernel (max over ranks): rows out for dispatch / scatter, rows back for
+        # the combines (pre-reduced: one partial per (token, GPU) pair)
+        moved = {"dispatch": rows_out.max().item() * h * 2, "scatter": rows_out.max().item() * h * 2,
+                 "combine": rows_in.max().item() * h * 2, "combine_bwd": rows_in.max().item() * h * 2}
+        row["fused_kernels"] = {
+            kk: {"ms": round(pm[kk], 3), "nvlink_bytes": int(moved[kk]),
+                 "achieved_gbs": round(moved[kk] / (pm[kk] * 1e-3) / 1e9, 1),
+                 "frac_of_link": round(moved[kk] / (pm[kk] * 1e-3) / 1e9 / link_gbs, 3)}
+            for kk in pm if kk in moved and pm[kk] > 0}
+        row["link_gbs"] = round(link_gbs, 1)
+        row["link_source"] = "measured peer pull" if args.link_gbs else "nominal pool figure"
     if rank == 0:
         print(json.dumps(row), flush=True)
     if isinstance(blk.ep, p2p_ep.P2PExpertParallel):
@@ -247,9 +292,11 @@ def main():
     ap.add_argument("--skew", type=float, default=1.0)
     ap.add_argument("--transport", default="p2p", choices=("p2p", "nccl", "baseline"))
     ap.add_argument("--sweep", action="store_true", help="tokens {2048,8192,16384} x skew {0,0.6,1.0,1.4}")
+    ap.add_argument("--no-link-probe", action="store_true", help="use 770 GB/s instead of measuring the link")
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--iters", type=int, default=5)
     args = ap.parse_args()
+    args.link_gbs = 0.0
     if args.sweep:
         for tk in (2048, 8192, 16384):
             for s in (0.0, 0.6, 1.0, 1.4):
