@@ -76,6 +76,8 @@ def main(args) -> int:
     if args.model not in SHAPES:
         return _unavailable(f"reference arm is defined for {sorted(SHAPES)} (got {args.model})")
     shape = SHAPES[args.model]
+    # the reference trainer's default is activation recomputation on; --ref-no-recompute measures it off
+    ckpt = not getattr(args, "ref_no_recompute", False)
     sys.path.insert(0, REF)
     import torch
     import torch.distributed as dist
@@ -109,7 +111,7 @@ def main(args) -> int:
     ps = get_parallel_state()
     configure_hiermoe(HierMoEConfig(), ep_group=ps.ep_group if getattr(ps, "ep_enabled", False) else None,
                       ep_fsdp_size=ps.ep_fsdp_size if getattr(ps, "ep_enabled", False) else 1,
-                      activation_checkpointing_enabled=True, fsdp_offload_enabled=False,
+                      activation_checkpointing_enabled=ckpt, fsdp_offload_enabled=False,
                       gradient_bytes_per_element=4)
     ops = OpsImplementationConfig(attn_implementation="sdpa", moe_implementation="fused_triton",
                                   cross_entropy_loss_implementation="eager", rms_norm_implementation="eager",
@@ -126,7 +128,7 @@ def main(args) -> int:
                                    init_device=init_device, ops_implementation=ops)
     model = build_parallelize_model(model, init_device=init_device, weights_path=None, enable_reshard_after_forward=True,
                                     mixed_precision=MixedPrecisionConfig(enable=mp_on),
-                                    enable_gradient_checkpointing=True,
+                                    enable_gradient_checkpointing=ckpt,
                                     basic_modules=list(getattr(model, "_no_split_modules", None) or []),
                                     enable_forward_prefetch=True)
     model.train()
@@ -192,7 +194,8 @@ def main(args) -> int:
                        "precision": "fsdp2 mixed precision (fp32 masters, bf16 compute)" if mp_on
                        else "bf16 parameters and optimizer states (no FSDP on one GPU)",
                        "micro_batch": mb, "parallelism": f"fsdp{world}+ep{world}",
-                       "ops": "moe fused_triton, attention sdpa, gradient checkpointing on"},
+                       "ops": "moe fused_triton, attention sdpa, gradient checkpointing "
+                              + ("on (its trainer default)" if ckpt else "off")},
             "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": pool[0].numel() * 8, "d2h_bytes_per_step": 4, "last_loss": last},
         }), flush=True)

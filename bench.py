@@ -64,6 +64,8 @@ def parse():
     p.add_argument("--rotate-by", type=int, default=16, help="adaptive run: experts per rotation")
     p.add_argument("--mapping-every", type=int, default=20, help="adaptive run: mapping-only update interval")
     p.add_argument("--layout-every", type=int, default=100, help="adaptive run: full (layout) update interval")
+    p.add_argument("--ref-no-recompute", action="store_true",
+                   help="reference arm: gradient checkpointing off (its trainer default is on)")
     p.add_argument("--ulysses", type=int, default=1,
                    help="Ulysses sequence-parallel group size (consecutive ranks share a batch; attention runs "
                         "on whole sequences over head groups)")

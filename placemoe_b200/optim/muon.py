@@ -33,8 +33,26 @@ from ..ops.optim import param_grad
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
 
 
+def _ns_matrix_cuda(x: torch.Tensor, steps: int) -> torch.Tensor:
+    """Newton-Schulz iterations of one wide bf16 matrix [m, n] (m <= n) on the tcgen05 GEMMs."""
+    from ..ops.gemm import gemm_nn, gemm_nt
+
+    a, b, c = NS_COEFFS
+    x = x.contiguous()
+    for _ in range(steps):
+        s = gemm_nt(x, x)  # x x^T   [m, m]
+        y = torch.add(s, gemm_nn(s, s), alpha=c / b).mul_(b)  # b*s + c*s^2
+        x = torch.add(gemm_nn(y, x), x, alpha=a)  # a*x + y x
+    return x
+
+
 def zeropower_newton_schulz(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
-    """Approximate orthogonal factor of the last two dims of ``g`` (batched over leading dims)."""
+    """Approximate orthogonal factor of the last two dims of ``g`` (batched over leading dims).
+
+    CUDA runs the three products of every iteration on the tcgen05 GEMM kernels (bf16 operands, fp32
+    accumulation), one matrix at a time; the kernels need both dims to be multiples of 8, other shapes
+    (tiny test matrices) are rejected.  CPU runs the same iteration in fp32 with torch matmuls.
+    """
     if g.dim() < 2:
         raise ValueError("Newton-Schulz needs a matrix")
     a, b, c = NS_COEFFS
@@ -43,10 +61,17 @@ def zeropower_newton_schulz(g: torch.Tensor, steps: int = 5, eps: float = 1e-7) 
     if tall:
         x = x.mT
     x = x / (x.norm(dim=(-2, -1), keepdim=True) + eps)
-    for _ in range(steps):
-        s = x @ x.mT
-        y = b * s + c * (s @ s)
-        x = a * x + y @ x
+    if x.is_cuda:
+        if x.size(-2) % 8 or x.size(-1) % 8:
+            raise ValueError(f"Muon on CUDA needs matrix dims that are multiples of 8, got {tuple(x.shape[-2:])}")
+        lead = x.shape[:-2]
+        flat = x.reshape(-1, x.size(-2), x.size(-1))
+        x = torch.stack([_ns_matrix_cuda(m, steps) for m in flat.unbind(0)]).reshape(*lead, *x.shape[-2:])
+    else:
+        for _ in range(steps):
+            s = x @ x.mT
+            y = b * s + c * (s @ s)
+            x = a * x + y @ x
     if tall:
         x = x.mT
     return x
