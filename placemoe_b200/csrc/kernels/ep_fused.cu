@@ -101,6 +101,39 @@ PM_DEVICE void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ 
   for (; v < n16; v += 32) dst[v] = __ldcg(src + v);
 }
 
+// acc[0..7] += the eight bf16 values of u
+PM_DEVICE void add_bf16x8(float (&acc)[8], const uint4& u) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    acc[2 * c] += bf16_lo(w[c]);
+    acc[2 * c + 1] += bf16_hi(w[c]);
+  }
+}
+
+// Sum in fp32 of chunk v (16 bytes) of up to kEpMaxK rows src[idx[i] * stride16 + v], i < cnt; the loads of
+// four rows are issued before their adds so a warp keeps several row reads in flight.
+template <bool LDCG>
+PM_DEVICE uint4 sum_rows_chunk(const uint4* __restrict__ src, const int (&idx)[16], int cnt, size_t stride16,
+                               int v) {
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int i0 = 0; i0 < 16; i0 += 4) {
+    if (i0 < cnt) {
+      uint4 u[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4* a = src + (size_t)idx[i0 + j] * stride16 + v;
+        u[j] = i0 + j < cnt ? (LDCG ? __ldcg(a) : __ldg(a)) : make_uint4(0u, 0u, 0u, 0u);  // bf16 zeros
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) add_bf16x8(acc, u[j]);
+    }
+  }
+  return make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
+                    pack_bf16(acc[6], acc[7]));
+}
+
 PM_DEVICE void warp_zero_row(uint4* __restrict__ dst, int n16, int lane) {
   for (int v = lane; v < n16; v += 32) dst[v] = make_uint4(0, 0, 0, 0);
 }
@@ -364,29 +397,14 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     for (int i = 0; i < kEpMaxK; ++i) {
       int v = i < g.kpad ? __ldcg(tab + i) : -1;
       if (v >= 0 && !PM_PEER_INDEX_OK(g.st, v < n)) v = -1;
-      list[i] = v;
       cnt += (v >= 0 && cnt == i) ? 1 : 0;
+      list[i] = v >= 0 ? v : 0;
     }
     const int t = m.w / K;
     uint4* dstrow = reinterpret_cast<uint4*>(reinterpret_cast<char*>(s_peers[m.z]) + g.off_back +
                                              ((size_t)t * W + g.rank) * g.H * 2);
-    for (int v = lane; v < n16; v += 32) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int i = 0; i < kEpMaxK; ++i) {
-        if (i < cnt) {
-          const uint4 u = reinterpret_cast<const uint4*>(rows + (size_t)list[i] * g.H)[v];
-          const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            acc[2 * c] += bf16_lo(uu[c]);
-            acc[2 * c + 1] += bf16_hi(uu[c]);
-          }
-        }
-      }
-      dstrow[v] = make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
-                             pack_bf16(acc[6], acc[7]));
-    }
+    const uint4* src = reinterpret_cast<const uint4*>(rows);
+    for (int v = lane; v < n16; v += 32) dstrow[v] = sum_rows_chunk<false>(src, list, cnt, n16, v);
   }
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpCombine);
 
@@ -402,24 +420,16 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     if (dw_out != nullptr && lane < K)
       dw_out[t * K + lane] = p >= 0 ? __ldcg(reinterpret_cast<const float*>(me + g.off_dw) + t * K + lane) : 0.f;
     const uint4* back = reinterpret_cast<const uint4*>(me + g.off_back + (size_t)t * W * g.H * 2);
-    for (int v = lane; v < n16; v += 32) {
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      unsigned mm = dmask;
-      while (mm) {
-        const int dd = __ffs(mm) - 1;
-        mm &= mm - 1;
-        const uint4 u = __ldcg(back + (size_t)dd * n16 + v);
-        const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
+    int dl[kEpMaxK];  // destination GPUs of this token (at most K), lowest first
+    unsigned mm = dmask;
+    const int nd = min(__popc(dmask), kEpMaxK);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          acc[2 * c] += bf16_lo(uu[c]);
-          acc[2 * c + 1] += bf16_hi(uu[c]);
-        }
-      }
-      reinterpret_cast<uint4*>(out + (size_t)t * g.H)[v] =
-          make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
-                     pack_bf16(acc[6], acc[7]));
+    for (int i = 0; i < kEpMaxK; ++i) {
+      dl[i] = mm ? __ffs(mm) - 1 : 0;
+      mm &= mm - 1;
     }
+    uint4* orow = reinterpret_cast<uint4*>(out + (size_t)t * g.H);
+    for (int v = lane; v < n16; v += 32) orow[v] = sum_rows_chunk<true>(back, dl, nd, n16, v);
   }
 }
 
