@@ -43,7 +43,8 @@ def parse():
     p.add_argument("--seq", type=int, default=4096)
     p.add_argument("--batch-per-gpu", type=int, default=8)
     p.add_argument("--micro-batch", type=int, default=0,
-                   help="sequences per micro-batch (default 4; 2 for qwen3_30b_a3b)")
+                   help="sequences per micro-batch (default 4; 1 for qwen3_30b_a3b, whose 48 layers of saved "
+                        "activations and receive slabs would not fit 180 GB at 2)")
     p.add_argument("--redundant-slots", type=int, default=-1,
                    help="extra expert slots per GPU for replicas (default when N > 1: 4 for qwen3_30b_a3b, "
                         "else 1; 0 on one GPU)")
@@ -73,7 +74,7 @@ def parse():
                    help="re-gather dispatched expert inputs in the backward instead of keeping them (memory)")
     args = p.parse_args()
     if args.micro_batch <= 0:
-        args.micro_batch = 2 if args.model == "qwen3_30b_a3b" else 4
+        args.micro_batch = 1 if args.model == "qwen3_30b_a3b" else 4
     return args
 
 
