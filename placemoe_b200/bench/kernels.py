@@ -196,6 +196,57 @@ def bench_attn_compare(batch, seq, heads, kv_heads, dim, iters):
             print(json.dumps({"op": f"sdpa-{name}[{tag}]", "unavailable": str(e).splitlines()[0][:200]}), flush=True)
 
 
+def bench_ep_local(tokens, iters):
+    """Fused EP kernels on a one-rank group (OLMoE expert shape): every assignment stays on this GPU, so
+    this times the kernels' local work -- histograms, positions, row stores, padding, local copies, the
+    fp32 pre-reduction and token sums -- without NVLink traffic.  Per-kernel CUDA-event times (mean)."""
+    import torch.distributed as dist  # noqa: F401  (the one-rank arena needs no process group)
+
+    from placemoe_b200.models.config import get_preset
+    from placemoe_b200.models.moe_decoder import MoEBlock
+    from placemoe_b200.parallel import p2p_ep
+    from placemoe_b200.parallel.data_parallel import expert_topology
+    from placemoe_b200.parallel.placement import build_placements
+
+    cfg = get_preset("olmoe_1b_7b")
+    topo = expert_topology(cfg.num_experts, 1, 0)
+    with torch.device("cuda"):
+        blk = MoEBlock(cfg, 0, topo.slots_per_rank)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        blk.gate.normal_(0, 0.02)
+        blk.gate_up_proj.normal_(0, 0.02)
+        blk.down_proj.normal_(0, 0.02)
+    blk.placement = build_placements(None, topo, 0, [blk.layer_key])[blk.layer_key]
+    blk.ep = p2p_ep.P2PExpertParallel()
+    blk.ep_slab = 0
+    blk.train()
+    x = torch.randn(tokens, cfg.hidden_size, device="cuda").bfloat16().requires_grad_()
+    dy = torch.randn(tokens, cfg.hidden_size, device="cuda").bfloat16()
+    for _ in range(3):
+        blk(x).backward(dy)
+    torch.cuda.synchronize()
+    acc: dict = {}
+    for _ in range(iters):
+        p2p_ep.TIMER = p2p_ep.PhaseTimer()
+        blk(x).backward(dy)
+        torch.cuda.synchronize()
+        for k, v in p2p_ep.TIMER.phases().items():
+            acc[k] = acc.get(k, 0.0) + v / iters
+    p2p_ep.TIMER = None
+    rows = tokens * cfg.num_experts_per_tok * cfg.hidden_size * 2  # bytes of the expert-side rows
+    tok = tokens * cfg.hidden_size * 2
+    # HBM bytes each kernel must move at one rank: dispatch reads x and writes every expert row (primary
+    # stores + local copies read the primary); combine reads every expert row, writes and re-reads one
+    # partial per token and writes y; scatter mirrors dispatch for dy; combine_bwd mirrors combine.
+    need = {"dispatch": tok + 2 * rows, "scatter": tok + 2 * rows, "combine": rows + 3 * tok,
+            "combine_bwd": rows + 3 * tok}
+    for k in ("dispatch", "combine", "scatter", "combine_bwd"):
+        if k in acc:
+            report(f"ep_{k}[one rank, T{tokens} k{cfg.num_experts_per_tok} H{cfg.hidden_size}]", acc[k],
+                   nbytes=need[k])
+
+
 def bench_memory(tokens, hidden, iters):
     from placemoe_b200.ops import kernels
 
@@ -207,7 +258,8 @@ def bench_memory(tokens, hidden, iters):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", default="all", choices=("all", "gemm", "moe", "attn", "attn_compare", "memory"))
+    ap.add_argument("--op", default="all",
+                    choices=("all", "gemm", "moe", "attn", "attn_compare", "memory", "ep_local"))
     ap.add_argument("--m", type=int, default=8192)
     ap.add_argument("--n", type=int, default=2048)
     ap.add_argument("--k", type=int, default=2048)
@@ -235,6 +287,8 @@ def main():
             bench_moe(a.tokens, a.experts, a.topk, a.hidden, a.inter, a.iters, a.skew, al)
     if a.op in ("all", "attn"):
         bench_attn(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
+    if a.op == "ep_local":
+        bench_ep_local(a.tokens, a.iters)
     if a.op == "attn_compare":
         bench_attn_compare(a.batch, a.seq, a.heads, a.kv_heads, a.dim, a.iters)
     if a.op in ("all", "memory"):
