@@ -88,15 +88,23 @@ PM_DEVICE int nth_set_bit(unsigned m, int n) {
 
 PM_DEVICE int4 ldcg_i4(const void* p) { return __ldcg(reinterpret_cast<const int4*>(p)); }
 
-// Warp-cooperative row copy of n16 16-byte words, four loads in flight per lane.
+// Warp-cooperative row copy of n16 16-byte words: eight loads in flight per lane (a 4 KB row of
+// H = 2048 bf16 in one round), then four, then singles.
 PM_DEVICE void warp_copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int n16, int lane) {
   int v = lane;
+  for (; v + 224 < n16; v += 256) {
+    uint4 u[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) u[j] = __ldcg(src + v + 32 * j);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dst[v + 32 * j] = u[j];
+  }
   for (; v + 96 < n16; v += 128) {
-    const uint4 a = __ldcg(src + v), b = __ldcg(src + v + 32), c = __ldcg(src + v + 64), d = __ldcg(src + v + 96);
-    dst[v] = a;
-    dst[v + 32] = b;
-    dst[v + 64] = c;
-    dst[v + 96] = d;
+    uint4 u[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) u[j] = __ldcg(src + v + 32 * j);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) dst[v + 32 * j] = u[j];
   }
   for (; v < n16; v += 32) dst[v] = __ldcg(src + v);
 }
@@ -404,7 +412,10 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     uint4* dstrow = reinterpret_cast<uint4*>(reinterpret_cast<char*>(s_peers[m.z]) + g.off_back +
                                              ((size_t)t * W + g.rank) * g.H * 2);
     const uint4* src = reinterpret_cast<const uint4*>(rows);
-    for (int v = lane; v < n16; v += 32) dstrow[v] = sum_rows_chunk<false>(src, list, cnt, n16, v);
+    if (cnt == 1)  // one assignment of the token on this GPU: the partial is its row
+      warp_copy_row(dstrow, src + (size_t)list[0] * n16, n16, lane);
+    else
+      for (int v = lane; v < n16; v += 32) dstrow[v] = sum_rows_chunk<false>(src, list, cnt, n16, v);
   }
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpCombine);
 
@@ -429,7 +440,10 @@ __global__ void __launch_bounds__(kEpThreads, 2)
       mm &= mm - 1;
     }
     uint4* orow = reinterpret_cast<uint4*>(out + (size_t)t * g.H);
-    for (int v = lane; v < n16; v += 32) orow[v] = sum_rows_chunk<true>(back, dl, nd, n16, v);
+    if (nd == 1)  // one destination GPU: the token's output is its partial
+      warp_copy_row(orow, back + (size_t)dl[0] * n16, n16, lane);
+    else
+      for (int v = lane; v < n16; v += 32) orow[v] = sum_rows_chunk<true>(back, dl, nd, n16, v);
   }
 }
 
