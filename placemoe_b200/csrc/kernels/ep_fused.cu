@@ -120,22 +120,22 @@ PM_DEVICE void add_bf16x8(float (&acc)[8], const uint4& u) {
 }
 
 // Sum in fp32 of chunk v (16 bytes) of up to kEpMaxK rows src[idx[i] * stride16 + v], i < cnt; the loads of
-// four rows are issued before their adds so a warp keeps several row reads in flight.
+// eight rows are issued before their adds so a warp keeps several row reads in flight.
 template <bool LDCG>
-PM_DEVICE uint4 sum_rows_chunk(const uint4* __restrict__ src, const int (&idx)[16], int cnt, size_t stride16,
+PM_DEVICE uint4 sum_rows_chunk(const uint4* __restrict__ src, const int* idx, int cnt, size_t stride16,
                                int v) {
   float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int i0 = 0; i0 < 16; i0 += 4) {
+  for (int i0 = 0; i0 < 16; i0 += 8) {
     if (i0 < cnt) {
-      uint4 u[4];
+      uint4 u[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 8; ++j) {
         const uint4* a = src + (size_t)idx[i0 + j] * stride16 + v;
         u[j] = i0 + j < cnt ? (LDCG ? __ldcg(a) : __ldg(a)) : make_uint4(0u, 0u, 0u, 0u);  // bf16 zeros
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) add_bf16x8(acc, u[j]);
+      for (int j = 0; j < 8; ++j) add_bf16x8(acc, u[j]);
     }
   }
   return make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
@@ -382,6 +382,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
                       const int* __restrict__ pos, const int* __restrict__ dst, const int* __restrict__ offsets,
                       __nv_bfloat16* __restrict__ out, float* __restrict__ dw_out) {
   __shared__ long long s_peers[kEpMaxPeers];
+  __shared__ int s_list[kEpWarps][kEpMaxK];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, blk = blockIdx.x;
   const int K = g.K, W = g.W, n16 = g.H / 8;
@@ -399,15 +400,17 @@ __global__ void __launch_bounds__(kEpThreads, 2)
       reinterpret_cast<float*>(s_peers[m.z] + g.off_dw)[m.w] = dscale[q];
     if (m.x != q) continue;
     const int* tab = reinterpret_cast<const int*>(me + g.off_tab) + (size_t)q * g.kpad;
-    int list[kEpMaxK];
+    int* list = s_list[warp];  // this primary's rows (shared memory keeps them out of registers)
     int cnt = 0;
+    __syncwarp();  // every lane is done with the previous primary's list
 #pragma unroll
     for (int i = 0; i < kEpMaxK; ++i) {
       int v = i < g.kpad ? __ldcg(tab + i) : -1;
       if (v >= 0 && !PM_PEER_INDEX_OK(g.st, v < n)) v = -1;
       cnt += (v >= 0 && cnt == i) ? 1 : 0;
-      list[i] = v >= 0 ? v : 0;
+      if (lane == 0) list[i] = v >= 0 ? v : 0;
     }
+    __syncwarp();
     const int t = m.w / K;
     uint4* dstrow = reinterpret_cast<uint4*>(reinterpret_cast<char*>(s_peers[m.z]) + g.off_back +
                                              ((size_t)t * W + g.rank) * g.H * 2);
@@ -431,14 +434,16 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     if (dw_out != nullptr && lane < K)
       dw_out[t * K + lane] = p >= 0 ? __ldcg(reinterpret_cast<const float*>(me + g.off_dw) + t * K + lane) : 0.f;
     const uint4* back = reinterpret_cast<const uint4*>(me + g.off_back + (size_t)t * W * g.H * 2);
-    int dl[kEpMaxK];  // destination GPUs of this token (at most K), lowest first
+    int* dl = s_list[warp];  // destination GPUs of this token (at most K), lowest first
     unsigned mm = dmask;
     const int nd = min(__popc(dmask), kEpMaxK);
+    __syncwarp();
 #pragma unroll
     for (int i = 0; i < kEpMaxK; ++i) {
-      dl[i] = mm ? __ffs(mm) - 1 : 0;
+      if (lane == 0) dl[i] = mm ? __ffs(mm) - 1 : 0;
       mm &= mm - 1;
     }
+    __syncwarp();
     uint4* orow = reinterpret_cast<uint4*>(out + (size_t)t * g.H);
     if (nd == 1)  // one destination GPU: the token's output is its partial
       warp_copy_row(orow, back + (size_t)dl[0] * n16, n16, lane);
