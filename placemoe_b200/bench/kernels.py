@@ -245,6 +245,28 @@ def bench_ep_local(tokens, iters):
         if k in acc:
             report(f"ep_{k}[one rank, T{tokens} k{cfg.num_experts_per_tok} H{cfg.hidden_size}]", acc[k],
                    nbytes=need[k])
+    # one more pass with CTA 0's phase timestamps (%globaltimer) to split each kernel's time
+    from placemoe_b200.ops import kernels
+
+    marks = torch.zeros(24, dtype=torch.int64, device="cuda")
+    kernels().ep_phase_marks(marks)
+    y = blk(x)
+    torch.cuda.synchronize()
+    fwd = marks.tolist()  # dispatch 0-7, combine (forward) 8-11
+    y.backward(dy)
+    torch.cuda.synchronize()
+    bwd = marks.tolist()  # scatter 16-19, combine_bwd 8-11
+    kernels().ep_phase_marks(None)
+
+    def split(m, base, names):
+        return {n: round((m[base + i + 1] - m[base + i]) / 1e3, 1) for i, n in enumerate(names)}
+
+    print(json.dumps({"ep_phases_us": {
+        "dispatch": split(fwd, 0, ["histogram", "count_exchange", "segments", "positions", "row_stores",
+                                   "rows_barrier", "local_copies"]),
+        "combine": split(fwd, 8, ["pre_reduce", "barrier", "token_sums"]),
+        "scatter": split(bwd, 16, ["row_stores", "barrier", "local_copies"]),
+        "combine_bwd": split(bwd, 8, ["pre_reduce", "barrier", "token_sums"])}}), flush=True)
 
 
 def bench_memory(tokens, hidden, iters):

@@ -45,6 +45,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_pull", &pm::p2p_pull);
   // fused expert-parallel dispatch / combine (one cooperative kernel per phase)
   m.def("ep_scratch_ints", &pm::ep_scratch_ints);
+  m.def("ep_phase_marks", &pm::ep_phase_marks, "int64[24] buffer for per-phase timestamps of the EP kernels");
   m.def("ep_dispatch", &pm::ep_dispatch);
   m.def("ep_combine", &pm::ep_combine);
   m.def("ep_scatter", &pm::ep_scatter);

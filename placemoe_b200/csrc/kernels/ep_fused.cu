@@ -72,7 +72,14 @@ struct EpGeo {
   int* st;            // sticky status block
   unsigned* gbar;     // grid barrier words [2]
   int* blk;           // [gridDim.x][B] per-CTA bucket counts (dispatch)
+  unsigned long long* marks;  // optional phase timestamps (CTA 0, %globaltimer ns), nullptr = off
 };
+
+// Phase timestamp of CTA 0 (diagnostics: the kernel bench reads them to split a kernel's time).
+// Slots: dispatch 0-7, combine 8-11, scatter 16-19.
+PM_DEVICE void mark_phase(const EpGeo& g, int i) {
+  if (g.marks != nullptr && blockIdx.x == 0 && threadIdx.x == 0) g.marks[i] = now_ns();
+}
 
 PM_DEVICE int lanemask_lt() {
   unsigned m;
@@ -203,6 +210,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   for (int i = tid; i < kEpWarps * B; i += kEpThreads) wrun[i] = 0;
   __syncthreads();
 
+  mark_phase(g, 0);
   const int chunk = (g.T + G - 1) / G;
   const int t_beg = min(g.T, blk * chunk), t_end = min(g.T, t_beg + chunk);
   const int sub = (chunk + kEpWarps - 1) / kEpWarps;
@@ -225,6 +233,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     g.blk[(size_t)blk * B + b] = run;
   }
   grid_barrier(g.gbar, 2 * g.budget_ns, g.st);
+  mark_phase(g, 1);
 
   // ---- B: count row to every peer (CTA 0); every CTA: its base within each bucket
   int* counts_local = reinterpret_cast<int*>(s_peers[g.rank] + g.off_counts) + (size_t)g.parity * W * B;
@@ -242,6 +251,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     base[b] = t;
   }
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpCounts);
+  mark_phase(g, 2);
 
   // ---- C: segment layout of every destination, positions, stores
   for (int b = tid; b < B; b += kEpThreads) {
@@ -277,6 +287,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   }
   __syncthreads();
 
+  mark_phase(g, 3);
   // positions: stable (token, k) order within every bucket
   for (int a0 = wt0 * K; a0 < wt1 * K; a0 += 32) {
     const int a = a0 + lane;
@@ -296,6 +307,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   }
   __syncthreads();
 
+  mark_phase(g, 4);
   const int n16 = g.H / 8;
   for (int t = t_beg + warp; t < t_end; t += kEpWarps) {
     const int a = t * K + lane;
@@ -359,7 +371,9 @@ __global__ void __launch_bounds__(kEpThreads, 2)
       }
     }
   }
+  mark_phase(g, 5);
   grid_peer_barrier(g, s_peers, g.epoch + 1, kWaitEpRows);
+  mark_phase(g, 6);
 
   // ---- D: local copies for the other assignments of a token on this GPU; routing weights
   {
@@ -374,6 +388,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
                       reinterpret_cast<const uint4*>(me + g.off_x + (size_t)m.x * g.H * 2), n16, lane);
     }
   }
+  mark_phase(g, 7);
 }
 
 // ------------------------------------------------------------------------------------ combine
@@ -390,6 +405,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   __syncthreads();
   char* me = reinterpret_cast<char*>(s_peers[g.rank]);
   const int n = min(offsets[g.S], g.cap);
+  mark_phase(g, 8);
 
   // ---- A: pre-reduce every primary's rows, partial sum back to the source
   for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
@@ -420,7 +436,9 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     else
       for (int v = lane; v < n16; v += 32) dstrow[v] = sum_rows_chunk<false>(src, list, cnt, n16, v);
   }
+  mark_phase(g, 9);
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpCombine);
+  mark_phase(g, 10);
 
   // ---- B: per token, the sum of its partials (one per destination GPU)
   for (int t = blk * kEpWarps + warp; t < g.T; t += G * kEpWarps) {
@@ -450,6 +468,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     else
       for (int v = lane; v < n16; v += 32) orow[v] = sum_rows_chunk<true>(back, dl, nd, n16, v);
   }
+  mark_phase(g, 11);
 }
 
 // ------------------------------------------------------------------------------------ scatter
@@ -464,6 +483,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   __syncthreads();
   char* me = reinterpret_cast<char*>(s_peers[g.rank]);
   const int n = min(offsets[g.S], g.cap);
+  mark_phase(g, 16);
 
   // ---- A: dy once per (token, destination GPU); padding rows of this rank zeroed
   for (int t = blk * kEpWarps + warp; t < g.T; t += G * kEpWarps) {
@@ -489,7 +509,9 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
     if (m.x < 0) warp_zero_row(reinterpret_cast<uint4*>(me + g.off_dy + (size_t)q * g.H * 2), n16, lane);
   }
+  mark_phase(g, 17);
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpScatter);
+  mark_phase(g, 18);
 
   // ---- B: local copies for the token's other assignments on this GPU
   for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
@@ -498,11 +520,25 @@ __global__ void __launch_bounds__(kEpThreads, 2)
       warp_copy_row(reinterpret_cast<uint4*>(me + g.off_dy + (size_t)q * g.H * 2),
                     reinterpret_cast<const uint4*>(me + g.off_dy + (size_t)m.x * g.H * 2), n16, lane);
   }
+  mark_phase(g, 19);
 }
 
 // ------------------------------------------------------------------------------------ host side
 // geo (int64): W, rank, S, K, H, T_cap, cap, align, kpad, parity,
 //              off_flags, off_counts, off_x, off_meta, off_tab, off_back, off_dw, off_dy
+// Phase-timestamp buffer for diagnostics (set by ep_phase_marks; nullptr = no timestamps).
+static unsigned long long* g_ep_marks = nullptr;
+
+void ep_phase_marks(c10::optional<torch::Tensor> buf) {
+  if (!buf.has_value()) {
+    g_ep_marks = nullptr;
+    return;
+  }
+  PM_CHECK_CUDA(*buf);
+  TORCH_CHECK(buf->scalar_type() == torch::kInt64 && buf->numel() >= 24, "marks: int64[24]");
+  g_ep_marks = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+}
+
 static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers, const torch::Tensor& scratch,
                       const torch::Tensor& status, int64_t epoch, double timeout_s, int T) {
   TORCH_CHECK(v.size() == 18, "ep geometry: 18 values");
@@ -527,6 +563,7 @@ static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers,
   g.st = status.data_ptr<int>();
   g.gbar = reinterpret_cast<unsigned*>(scratch.data_ptr<int>());
   g.blk = scratch.data_ptr<int>() + 2;
+  g.marks = g_ep_marks;
   return g;
 }
 

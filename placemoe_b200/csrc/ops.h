@@ -74,6 +74,7 @@ void p2p_pull(torch::Tensor dst, torch::Tensor peers, int64_t src_rank, int64_t 
 
 // fused expert-parallel dispatch / combine over peer memory (ep_fused.cu)
 int64_t ep_scratch_ints(int64_t world, int64_t slots);
+void ep_phase_marks(c10::optional<torch::Tensor> buf);
 void ep_dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w, torch::Tensor dest_tab, torch::Tensor slot_tab,
                  torch::Tensor peers, std::vector<int64_t> geo, torch::Tensor scratch, torch::Tensor status,
                  int64_t epoch, double timeout_s, torch::Tensor pos, torch::Tensor dst, torch::Tensor offsets,
