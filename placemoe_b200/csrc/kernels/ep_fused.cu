@@ -201,7 +201,8 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   int* wrun = sm;                       // [kEpWarps][B]
   int* base = wrun + kEpWarps * B;      // [B]: block base, then full per-bucket base
   int* tot = base + B;                  // [B]: assignments per bucket over all sources
-  int* start = tot + B;                 // [B]: segment start of bucket (d, s) at d
+  int* start = tot + B;                 // [B]: segment start of bucket (d, s) at d; in phase B the
+                                        // [2][J][B] stripe sums (ep_dispatch_smem sizes it)
   __shared__ long long s_peers[kEpMaxPeers];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = gridDim.x, blk = blockIdx.x;
@@ -237,18 +238,43 @@ __global__ void __launch_bounds__(kEpThreads, 2)
 
   // ---- B: count row to every peer (CTA 0); every CTA: its base within each bucket
   int* counts_local = reinterpret_cast<int*>(s_peers[g.rank] + g.off_counts) + (size_t)g.parity * W * B;
-  if (blk == 0) {
-    for (int b = tid; b < B; b += kEpThreads) {
-      int t = 0;
-      for (int k = 0; k < G; ++k) t += __ldcg(&g.blk[(size_t)k * B + b]);
-      for (int r = 0; r < W; ++r)
-        reinterpret_cast<int*>(s_peers[r] + g.off_counts)[(size_t)g.parity * W * B + (size_t)g.rank * B + b] = t;
+  {
+    // Every CTA sums the block counts of each bucket over the CTAs before it (its base) and over all CTAs
+    // (the totals, sent by CTA 0).  Threads split the blocks into J stripes per bucket, four independent
+    // loads in flight each, then one thread per bucket adds the stripes: a serial walk over ~150 L2
+    // reads per thread would cost ~100 us of latency.
+    const int J = B >= kEpThreads ? 1 : kEpThreads / B;
+    int* part_below = start;  // [J][B] (start / tot are not used before phase C) -- see the smem plan
+    int* part_all = start + J * B;
+    for (int i = tid; i < B * J; i += kEpThreads) {
+      const int b = i % B, j = i / B;
+      int below = 0, all = 0, k = j;
+      for (; k + 3 * J < G; k += 4 * J) {
+        const int c0 = __ldcg(&g.blk[(size_t)k * B + b]), c1 = __ldcg(&g.blk[(size_t)(k + J) * B + b]);
+        const int c2 = __ldcg(&g.blk[(size_t)(k + 2 * J) * B + b]), c3 = __ldcg(&g.blk[(size_t)(k + 3 * J) * B + b]);
+        all += c0 + c1 + c2 + c3;
+        below += (k < blk ? c0 : 0) + (k + J < blk ? c1 : 0) + (k + 2 * J < blk ? c2 : 0) + (k + 3 * J < blk ? c3 : 0);
+      }
+      for (; k < G; k += J) {
+        const int c = __ldcg(&g.blk[(size_t)k * B + b]);
+        all += c;
+        below += k < blk ? c : 0;
+      }
+      part_below[j * B + b] = below;
+      part_all[j * B + b] = all;
     }
-  }
-  for (int b = tid; b < B; b += kEpThreads) {
-    int t = 0;
-    for (int k = 0; k < blk; ++k) t += __ldcg(&g.blk[(size_t)k * B + b]);
-    base[b] = t;
+    __syncthreads();
+    for (int b = tid; b < B; b += kEpThreads) {
+      int below = 0, all = 0;
+      for (int j = 0; j < J; ++j) {
+        below += part_below[j * B + b];
+        all += part_all[j * B + b];
+      }
+      base[b] = below;
+      if (blk == 0)
+        for (int r = 0; r < W; ++r)
+          reinterpret_cast<int*>(s_peers[r] + g.off_counts)[(size_t)g.parity * W * B + (size_t)g.rank * B + b] = all;
+    }
   }
   grid_peer_barrier(g, s_peers, g.epoch, kWaitEpCounts);
   mark_phase(g, 2);
@@ -567,6 +593,13 @@ static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers,
   return g;
 }
 
+// Dynamic shared memory of the dispatch kernel: warp counters, base and totals, then the area that
+// holds the segment starts in phase C and the [2][J][B] stripe sums of phase B.
+static size_t ep_dispatch_smem(int B) {
+  const int J = B >= kEpThreads ? 1 : kEpThreads / B;
+  return (size_t)(kEpWarps + 2) * B * sizeof(int) + (size_t)std::max(B, 2 * J * B) * sizeof(int);
+}
+
 static int ep_grid(const void* fn, size_t smem) {
   int dev, sms, per = 0;
   C10_CUDA_CHECK(cudaGetDevice(&dev));
@@ -608,7 +641,7 @@ void ep_dispatch(torch::Tensor x, torch::Tensor idx, torch::Tensor w, torch::Ten
   TORCH_CHECK(row_scale.numel() >= g.cap && row_scale.scalar_type() == torch::kFloat32, "row_scale: fp32 [cap]");
   g.E = (int)dest_tab.numel();
   const int B = g.W * g.S;
-  const size_t smem = (size_t)(kEpWarps + 3) * B * sizeof(int);
+  const size_t smem = ep_dispatch_smem(B);
   const void* fn = reinterpret_cast<const void*>(&ep_dispatch_kernel);
   C10_CUDA_CHECK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = ep_grid(fn, smem);

@@ -294,6 +294,8 @@ class P2PExpertParallel:
             tokens = max(t, self.arena.tokens if self.arena is not None else 0)
             self.arena = None
             torch.cuda.current_stream(device).synchronize()
+            # the symmetric arena comes from the driver, not from torch's cache: return cached blocks first
+            torch.cuda.empty_cache()
             self.arena = EpArena(self.group, self.world, self.rank, tokens, k, h, slots, layers,
                                  self.capacity_factor, device)
         return self.arena
@@ -303,7 +305,10 @@ class P2PExpertParallel:
         return None if self.arena is None else self.arena.status[2:3]
 
     def check_capacity(self) -> None:
-        """Raise :class:`EPCapacityExceeded` if any rank overflowed since the last check (one host read)."""
+        """Raise :class:`EPCapacityExceeded` if any rank overflowed since the last check (one host read).
+
+        ``last_overflow_rows`` keeps the largest row count seen, so the caller can size the next
+        arena for what the step needed (:meth:`grow_capacity`) instead of blindly doubling it."""
         if self.arena is None:
             return
         worst = self.arena.status[2:3].clone()
@@ -312,8 +317,18 @@ class P2PExpertParallel:
         self.arena.status[2].zero_()
         rows = int(worst.item())
         if rows > self.arena.cap:
+            self.last_overflow_rows = rows
             raise EPCapacityExceeded(f"received {rows} expert rows, slab holds {self.arena.cap} "
                                      f"(capacity_factor {self.capacity_factor})")
+
+    def grow_capacity(self, margin: float = 1.15) -> float:
+        """New capacity factor after an overflow: the rows the step needed plus ``margin``, at least a quarter
+        more than before, at most the world size (every assignment of every source)."""
+        a = self.arena
+        rows = getattr(self, "last_overflow_rows", 0)
+        need = (rows - a.slots * (a.align - 1)) / float(a.tokens * a.k) if a is not None and rows else 0.0
+        self.capacity_factor = min(float(self.world), max(self.capacity_factor * 1.25, need * margin))
+        return self.capacity_factor
 
     def moe_forward(self, blk, x, bias, aux_coef):
         t, h = x.shape

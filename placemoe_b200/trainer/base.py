@@ -299,7 +299,10 @@ class Trainer:
                 if rsync is not None:
                     rsync.wait()
                 self._zero_all_grads()
-                ep.capacity_factor = min(float(self.world), ep.capacity_factor * 2)
+                if hasattr(ep, "grow_capacity"):  # size for the rows the step needed (plus a margin)
+                    ep.grow_capacity()
+                else:
+                    ep.capacity_factor = min(float(self.world), ep.capacity_factor * 2)
                 self.metrics["ep_capacity_factor"] = ep.capacity_factor
         loss = torch.stack(losses).mean()
         self.optimizer_step()
