@@ -67,6 +67,7 @@ struct EpGeo {
   int W, rank, S, K, H, T, cap, align, kpad, parity;
   int E, t_cap;       // logical experts (dispatch tables), tokens the return buffers hold
   long long off_flags, off_counts, off_x, off_meta, off_tab, off_back, off_dw, off_dy;
+  long long off_prim;  // layer slab: [0] count, [1..] positions of this GPU's primary rows
   unsigned epoch;     // first barrier epoch used by this launch
   long long budget_ns;
   int* st;            // sticky status block
@@ -212,6 +213,8 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   __syncthreads();
 
   mark_phase(g, 0);
+  if (blk == 0 && tid == 0)  // this layer's list of primary rows is rebuilt in phase D
+    *reinterpret_cast<int*>(reinterpret_cast<char*>(s_peers[g.rank]) + g.off_prim) = 0;
   const int chunk = (g.T + G - 1) / G;
   const int t_beg = min(g.T, blk * chunk), t_end = min(g.T, t_beg + chunk);
   const int sub = (chunk + kEpWarps - 1) / kEpWarps;
@@ -408,7 +411,13 @@ __global__ void __launch_bounds__(kEpThreads, 2)
     for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
       const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
       const bool ok = m.x < 0 || PM_PEER_INDEX_OK(g.st, m.x < n);
-      if (lane == 0) row_scale[q] = (m.x >= 0 && ok) ? __int_as_float(m.y) : 0.f;
+      if (lane == 0) {
+        row_scale[q] = (m.x >= 0 && ok) ? __int_as_float(m.y) : 0.f;
+        if (m.x == q) {  // a primary: the combine pre-reduces from it (list order is irrelevant to results)
+          int* prim = reinterpret_cast<int*>(me + g.off_prim);
+          prim[1 + atomicAdd(prim, 1)] = q;
+        }
+      }
       if (m.x >= 0 && m.x != q && ok)
         warp_copy_row(reinterpret_cast<uint4*>(me + g.off_x + (size_t)q * g.H * 2),
                       reinterpret_cast<const uint4*>(me + g.off_x + (size_t)m.x * g.H * 2), n16, lane);
@@ -433,26 +442,35 @@ __global__ void __launch_bounds__(kEpThreads, 2)
   const int n = min(offsets[g.S], g.cap);
   mark_phase(g, 8);
 
-  // ---- A: pre-reduce every primary's rows, partial sum back to the source
-  for (int q = blk * kEpWarps + warp; q < n; q += G * kEpWarps) {
+  // ---- A: pre-reduce every primary's rows, partial sum back to the source.  Warps walk the list of
+  // primaries the dispatch built (even work per warp: a primary's rows sit in different expert segments,
+  // so walking positions would give some warps many primaries and others none).
+  const int* prim = reinterpret_cast<const int*>(me + g.off_prim);
+  const int nprim = min(__ldcg(prim), n);
+  for (int i = blk * kEpWarps + warp; i < nprim; i += G * kEpWarps) {
+    const int q = __ldcg(prim + 1 + i);
+    if (!PM_PEER_INDEX_OK(g.st, q >= 0 && q < n)) continue;
     const int4 m = ldcg_i4(me + g.off_meta + (size_t)q * 16);
-    if (m.x < 0) continue;
-    if (!PM_PEER_INDEX_OK(g.st, m.z >= 0 && m.z < W && m.w >= 0 && m.w < g.t_cap * K)) continue;
-    if (dscale != nullptr && lane == 0)
-      reinterpret_cast<float*>(s_peers[m.z] + g.off_dw)[m.w] = dscale[q];
     if (m.x != q) continue;
+    if (!PM_PEER_INDEX_OK(g.st, m.z >= 0 && m.z < W && m.w >= 0 && m.w < g.t_cap * K)) continue;
     const int* tab = reinterpret_cast<const int*>(me + g.off_tab) + (size_t)q * g.kpad;
     int* list = s_list[warp];  // this primary's rows (shared memory keeps them out of registers)
     int cnt = 0;
     __syncwarp();  // every lane is done with the previous primary's list
 #pragma unroll
-    for (int i = 0; i < kEpMaxK; ++i) {
-      int v = i < g.kpad ? __ldcg(tab + i) : -1;
+    for (int j = 0; j < kEpMaxK; ++j) {
+      int v = j < g.kpad ? __ldcg(tab + j) : -1;
       if (v >= 0 && !PM_PEER_INDEX_OK(g.st, v < n)) v = -1;
-      cnt += (v >= 0 && cnt == i) ? 1 : 0;
-      if (lane == 0) list[i] = v >= 0 ? v : 0;
+      cnt += (v >= 0 && cnt == j) ? 1 : 0;
+      if (lane == 0) list[j] = v >= 0 ? v : 0;
     }
     __syncwarp();
+    if (dscale != nullptr && lane < cnt) {  // routing-weight gradient of every assignment of the token here
+      const int qi = list[lane];
+      const int4 mi = ldcg_i4(me + g.off_meta + (size_t)qi * 16);
+      if (PM_PEER_INDEX_OK(g.st, mi.w >= 0 && mi.w < g.t_cap * K))
+        reinterpret_cast<float*>(s_peers[m.z] + g.off_dw)[mi.w] = dscale[qi];
+    }
     const int t = m.w / K;
     uint4* dstrow = reinterpret_cast<uint4*>(reinterpret_cast<char*>(s_peers[m.z]) + g.off_back +
                                              ((size_t)t * W + g.rank) * g.H * 2);
@@ -551,7 +569,7 @@ __global__ void __launch_bounds__(kEpThreads, 2)
 
 // ------------------------------------------------------------------------------------ host side
 // geo (int64): W, rank, S, K, H, T_cap, cap, align, kpad, parity,
-//              off_flags, off_counts, off_x, off_meta, off_tab, off_back, off_dw, off_dy
+//              off_flags, off_counts, off_x, off_meta, off_tab, off_back, off_dw, off_dy, off_prim
 // Phase-timestamp buffer for diagnostics (set by ep_phase_marks; nullptr = no timestamps).
 static unsigned long long* g_ep_marks = nullptr;
 
@@ -567,7 +585,7 @@ void ep_phase_marks(c10::optional<torch::Tensor> buf) {
 
 static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers, const torch::Tensor& scratch,
                       const torch::Tensor& status, int64_t epoch, double timeout_s, int T) {
-  TORCH_CHECK(v.size() == 18, "ep geometry: 18 values");
+  TORCH_CHECK(v.size() == 19, "ep geometry: 19 values");
   PM_CHECK_CUDA(peers); PM_CHECK_CUDA(scratch); PM_CHECK_CUDA(status);
   TORCH_CHECK(peers.scalar_type() == torch::kInt64 && peers.numel() == v[0] && v[0] <= kEpMaxPeers, "peer table");
   TORCH_CHECK(status.scalar_type() == torch::kInt32 && status.numel() >= 4, "status: int32[4]");
@@ -578,12 +596,12 @@ static EpGeo make_geo(const std::vector<int64_t>& v, const torch::Tensor& peers,
   g.T = T; g.cap = (int)v[6]; g.align = (int)v[7]; g.kpad = (int)v[8]; g.parity = (int)v[9];
   g.E = 0; g.t_cap = (int)v[5];
   g.off_flags = v[10]; g.off_counts = v[11]; g.off_x = v[12]; g.off_meta = v[13]; g.off_tab = v[14];
-  g.off_back = v[15]; g.off_dw = v[16]; g.off_dy = v[17];
+  g.off_back = v[15]; g.off_dw = v[16]; g.off_dy = v[17]; g.off_prim = v[18];
   TORCH_CHECK(T <= v[5], "more tokens than the arena holds");
   TORCH_CHECK(g.K >= 1 && g.K <= kEpMaxK && g.kpad % 4 == 0 && g.kpad >= g.K && g.kpad <= kEpMaxK, "top-k");
   TORCH_CHECK(g.W * g.S <= kEpMaxBuckets && g.W <= 32, "W * S <= 1024 buckets, W <= 32");
   TORCH_CHECK(g.H % 8 == 0 && g.align > 0 && g.cap % g.align == 0, "geometry");
-  for (int i = 10; i < 18; ++i) TORCH_CHECK(v[i] % 16 == 0, "16-byte aligned arena regions");
+  for (int i = 10; i < 19; ++i) TORCH_CHECK(v[i] % 16 == 0, "16-byte aligned arena regions");
   g.epoch = (unsigned)epoch;
   g.budget_ns = (long long)(timeout_s * 1e9);
   g.st = status.data_ptr<int>();

@@ -146,8 +146,10 @@ class EpArena:
             region("meta", self.cap * 16)
             t0 = off
             region("tab", self.cap * self.kpad * 4)
-            self.slab_off.append((x0, m0, t0))
-        del lay["x"], lay["meta"], lay["tab"]
+            p0 = off
+            region("prim", (self.cap + 1) * 4)  # primary rows of this GPU (count, then positions)
+            self.slab_off.append((x0, m0, t0, p0))
+        del lay["x"], lay["meta"], lay["tab"], lay["prim"]
         self.layout = lay
         self.nbytes = off
         if world > 1:
@@ -176,10 +178,10 @@ class EpArena:
     def geo(self, slab: int, toggle: bool = False) -> list[int]:
         if toggle:
             self.parity ^= 1
-        x0, m0, t0 = self.slab_off[slab]
+        x0, m0, t0, p0 = self.slab_off[slab]
         L = self.layout
         return [self.world, self.rank, self.slots, self.k, self.hidden, self.tokens, self.cap, self.align, self.kpad,
-                self.parity, L["flags"], L["counts"], x0, m0, t0, L["back"], L["dw"], L["dy"]]
+                self.parity, L["flags"], L["counts"], x0, m0, t0, L["back"], L["dw"], L["dy"], p0]
 
     def epochs(self, n: int) -> int:
         """First epoch of a launch that runs ``n`` peer barriers."""

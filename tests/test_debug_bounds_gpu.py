@@ -69,10 +69,12 @@ def test_fused_dispatch_rejects_bad_expert_id():
     off_back = off_tab + cap * kpad * 4
     off_dw = off_back + t * h * 2
     off_dy = off_dw + t * k * 4 + 256
-    total = off_dy + cap * h * 2
+    off_prim = off_dy + cap * h * 2
+    total = off_prim + (cap + 1) * 4 + 16
     arena = torch.zeros(total, dtype=torch.uint8, device=dev)
     peers = torch.tensor([arena.data_ptr()], dtype=torch.int64, device=dev)
-    geo = [1, 0, slots, k, h, t, cap, align, kpad, 0, 0, 256, off_x, off_meta, off_tab, off_back, off_dw, off_dy]
+    geo = [1, 0, slots, k, h, t, cap, align, kpad, 0, 0, 256, off_x, off_meta, off_tab, off_back, off_dw, off_dy,
+           off_prim]
     scratch = torch.zeros(int(dbg.ep_scratch_ints(1, slots)), dtype=torch.int32, device=dev)
     pos = torch.empty(t, k, dtype=torch.int32, device=dev)
     dst = torch.empty(t, k, dtype=torch.int32, device=dev)
