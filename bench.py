@@ -53,6 +53,10 @@ def parse():
                         "from the captured demand")
     p.add_argument("--plan-steps", type=int, default=-1,
                    help="steps of captured routes the PlaceMoE planner uses before timing (default: 20 when N > 1)")
+    p.add_argument("--capture-seq", type=int, default=-1,
+                   help="sequence length of the route-capture steps before planning (default: the full --seq; "
+                        "1024 for qwen3_30b_a3b, whose unplanned skewed layout would otherwise size the receive "
+                        "slabs for ~4x the balanced load)")
     p.add_argument("--artifact", default="")
     p.add_argument("--layers", type=int, default=0, help="override layer count (diagnostics only)")
     p.add_argument("--ep-transport", default="auto", choices=("auto", "p2p", "nccl"))
@@ -148,8 +152,9 @@ def plan_placement(trainer, pool, args, rank, world):
     root = holder[0]
     rec = RouteRecorder(trainer.model, root)
     rec.enabled = True
+    cap_seq = args.capture_seq if args.capture_seq > 0 else args.seq
     for s in range(args.plan_steps):
-        trainer.train_step(next(pool))
+        trainer.train_step(next(pool)[:, :cap_seq])
         rec.record_step(s)
     rec.enabled = False
     for blk in trainer.model.moe_blocks():
@@ -181,6 +186,14 @@ def plan_placement(trainer, pool, args, rank, world):
         moved += migrate_layer(trainer, blk, plans[blk.layer_key])
     trainer._norm_table = None
     trainer.optimizer.reset_tables()
+    # the capture steps ran on the unplanned layout; the planned one is balanced, so the receive slabs go
+    # back to the default capacity (a new arena is allocated at the next step, collectively)
+    ep = trainer.pstate.ep
+    if hasattr(ep, "arena"):
+        ep.arena = None
+        ep.capacity_factor = 2.0
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
     dist.barrier()
     agg = report[0] or {}
     return {"plan_steps": args.plan_steps, "planner_ms": round(planner_ms, 1),
@@ -291,6 +304,8 @@ def main():
         args.redundant_slots = 0
     if args.redundant_slots < 0:
         args.redundant_slots = (4 if big else 1) if world > 1 else 0
+    if args.capture_seq < 0:
+        args.capture_seq = 1024 if big else 0
     if args.plan_steps < 0:
         args.plan_steps = 20 if world > 1 and not args.artifact and args.placement != "fixed_ep" else 0
     local = int(os.environ.get("LOCAL_RANK", "0"))

@@ -19,8 +19,13 @@ forward
      and stored into the source's return rows -> barrier -> token sums.
 backward
   ``ep_scatter`` (dy once per (token, GPU), local copies), fc2 dgrad +
-  dSwiGLU, fc1 dgrad, two grouped weight-gradient GEMMs, ``ep_combine`` of
-  the data gradients (with the routing-weight gradients riding along).
+  dSwiGLU, fc1 dgrad, then ``ep_combine`` of the data gradients (with the
+  routing-weight gradients riding along) while the two grouped weight-gradient
+  GEMMs run on a side stream: they do not feed dx, so their tensor-core work
+  overlaps the combine's NVLink traffic.  The output-gradient buffer is double
+  buffered by layer parity, and a layer's combine waits for the previous
+  layer's weight gradients, which keeps a peer's scatter from refilling a
+  buffer that a weight gradient still reads.
 
 The receive slab of every layer lives until the layer's backward (the fc1
 weight gradient reads it), so the arena holds one slab per MoE layer: the
@@ -137,7 +142,9 @@ class EpArena:
         region("counts", 2 * world * world * slots * 4)
         region("back", tokens * world * hidden * 2)
         region("dw", tokens * k * 4)
-        region("dy", self.cap * hidden * 2)
+        region("dy", self.cap * hidden * 2)  # output gradients of even layers
+        region("dy1", self.cap * hidden * 2)  # odd layers: a layer's weight gradient may still read its
+        # dy rows while the next layer's scatter fills the other buffer
         self.slab_off = []
         for _ in range(layers):
             x0 = off
@@ -180,8 +187,9 @@ class EpArena:
             self.parity ^= 1
         x0, m0, t0, p0 = self.slab_off[slab]
         L = self.layout
+        dy = L["dy1"] if slab % 2 else L["dy"]
         return [self.world, self.rank, self.slots, self.k, self.hidden, self.tokens, self.cap, self.align, self.kpad,
-                self.parity, L["flags"], L["counts"], x0, m0, t0, L["back"], L["dw"], L["dy"], p0]
+                self.parity, L["flags"], L["counts"], x0, m0, t0, L["back"], L["dw"], dy, p0]
 
     def epochs(self, n: int) -> int:
         """First epoch of a launch that runs ``n`` peer barriers."""
@@ -193,8 +201,8 @@ class EpArena:
         x0 = self.slab_off[slab][0]
         return self.buf[x0: x0 + self.cap * self.hidden * 2].view(torch.bfloat16).view(self.cap, self.hidden)
 
-    def dy_view(self) -> torch.Tensor:
-        o = self.layout["dy"]
+    def dy_view(self, slab: int = 0) -> torch.Tensor:
+        o = self.layout["dy1"] if slab % 2 else self.layout["dy"]
         return self.buf[o: o + self.cap * self.hidden * 2].view(torch.bfloat16).view(self.cap, self.hidden)
 
 
@@ -244,25 +252,29 @@ class _FusedEPMoE(torch.autograd.Function):
         with _span("scatter"):
             kn.ep_scatter(dy, pos, dst, offsets, arena.peers, arena.geo(slab), arena.scratch, arena.status,
                           arena.epochs(1), BARRIER_TIMEOUT_S)
-        dyd = arena.dy_view()
+        dyd = arena.dy_view(slab)
         xd = arena.x_view(slab)
         dgu = torch.empty_like(gu)
         dscale = torch.zeros(cap, device=dev, dtype=torch.float32)
         kn.moe_fc2_dgrad_dswiglu(dyd, w2, offsets, gu, row_scale, dgu, dscale, arena.align)
         dxd = torch.empty(cap, arena.hidden, device=dev, dtype=torch.bfloat16)
         kn.moe_grouped_gemm(dgu, w1, offsets, dxd, True, arena.align)
-        if blk.down_proj.requires_grad:
-            kn.moe_wgrad(dyd, hbuf, offsets, *moe_ops.wgrad_target(blk.down_proj), None)
-        if blk.gate_up_proj.requires_grad:
-            kn.moe_wgrad(dgu, xd, offsets, *moe_ops.wgrad_target(blk.gate_up_proj), None)
+        ep = blk.ep
+        # The weight gradients do not feed dx: they run on the weight-gradient stream while the combine
+        # moves the data gradients over NVLink (the two kernels fit on an SM together).  Before this
+        # layer's combine, the stream also waits for the previous MoE layer's weight gradients: a peer
+        # can only start refilling that layer's dy buffer (two layers on) after passing this barrier.
+        done = ep.wgrad_async(blk, dyd, hbuf, dgu, xd, offsets)
+        ep.wait_previous_wgrad()
         dx = torch.empty(t, arena.hidden, device=dev, dtype=torch.bfloat16)
         dw = torch.empty(t, k, device=dev, dtype=torch.float32)
         with _span("combine_bwd"):
             kn.ep_combine(dxd, dscale, pos, dst, offsets, arena.peers, arena.geo(slab), arena.scratch, arena.status,
                           arena.epochs(1), BARRIER_TIMEOUT_S, dx, dw)
-        rs = getattr(blk.ep, "replica_sync", None)
-        if rs is not None:  # this layer's expert gradients are final: reduce replicas on the side stream
-            rs.layer_ready(blk)
+        ep.previous_wgrad = done
+        rs = getattr(ep, "replica_sync", None)
+        if rs is not None:  # this layer's expert gradients are final once `done` fires: reduce replicas
+            rs.layer_ready(blk, after=done)
         return dx, dw, None, None, None, None
 
 
@@ -286,9 +298,47 @@ class P2PExpertParallel:
         self.num_layers = 1
         self.arena: EpArena | None = None
         self.replica_sync = None  # p2p_sync.ReplicaGradSync, set by the trainer
+        self.wgrad_stream: torch.cuda.Stream | None = None
+        self.pending_wgrad: list = []
+        self.previous_wgrad = None
         from .ep import ExpertParallel
 
         self._router = ExpertParallel._route.__get__(self)
+
+    # ------------------------------------------------------------ weight gradients on a side stream
+    def wgrad_async(self, blk, dyd, hbuf, dgu, xd, offsets) -> torch.cuda.Event:
+        """Launch the layer's two expert weight-gradient GEMMs on the weight-gradient stream, ordered after
+        the work issued so far on the current stream; returns the event that marks their end."""
+        cur = torch.cuda.current_stream(dyd.device)
+        if self.wgrad_stream is None or self.wgrad_stream.device != dyd.device:
+            self.wgrad_stream = torch.cuda.Stream(device=dyd.device)
+        ready = torch.cuda.Event()
+        ready.record(cur)
+        kn = moe_ops.kernels()
+        with torch.cuda.stream(self.wgrad_stream):
+            self.wgrad_stream.wait_event(ready)
+            if blk.down_proj.requires_grad:
+                kn.moe_wgrad(dyd, hbuf, offsets, *moe_ops.wgrad_target(blk.down_proj), None)
+            if blk.gate_up_proj.requires_grad:
+                kn.moe_wgrad(dgu, xd, offsets, *moe_ops.wgrad_target(blk.gate_up_proj), None)
+            done = torch.cuda.Event()
+            done.record(self.wgrad_stream)
+        for t in (hbuf, dgu, offsets):  # allocated on the current stream, read on the side stream
+            t.record_stream(self.wgrad_stream)
+        self.pending_wgrad.append(done)
+        return done
+
+    def wait_previous_wgrad(self) -> None:
+        if self.previous_wgrad is not None:
+            torch.cuda.current_stream().wait_event(self.previous_wgrad)
+
+    def wait_wgrads(self) -> None:
+        """Make the current stream wait for every launched weight gradient (before the optimizer)."""
+        cur = torch.cuda.current_stream()
+        for ev in self.pending_wgrad:
+            cur.wait_event(ev)
+        self.pending_wgrad.clear()
+        self.previous_wgrad = None
 
     def _arena_for(self, t, k, h, slots, device) -> EpArena:
         layers = max(1, self.num_layers)
@@ -336,6 +386,8 @@ class P2PExpertParallel:
         t, h = x.shape
         k = blk.cfg.num_experts_per_tok
         w, idx, aux = self._router(blk, x, bias, aux_coef)
+        if self.pending_wgrad:  # a receive slab may still be read by a weight gradient of the last backward
+            self.wait_wgrads()
         arena = self._arena_for(t, k, h, blk.num_local_slots, x.device)
         slab = getattr(blk, "ep_slab", 0)
         y = _FusedEPMoE.apply(x, w, idx.to(torch.int32).contiguous(), blk, arena, slab)

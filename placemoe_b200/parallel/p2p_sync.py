@@ -136,15 +136,18 @@ class ReplicaGradSync:
             self._plans[blk.layer_key] = plan
         return plan
 
-    def layer_ready(self, blk) -> None:
-        """Called at the end of a layer's expert backward (main stream)."""
+    def layer_ready(self, blk, after: torch.cuda.Event | None = None) -> None:
+        """Called at the end of a layer's expert backward (main stream); ``after``: the event that marks
+        the end of the layer's weight gradients when they run on another stream."""
         if not self.armed:
             return
         plan = self._plan(blk)
         if not plan.active:  # no replicated expert in this layer on any rank
             return
-        ready = torch.cuda.Event()
-        ready.record()
+        ready = after
+        if ready is None:
+            ready = torch.cuda.Event()
+            ready.record()
         with torch.cuda.stream(self.stream):
             self.stream.wait_event(ready)
             sync_layer(blk, plan, self.x)

@@ -250,6 +250,11 @@ class Trainer:
         if aux is not None:
             total = total + aux / self.world
         total.backward()
+        ep = self.pstate.ep if self.pstate is not None else None
+        if hasattr(ep, "wait_wgrads"):
+            # the last MoE layer's weight gradients may still read its receive slab, which the next
+            # micro-batch's dispatch refills (peers store into it once this rank reaches that dispatch)
+            ep.wait_wgrads()
         return loss.detach()
 
     def train_step(self, input_ids: torch.Tensor, *, read_loss: bool = True, cu_seqlens: torch.Tensor | None = None):
