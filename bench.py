@@ -139,6 +139,8 @@ def plan_placement(trainer, pool, args, rank, world):
     parameter + optimizer-state migration.  Returns a summary for the JSON line."""
     import tempfile
 
+    import torch
+
     import torch.distributed as dist
 
     from placemoe_b200.parallel.migration import migrate_layer

@@ -6,7 +6,9 @@
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "placemoe_b200 planner C++ cores";
   m.def("accumulate_route_stats", &pmp::accumulate_route_stats, "demand/affinity accumulation for one source rank");
-  m.def("evaluate_routes", &pmp::evaluate_routes, "exact one-level route replay");
+  m.def("evaluate_routes", &pmp::evaluate_routes, "exact one-level route replay of one step");
+  m.def("evaluate_routes_batch", &pmp::evaluate_routes_batch,
+        "exact one-level route replay of several steps (S tensors per step), one result row per step");
   m.def("optimize_mapping", &pmp::optimize_mapping, "mapping coordinate descent (in place)");
   m.def("refine_partition", &pmp::refine_partition, "capacity-constrained pairwise exchange (in place)");
   m.def("optimize_mapping_normalized", &pmp::optimize_mapping_normalized,

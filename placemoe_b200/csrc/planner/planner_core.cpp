@@ -8,7 +8,10 @@
 // level, so the evaluator only counts per-destination-GPU unique rows.
 #include <torch/extension.h>
 
+#include <ATen/Parallel.h>
+
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <limits>
 #include <thread>
@@ -21,80 +24,169 @@ namespace pmp {
 // ---------------------------------------------------------------------------
 // Exact route replay.
 //
-// routes[s]: [T_s, k] logical experts chosen by tokens of source rank s.
+// routes[i]: [T_i, k] logical experts chosen by tokens of source rank i % S
+//            (S = mapping.size(0)); routes[i] belongs to step i / S.
 // mapping:   [S, E] physical slot used by source s for expert e.
 // slot_rank: [N] rank holding each slot.
 // For every token: destination ranks = rank(mapping[s, e_j]); each remote
 // destination receives the hidden row once (deduplicated) plus `meta_bytes`
-// per assignment.  Returns a float64 tensor:
+// per assignment.  Returns float64 [n_steps, 5 + 3R], one row per step:
 //   [0] max over ranks of max(send_bytes, recv_bytes)
 //   [1] max over ranks of assignments
 //   [2] total remote unique rows      [3] total remote assignments
-//   [4] total assignments             [5 .. 5+S) send bytes per rank
-//   [5+S .. 5+2S) recv bytes          [5+2S .. 5+3S) assignments per rank
+//   [4] total assignments             [5 .. 5+R) send bytes per rank
+//   [5+R .. 5+2R) recv bytes          [5+2R .. 5+3R) assignments per rank
+//
+// The (step, source) pairs are independent: they run on a pool of
+// at::get_num_threads() threads (the caller's torch thread setting, which
+// the planner process pins to its CPU set), each into its own integer
+// counters, and are summed in a fixed order afterwards, so the result does not
+// depend on the thread count.  Counting is in integers (rows and assignments
+// per destination); bytes are formed once per step.
 // ---------------------------------------------------------------------------
-torch::Tensor evaluate_routes(std::vector<torch::Tensor> routes, torch::Tensor mapping, torch::Tensor slot_rank,
-                              double row_bytes, double meta_bytes) {
-  const int64_t S = (int64_t)routes.size();
-  auto M = mapping.to(torch::kInt64).contiguous();
-  auto R = slot_rank.to(torch::kInt64).contiguous();
-  TORCH_CHECK(M.dim() == 2 && M.size(0) == S, "mapping must be [S, E]");
-  const int64_t E = M.size(1);
-  const int64_t* mp = M.data_ptr<int64_t>();
-  const int64_t* rp = R.data_ptr<int64_t>();
-  const int64_t N = R.numel();
-  int64_t num_ranks = 0;
-  for (int64_t i = 0; i < N; ++i) num_ranks = std::max(num_ranks, rp[i] + 1);
-  TORCH_CHECK(num_ranks <= 64, "evaluate_routes supports up to 64 ranks");
-  std::vector<double> send(num_ranks, 0.0), recv(num_ranks, 0.0), assign(num_ranks, 0.0);
-  double rows_remote = 0, asg_remote = 0, asg_total = 0;
-  for (int64_t s = 0; s < S; ++s) {
-    auto rt = routes[s].to(torch::kInt64).contiguous();
-    TORCH_CHECK(rt.dim() == 2, "routes must be [T, k]");
-    const int64_t T = rt.size(0), K = rt.size(1);
-    const int64_t* r = rt.data_ptr<int64_t>();
-    const int64_t* ms = mp + s * E;
-    const int64_t src_rank = s;  // source ranks are EP ranks
-    for (int64_t t = 0; t < T; ++t) {
-      uint64_t mask = 0;
-      int cnt[64];
-      for (int64_t j = 0; j < K; ++j) {
-        const int64_t e = r[t * K + j];
-        TORCH_CHECK(e >= 0 && e < E, "route expert out of range");
-        const int64_t slot = ms[e];
-        TORCH_CHECK(slot >= 0 && slot < N, "mapping slot out of range");
-        const int64_t d = rp[slot];
-        if (!((mask >> d) & 1)) { mask |= 1ull << d; cnt[d] = 0; }
-        cnt[d] += 1;
-        assign[d] += 1;
-      }
-      asg_total += K;
-      for (int64_t d = 0; d < num_ranks; ++d) {
-        if (!((mask >> d) & 1) || d == src_rank) continue;
-        const double bytes = row_bytes + meta_bytes * cnt[d];
-        send[src_rank] += bytes;
-        recv[d] += bytes;
-        rows_remote += 1;
-        asg_remote += cnt[d];
-      }
+namespace {
+
+struct SourceCounts {
+  std::vector<int64_t> rows, asg;  // per destination rank: remote unique rows / remote assignments received
+  std::vector<int64_t> load;       // per destination rank: all assignments (local ones included)
+  int64_t total = 0;
+  bool bad = false;
+};
+
+template <typename Idx>
+void replay_source(const Idx* r, int64_t T, int64_t K, const uint8_t* dest, int64_t E, int64_t src, int64_t R,
+                   SourceCounts& c) {
+  c.rows.assign(R, 0);
+  c.asg.assign(R, 0);
+  c.load.assign(R, 0);
+  int32_t cnt[64];
+  for (int64_t t = 0; t < T; ++t) {
+    uint64_t mask = 0;
+    const Idx* row = r + t * K;
+    for (int64_t j = 0; j < K; ++j) {
+      const int64_t e = (int64_t)row[j];
+      if (e < 0 || e >= E) { c.bad = true; return; }
+      const int d = dest[e];
+      const uint64_t bit = 1ull << d;
+      if (!(mask & bit)) { mask |= bit; cnt[d] = 0; }
+      ++cnt[d];
+    }
+    for (uint64_t m = mask; m; m &= m - 1) {
+      const int d = __builtin_ctzll(m);
+      c.load[d] += cnt[d];
+      if (d == src) continue;
+      c.rows[d] += 1;
+      c.asg[d] += cnt[d];
     }
   }
-  auto out = torch::zeros({5 + 3 * num_ranks}, torch::kFloat64);
-  double* o = out.data_ptr<double>();
-  double peak_bytes = 0, peak_asg = 0;
-  for (int64_t d = 0; d < num_ranks; ++d) {
-    peak_bytes = std::max(peak_bytes, std::max(send[d], recv[d]));
-    peak_asg = std::max(peak_asg, assign[d]);
-    o[5 + d] = send[d];
-    o[5 + num_ranks + d] = recv[d];
-    o[5 + 2 * num_ranks + d] = assign[d];
+  c.total = T * K;
+}
+
+template <typename F>
+void run_pool(int64_t items, F&& fn) {
+  const int64_t nt = std::max<int64_t>(1, std::min<int64_t>(items, at::get_num_threads()));
+  if (nt == 1) {
+    for (int64_t i = 0; i < items; ++i) fn(i);
+    return;
   }
-  o[0] = peak_bytes;
-  o[1] = peak_asg;
-  o[2] = rows_remote;
-  o[3] = asg_remote;
-  o[4] = asg_total;
+  std::atomic<int64_t> next{0};
+  std::vector<std::thread> pool;
+  pool.reserve(nt);
+  for (int64_t w = 0; w < nt; ++w)
+    pool.emplace_back([&] {
+      for (int64_t i = next.fetch_add(1); i < items; i = next.fetch_add(1)) fn(i);
+    });
+  for (auto& th : pool) th.join();
+}
+
+}  // namespace
+
+torch::Tensor evaluate_routes_batch(std::vector<torch::Tensor> routes, torch::Tensor mapping, torch::Tensor slot_rank,
+                                    double row_bytes, double meta_bytes) {
+  auto M = mapping.to(torch::kInt64).contiguous();
+  auto Rk = slot_rank.to(torch::kInt64).contiguous();
+  TORCH_CHECK(M.dim() == 2, "mapping must be [S, E]");
+  const int64_t S = M.size(0), E = M.size(1);
+  TORCH_CHECK(S > 0 && (int64_t)routes.size() % S == 0, "routes must hold S tensors per step");
+  const int64_t steps = (int64_t)routes.size() / S;
+  const int64_t* mp = M.data_ptr<int64_t>();
+  const int64_t* rp = Rk.data_ptr<int64_t>();
+  const int64_t N = Rk.numel();
+  int64_t R = 0;
+  for (int64_t i = 0; i < N; ++i) {
+    TORCH_CHECK(rp[i] >= 0, "slot rank must be non-negative");
+    R = std::max(R, rp[i] + 1);
+  }
+  TORCH_CHECK(R <= 64, "route replay supports up to 64 ranks");
+  TORCH_CHECK(S <= R, "more sources than ranks");
+  // destination rank of every (source, expert), validated once
+  std::vector<uint8_t> dest(S * E);
+  for (int64_t i = 0; i < S * E; ++i) {
+    TORCH_CHECK(mp[i] >= 0 && mp[i] < N, "mapping slot out of range");
+    dest[i] = (uint8_t)rp[mp[i]];
+  }
+  std::vector<torch::Tensor> rt(routes.size());
+  for (size_t i = 0; i < routes.size(); ++i) {
+    auto x = routes[i];
+    if (x.scalar_type() != torch::kInt32 && x.scalar_type() != torch::kInt64) x = x.to(torch::kInt64);
+    rt[i] = x.contiguous();
+    TORCH_CHECK(rt[i].dim() == 2, "routes must be [T, k]");
+  }
+  std::vector<SourceCounts> part(routes.size());
+  run_pool((int64_t)routes.size(), [&](int64_t i) {
+    const int64_t s = i % S;
+    const auto& x = rt[i];
+    if (x.scalar_type() == torch::kInt32)
+      replay_source(x.data_ptr<int32_t>(), x.size(0), x.size(1), dest.data() + s * E, E, s, R, part[i]);
+    else
+      replay_source(x.data_ptr<int64_t>(), x.size(0), x.size(1), dest.data() + s * E, E, s, R, part[i]);
+  });
+  for (const auto& c : part) TORCH_CHECK(!c.bad, "route expert out of range");
+  auto out = torch::zeros({steps, 5 + 3 * R}, torch::kFloat64);
+  double* o = out.data_ptr<double>();
+  std::vector<int64_t> recv_rows(R), recv_asg(R), load(R);
+  for (int64_t st = 0; st < steps; ++st) {
+    double* row = o + st * (5 + 3 * R);
+    std::fill(recv_rows.begin(), recv_rows.end(), 0);
+    std::fill(recv_asg.begin(), recv_asg.end(), 0);
+    std::fill(load.begin(), load.end(), 0);
+    int64_t rows_remote = 0, asg_remote = 0, asg_total = 0;
+    for (int64_t s = 0; s < S; ++s) {
+      const auto& c = part[st * S + s];
+      int64_t sent_rows = 0, sent_asg = 0;
+      for (int64_t d = 0; d < R; ++d) {
+        recv_rows[d] += c.rows[d];
+        recv_asg[d] += c.asg[d];
+        load[d] += c.load[d];
+        sent_rows += c.rows[d];
+        sent_asg += c.asg[d];
+      }
+      row[5 + s] = row_bytes * (double)sent_rows + meta_bytes * (double)sent_asg;
+      rows_remote += sent_rows;
+      asg_remote += sent_asg;
+      asg_total += c.total;
+    }
+    double peak_bytes = 0, peak_asg = 0;
+    for (int64_t d = 0; d < R; ++d) {
+      const double recv = row_bytes * (double)recv_rows[d] + meta_bytes * (double)recv_asg[d];
+      row[5 + R + d] = recv;
+      row[5 + 2 * R + d] = (double)load[d];
+      peak_bytes = std::max(peak_bytes, std::max(row[5 + d], recv));
+      peak_asg = std::max(peak_asg, (double)load[d]);
+    }
+    row[0] = peak_bytes;
+    row[1] = peak_asg;
+    row[2] = (double)rows_remote;
+    row[3] = (double)asg_remote;
+    row[4] = (double)asg_total;
+  }
   return out;
+}
+
+torch::Tensor evaluate_routes(std::vector<torch::Tensor> routes, torch::Tensor mapping, torch::Tensor slot_rank,
+                              double row_bytes, double meta_bytes) {
+  TORCH_CHECK(mapping.dim() == 2 && mapping.size(0) == (int64_t)routes.size(), "mapping must be [S, E]");
+  return evaluate_routes_batch(std::move(routes), mapping, slot_rank, row_bytes, meta_bytes)[0];
 }
 
 // ---------------------------------------------------------------------------

@@ -54,7 +54,8 @@ class RouteReplayEvaluator:
     def __init__(self, samples, topology: PlaceMoETopology, *, hidden_size: int, bytes_per_element: int,
                  calibration: PlaceMoECalibration | None = None):
         """samples: list of steps, each a list (per source rank) of [T, k] int routes."""
-        self.samples = [[torch.as_tensor(r).to(torch.int64).contiguous() for r in step] for step in samples]
+        self.samples = [[torch.as_tensor(r).to(torch.int32).contiguous() for r in step] for step in samples]
+        self._flat = [r for step in self.samples for r in step]
         self.topology = topology
         self.row_bytes = float(hidden_size * bytes_per_element)
         self.cal = calibration or PlaceMoECalibration()
@@ -63,10 +64,8 @@ class RouteReplayEvaluator:
     def replay(self, mapping: np.ndarray) -> PlanCost:
         core = load_planner()
         m = torch.from_numpy(np.array(mapping, dtype=np.int64, copy=True))
-        acc = None
-        for step in self.samples:
-            out = core.evaluate_routes(step, m, self.slot_rank, self.row_bytes, float(META_BYTES_PER_ASSIGNMENT)).numpy()
-            acc = out if acc is None else acc + out
+        acc = core.evaluate_routes_batch(self._flat, m, self.slot_rank, self.row_bytes,
+                                         float(META_BYTES_PER_ASSIGNMENT)).numpy().sum(axis=0)
         n = len(self.samples)
         peak_bytes, peak_asg = acc[0] / n, acc[1] / n
         c = self.cal

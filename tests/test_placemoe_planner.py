@@ -135,6 +135,59 @@ def test_evaluator_counts_dedup_and_local_traffic():
     assert c.peak_assignments == 5  # rank0: 3 assignments, rank1: 5
 
 
+def _replay_oracle(steps, mapping, slot_rank, row_bytes, meta_bytes):
+    """Plain-Python restatement of the route replay: one row per step."""
+    r = int(slot_rank.max()) + 1
+    rows = []
+    for step in steps:
+        send, recv, load = np.zeros(r), np.zeros(r), np.zeros(r)
+        rem_rows = rem_asg = total = 0
+        for s, routes in enumerate(step):
+            for tok in routes.tolist():
+                per = {}
+                for e in tok:
+                    d = int(slot_rank[mapping[s, e]])
+                    per[d] = per.get(d, 0) + 1
+                    load[d] += 1
+                total += len(tok)
+                for d, c in per.items():
+                    if d != s:
+                        send[s] += row_bytes + meta_bytes * c
+                        recv[d] += row_bytes + meta_bytes * c
+                        rem_rows += 1
+                        rem_asg += c
+        rows.append([max(np.maximum(send, recv)), load.max(), rem_rows, rem_asg, total, *send, *recv, *load])
+    return np.array(rows)
+
+
+def test_batched_replay_matches_oracle_at_every_thread_count():
+    from placemoe_b200._build import load_planner
+
+    core = load_planner()
+    rng = np.random.default_rng(7)
+    s, e, k, slots = 4, 12, 3, 16
+    slot_rank = np.repeat(np.arange(s), slots // s)
+    mapping = rng.integers(0, slots, size=(s, e))
+    steps = [[torch.from_numpy(np.stack([rng.choice(e, k, replace=False) for _ in range(int(rng.integers(1, 40)))]))
+              for _ in range(s)] for _ in range(3)]
+    want = _replay_oracle(steps, mapping, slot_rank, 64.0, 8.0)
+    flat = [x.to(torch.int32) for st in steps for x in st]
+    old = torch.get_num_threads()
+    try:
+        for nt in (1, 3, 8):
+            torch.set_num_threads(nt)
+            got = core.evaluate_routes_batch(flat, torch.from_numpy(mapping), torch.from_numpy(slot_rank), 64.0, 8.0)
+            np.testing.assert_array_equal(got.numpy(), want)
+    finally:
+        torch.set_num_threads(old)
+    one = core.evaluate_routes(steps[1], torch.from_numpy(mapping), torch.from_numpy(slot_rank), 64.0, 8.0)
+    np.testing.assert_array_equal(one.numpy(), want[1])
+    bad = [x.clone() for x in flat]
+    bad[5][0, 0] = e
+    with pytest.raises(RuntimeError, match="out of range"):
+        core.evaluate_routes_batch(bad, torch.from_numpy(mapping), torch.from_numpy(slot_rank), 64.0, 8.0)
+
+
 def _plan_roundtrip(plan, topo):
     art = build_placemoe_artifact({"model.layers.0.mlp.experts": plan}, topo)
     text = json.dumps(art)
