@@ -631,11 +631,12 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 // that the even CTA also has the diagonal tile 2p of every head.  For each common tile the
 // two dQ partials are added on chip before one reduce-add: the even CTA owns head dims
 // [0, D/2), the odd CTA [D/2, D).  The warpgroup holding the dims the partner owns stores
-// them with st.shared::cluster straight into the partner's staging boxes and arrives on the
-// partner's `xfer_full` (release, cluster scope); the owner adds its own registers to the
-// received values in place and issues the TMA reduce-add.  Before each transfer the owner
-// signals `xfer_free` (its boxes are no longer read by its previous reductions and, for the
-// boxes in the dS^T buffer, by its MMAs).  This halves the fp32 bytes reduced into dQ.
+// them with st.shared::cluster straight into the partner's staging buffer (the 32 KB of boxes
+// 0-1, which on common tiles only the owning warpgroup uses) and arrives on the partner's
+// `xfer_full` (release, cluster scope); the owner adds its own registers to the received
+// values in place and issues the TMA reduce-add.  The owner signals `xfer_free` as soon as
+// the buffer is no longer read by its own reductions, one tile ahead, so the sender does not
+// wait on the owner's progress.  This halves the fp32 bytes reduced into dQ.
 constexpr int kBwdThreads = 320;
 constexpr int kBwdCompute = 256;  // threads of the two compute warpgroups
 
@@ -868,6 +869,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     };
     probs(0);
     const uint64_t sc2 = f2_pack(a.scale, a.scale);
+    // PAIR: tile it is common with the partner; the owning warpgroup's buffer for it is sStage
+    auto common_tile = [&](int it) { return PAIR && (crank == 1u || it % nqt != 0); };
+    if (PAIR && issuer && cg == (int)crank && common_tile(0))
+      mbar_arrive_cluster(mapa_shared(smem_u32(xfer_free), crank ^ 1u));
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / nqt;
       const int qt = kt + it % nqt;
@@ -944,7 +949,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             ok = mbar_wait_cluster_abortable(xfer_free, par, s_abort);
             ok = __all_sync(0xffffffffu, ok);
             if (ok) {
-              const uint32_t rbox = mapa_shared(smem_u32(bx0), crank ^ 1u);
+              const uint32_t rbox = mapa_shared(smem_u32(sStage), crank ^ 1u);
 #pragma unroll
               for (int cc = 0; cc < kBoxes; ++cc)
 #pragma unroll
@@ -956,8 +961,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             }
             continue;
           }
-          // this CTA owns these dims: free the boxes for the partner, wait for its half, add it
-          if (issuer) mbar_arrive_cluster(mapa_shared(smem_u32(xfer_free), crank ^ 1u));
+          // this CTA owns these dims: wait for the partner's half in sStage, add it
           ok = mbar_wait_cluster_abortable(xfer_full, par, s_abort);
           ok = __all_sync(0xffffffffu, ok);
           if (ok) {
@@ -965,7 +969,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
             for (int cc = 0; cc < kBoxes; ++cc)
 #pragma unroll
               for (int i = 0; i < 8; ++i) {
-                const uint4 w = *reinterpret_cast<const uint4*>(bx0 + cc * 16384 + r * 128 + ((i ^ (r & 7)) << 4));
+                const uint4 w = *reinterpret_cast<const uint4*>(sStage + cc * 16384 + r * 128 + ((i ^ (r & 7)) << 4));
                 uint32_t* d4 = dq + cc * 32 + 4 * i;
                 float x0, x1, x2, x3;
                 f2_unpack(add_f2(f2_pack(__uint_as_float(d4[0]), __uint_as_float(d4[1])),
@@ -978,19 +982,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
         }
       }
+      // owner of a common tile: its staging is sStage (where the partner's half landed)
+      uint8_t* const bx = common_tile(it) ? sStage : bx0;
 #pragma unroll
       for (int cc = 0; cc < kBoxes; ++cc)
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_swz(bx0 + cc * 16384, r, i,
+          st_swz(bx + cc * 16384, r, i,
                  make_uint4(dq[cc * 32 + 4 * i], dq[cc * 32 + 4 * i + 1], dq[cc * 32 + 4 * i + 2],
                             dq[cc * 32 + 4 * i + 3]));
       fence_proxy_async_smem();
       named_bar_sync(1 + cg, 128);
       if (issuer) {
 #pragma unroll
-        for (int cc = 0; cc < kBoxes; ++cc) tma_reduce_add_3d(&tmDQ, bx0 + cc * 16384, cg * kQD + cc * 32, h, tq0);
+        for (int cc = 0; cc < kBoxes; ++cc) tma_reduce_add_3d(&tmDQ, bx + cc * 16384, cg * kQD + cc * 32, h, tq0);
         bulk_commit();
+        // the owner frees sStage for the partner's next common tile once this reduction has read it
+        // (the even CTA's diagonal tiles also stage there, so the release waits for those too)
+        if (PAIR && cg == (int)crank && it + 1 < n_it && common_tile(it + 1)) {
+          bulk_wait_read_0();
+          mbar_arrive_cluster(mapa_shared(smem_u32(xfer_free), crank ^ 1u));
+        }
       }
     }
     if (issuer) bulk_wait_all();  // reductions complete before the CTA's shared memory goes away
