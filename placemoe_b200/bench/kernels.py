@@ -146,15 +146,7 @@ def bench_attn(batch, seq, heads, kv_heads, dim, iters):
     report(f"attn_fwd[B{batch} S{seq} H{heads}/{kv_heads} D{dim}]",
            time_fn(lambda: kernels().attn_fwd(q, kk, v, seq), iters), f)
     do = torch.randn_like(o)
-    kn = kernels()
-    old = kn.attn_bwd_set_pair(False)
-    try:
-        report("attn_bwd[single CTA]", time_fn(lambda: kn.attn_bwd(q, kk, v, o, lse, do, seq), iters), 2.5 * f)
-        kn.attn_bwd_set_pair(True)
-        report("attn_bwd[CTA pairs, dQ pre-add]", time_fn(lambda: kn.attn_bwd(q, kk, v, o, lse, do, seq), iters),
-               2.5 * f)
-    finally:
-        kn.attn_bwd_set_pair(old)
+    report("attn_bwd", time_fn(lambda: kernels().attn_bwd(q, kk, v, o, lse, do, seq), iters), 2.5 * f)
 
 
 def bench_attn_compare(batch, seq, heads, kv_heads, dim, iters):

@@ -33,7 +33,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("doc_lo") = py::none());
   m.def("attn_bwd", &pm::attn_bwd, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
         py::arg("dout"), py::arg("S"), py::arg("doc_hi") = py::none());
-  m.def("attn_bwd_set_pair", &pm::attn_bwd_set_pair, "use 2-CTA clusters with on-chip dQ pre-add; returns the previous setting");
   // loss
   m.def("ce_fwd_bwd", &pm::ce_fwd_bwd);
   // peer-to-peer data plane

@@ -625,18 +625,6 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ o, const __n
 // column), so each MMA k-step of 16 queries reads 8 columns.
 // CTAs run (batch, kv head) outer and key tile inner, so the CTAs resident at one time
 // share a few heads and their Q / dO tiles and dQ reductions stay in L2.
-//
-// PAIR (an even number of key tiles): CTAs 2p and 2p+1 of a 2-CTA cluster hold key tiles
-// 2p and 2p+1 of one (batch, kv head) and walk the same (head, query tile) sequence, except
-// that the even CTA also has the diagonal tile 2p of every head.  For each common tile the
-// two dQ partials are added on chip before one reduce-add: the even CTA owns head dims
-// [0, D/2), the odd CTA [D/2, D).  The warpgroup holding the dims the partner owns stores
-// them with st.shared::cluster straight into the partner's staging buffer (the 32 KB of boxes
-// 0-1, which on common tiles only the owning warpgroup uses) and arrives on the partner's
-// `xfer_full` (release, cluster scope); the owner adds its own registers to the received
-// values in place and issues the TMA reduce-add.  The owner signals `xfer_free` as soon as
-// the buffer is no longer read by its own reductions, one tile ahead, so the sender does not
-// wait on the owner's progress.  This halves the fp32 bytes reduced into dQ.
 constexpr int kBwdThreads = 320;
 constexpr int kBwdCompute = 256;  // threads of the two compute warpgroups
 
@@ -644,7 +632,7 @@ constexpr int kBwdCompute = 256;  // threads of the two compute warpgroups
 // base of dynamic shared memory must be 1024-byte aligned (checked in the kernel).
 template <int D>
 constexpr int bwd_smem() {
-  return 5 * (D / 64) * 16384 + 32768 + 32768 + 2048 + 256;
+  return 5 * (D / 64) * 16384 + 32768 + 32768 + 2048 + 128;
 }
 
 // P = 2^(S c - lse) for 32 queries of one key row, as bf16 pairs.  When MASK, query columns
@@ -673,7 +661,7 @@ PM_DEVICE void bwd_probs(const uint32_t (&sv)[32], const float4* lse4, float c, 
   }
 }
 
-template <int D, bool PAIR>
+template <int D>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
@@ -713,9 +701,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint64_t* ds_done = bars + 11;
   uint64_t* dq_drained = bars + 12;
   uint64_t* dkv_full = bars + 13;
-  uint64_t* xfer_full = bars + 14;  // PAIR: the partner's dQ half for this CTA's dims has landed
-  uint64_t* xfer_free = bars + 15;  // PAIR: the partner's staging boxes may be written
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 16);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -737,19 +723,15 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(s_full, 1); mbar_init(dp_full, 1); mbar_init(dq_full, 1);
     mbar_init(p_done, kBwdCompute); mbar_init(ds_done, kBwdCompute); mbar_init(dq_drained, kBwdCompute);
     mbar_init(dkv_full, 1);
-    mbar_init(xfer_full, 128);
-    mbar_init(xfer_free, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
   if (warp == 1) { tmem_alloc(s_tmem, 512); tmem_relinquish(); }
   tc_fence_before();
   __syncthreads();
-  if (PAIR) cluster_sync();  // the partner's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const uint32_t tA = tmem, tB = tmem + 128, tDV = tmem + 256, tDK = tmem + 256 + D;
-  const uint32_t crank = PAIR ? cluster_ctarank() : 0u;  // == kt & 1 (clusters of 2, nq even)
 
   if (warp == 0) {
     if (lane == 0) {
@@ -869,10 +851,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     };
     probs(0);
     const uint64_t sc2 = f2_pack(a.scale, a.scale);
-    // PAIR: tile it is common with the partner; the owning warpgroup's buffer for it is sStage
-    auto common_tile = [&](int it) { return PAIR && (crank == 1u || it % nqt != 0); };
-    if (PAIR && issuer && cg == (int)crank && common_tile(0))
-      mbar_arrive_cluster(mapa_shared(smem_u32(xfer_free), crank ^ 1u));
     for (int it = 0; it < n_it; ++it) {
       const int h = hk * G + it / nqt;
       const int qt = kt + it % nqt;
@@ -938,71 +916,19 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       }
       if (issuer) bulk_wait_read_0();  // this group's previous reductions have read its staging
       if (!named_bar_and(6, kBwdCompute, ok)) { ok = false; break; }
-      if constexpr (PAIR) {
-        // common tile with the partner (every tile of the odd CTA, all but the diagonal of the even one)
-        const int off = it % nqt;
-        if (crank == 1u || off != 0) {
-          const int mi = crank == 1u ? it : (it / nqt) * (nqt - 1) + off - 1;
-          const uint32_t par = (uint32_t)(mi & 1);
-          if (cg != (int)crank) {
-            // the partner owns these dims: store them into its staging boxes, then arrive there
-            ok = mbar_wait_cluster_abortable(xfer_free, par, s_abort);
-            ok = __all_sync(0xffffffffu, ok);
-            if (ok) {
-              const uint32_t rbox = mapa_shared(smem_u32(sStage), crank ^ 1u);
-#pragma unroll
-              for (int cc = 0; cc < kBoxes; ++cc)
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  st_cluster_v4(rbox + cc * 16384 + r * 128 + ((i ^ (r & 7)) << 4),
-                                make_uint4(dq[cc * 32 + 4 * i], dq[cc * 32 + 4 * i + 1], dq[cc * 32 + 4 * i + 2],
-                                           dq[cc * 32 + 4 * i + 3]));
-              mbar_arrive_cluster(mapa_shared(smem_u32(xfer_full), crank ^ 1u));
-            }
-            continue;
-          }
-          // this CTA owns these dims: wait for the partner's half in sStage, add it
-          ok = mbar_wait_cluster_abortable(xfer_full, par, s_abort);
-          ok = __all_sync(0xffffffffu, ok);
-          if (ok) {
-#pragma unroll
-            for (int cc = 0; cc < kBoxes; ++cc)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const uint4 w = *reinterpret_cast<const uint4*>(sStage + cc * 16384 + r * 128 + ((i ^ (r & 7)) << 4));
-                uint32_t* d4 = dq + cc * 32 + 4 * i;
-                float x0, x1, x2, x3;
-                f2_unpack(add_f2(f2_pack(__uint_as_float(d4[0]), __uint_as_float(d4[1])),
-                                 f2_pack(__uint_as_float(w.x), __uint_as_float(w.y))), x0, x1);
-                f2_unpack(add_f2(f2_pack(__uint_as_float(d4[2]), __uint_as_float(d4[3])),
-                                 f2_pack(__uint_as_float(w.z), __uint_as_float(w.w))), x2, x3);
-                d4[0] = __float_as_uint(x0); d4[1] = __float_as_uint(x1);
-                d4[2] = __float_as_uint(x2); d4[3] = __float_as_uint(x3);
-              }
-          }
-        }
-      }
-      // owner of a common tile: its staging is sStage (where the partner's half landed)
-      uint8_t* const bx = common_tile(it) ? sStage : bx0;
 #pragma unroll
       for (int cc = 0; cc < kBoxes; ++cc)
 #pragma unroll
         for (int i = 0; i < 8; ++i)
-          st_swz(bx + cc * 16384, r, i,
+          st_swz(bx0 + cc * 16384, r, i,
                  make_uint4(dq[cc * 32 + 4 * i], dq[cc * 32 + 4 * i + 1], dq[cc * 32 + 4 * i + 2],
                             dq[cc * 32 + 4 * i + 3]));
       fence_proxy_async_smem();
       named_bar_sync(1 + cg, 128);
       if (issuer) {
 #pragma unroll
-        for (int cc = 0; cc < kBoxes; ++cc) tma_reduce_add_3d(&tmDQ, bx + cc * 16384, cg * kQD + cc * 32, h, tq0);
+        for (int cc = 0; cc < kBoxes; ++cc) tma_reduce_add_3d(&tmDQ, bx0 + cc * 16384, cg * kQD + cc * 32, h, tq0);
         bulk_commit();
-        // the owner frees sStage for the partner's next common tile once this reduction has read it
-        // (the even CTA's diagonal tiles also stage there, so the release waits for those too)
-        if (PAIR && cg == (int)crank && it + 1 < n_it && common_tile(it + 1)) {
-          bulk_wait_read_0();
-          mbar_arrive_cluster(mapa_shared(smem_u32(xfer_free), crank ^ 1u));
-        }
       }
     }
     if (issuer) bulk_wait_all();  // reductions complete before the CTA's shared memory goes away
@@ -1039,7 +965,6 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
-  if (PAIR) cluster_sync();  // no CTA leaves while its partner may still store into its shared memory
 }
 
 // fp32 -> bf16
@@ -1153,36 +1078,6 @@ std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Ten
   return {o, lse};
 }
 
-// Backward with CTA pairs (on-chip dQ pre-add) when the key-tile count is even; switchable for
-// comparisons.  Returns the previous setting.
-static bool g_attn_bwd_pair = false;
-bool attn_bwd_set_pair(bool on) {
-  const bool old = g_attn_bwd_pair;
-  g_attn_bwd_pair = on;
-  return old;
-}
-
-template <int D, bool PAIR>
-static void launch_bwd(int grid, cudaStream_t stream, const CUtensorMap& mq, const CUtensorMap& mk,
-                       const CUtensorMap& mv, const CUtensorMap& mdo, const CUtensorMap& mdq, const AttnArgs& a) {
-  auto kern = attn_bwd_kernel<D, PAIR>;
-  C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<D>()));
-  cudaLaunchConfig_t cfg;
-  memset(&cfg, 0, sizeof(cfg));
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(kBwdThreads, 1, 1);
-  cfg.dynamicSmemBytes = bwd_smem<D>();
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = PAIR ? 2 : 1;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = PAIR ? 1 : 0;
-  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, mdo, mdq, a));
-}
-
 std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dout, int64_t S,
                                     c10::optional<torch::Tensor> doc_hi) {
@@ -1217,14 +1112,16 @@ std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Ten
   CUtensorMap mq = head_map(q), mk = head_map(k), mv = head_map(v), mdo = head_map(dout);
   CUtensorMap mdq = dq_acc_map(dq_acc);
   const int grid = a.B * Hkv * ((int)S / kTile);
-  const bool pair = g_attn_bwd_pair && ((int)S / kTile) % 2 == 0;
   if (D == 128) {
-    if (pair) launch_bwd<128, true>(grid, stream, mq, mk, mv, mdo, mdq, a);
-    else launch_bwd<128, false>(grid, stream, mq, mk, mv, mdo, mdq, a);
+    auto kern = attn_bwd_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<128>()));
+    kern<<<grid, kBwdThreads, bwd_smem<128>(), stream>>>(mq, mk, mv, mdo, mdq, a);
   } else {
-    if (pair) launch_bwd<64, true>(grid, stream, mq, mk, mv, mdo, mdq, a);
-    else launch_bwd<64, false>(grid, stream, mq, mk, mv, mdo, mdq, a);
+    auto kern = attn_bwd_kernel<64>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bwd_smem<64>()));
+    kern<<<grid, kBwdThreads, bwd_smem<64>(), stream>>>(mq, mk, mv, mdo, mdq, a);
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
   const long long n = (long long)T * Hq * D;
   f32_to_bf16_kernel<<<(unsigned)((n / 4 + 255) / 256 + 1), 256, 0, stream>>>(dq_acc.data_ptr<float>(),
                                                                               (__nv_bfloat16*)dq.data_ptr(), n);

@@ -330,42 +330,6 @@ PM_DEVICE void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
 }
 
-// 16-byte store into shared memory given by a shared::cluster address (possibly the peer CTA's).
-PM_DEVICE void st_cluster_v4(uint32_t addr, uint4 v) {
-  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
-               "r"(v.w)
-               : "memory");
-}
-
-// try_wait with cluster-scope acquire: what the arriving threads of another CTA of the cluster
-// stored before their release-arrive is visible once the phase completed.
-PM_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n"
-      " mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded cluster-scope wait that also gives up when another role of the CTA raised `abort`.
-PM_DEVICE bool mbar_wait_cluster_abortable(uint64_t* bar, uint32_t parity, volatile int* abort) {
-  if (mbar_try_wait_cluster(bar, parity)) return true;
-  long long start = clock64();
-  while (!mbar_try_wait_cluster(bar, parity)) {
-    if (*abort) return false;
-    if (clock64() - start > kWaitBudgetCycles) {
-      set_error(kErrMbarTimeout);
-      *abort = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
 // Tensor loads into this CTA's shared memory whose completion is counted on the
 // pair leader's mbarrier (`bar_cluster_addr` from mapa_shared(..., 0)).
 PM_DEVICE void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int x, int y) {

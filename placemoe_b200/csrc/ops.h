@@ -52,7 +52,6 @@ void sq_norm(torch::Tensor table, torch::Tensor meta, torch::Tensor out);
 // attention_sm100.cu
 std::vector<torch::Tensor> attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t S,
                                     c10::optional<torch::Tensor> doc_lo);
-bool attn_bwd_set_pair(bool on);
 std::vector<torch::Tensor> attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o,
                                     torch::Tensor lse, torch::Tensor dout, int64_t S, c10::optional<torch::Tensor> doc_hi);
 

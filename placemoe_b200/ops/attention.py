@@ -14,7 +14,6 @@ attention forward/backward through FA2/FA3/FA4).
 from __future__ import annotations
 
 import math
-import os
 
 import torch
 import torch.nn.functional as F
@@ -65,17 +64,8 @@ def attention_reference(q, k, v, seq_len, docs=None):
     return o.transpose(1, 2).reshape(t, hq, d).to(q.dtype)
 
 
-_PAIR_SET = False
-
-
 def _has_kernel() -> bool:
-    global _PAIR_SET
-    kn = kernels()
-    if not _PAIR_SET and hasattr(kn, "attn_bwd_set_pair"):
-        # backward on 2-CTA clusters (dQ halves added on chip before one reduce-add); 0 turns it off
-        kn.attn_bwd_set_pair(os.environ.get("PLACEMOE_ATTN_BWD_PAIR", "0") != "0")
-        _PAIR_SET = True
-    return hasattr(kn, "attn_fwd")
+    return hasattr(kernels(), "attn_fwd")
 
 
 class _FlashAttn(torch.autograd.Function):

@@ -229,42 +229,6 @@ def test_attention_fwd_bwd(b, s, hq, hkv, d, qscale):
     assert math.isfinite(o.float().sum().item())
 
 
-@pytest.mark.parametrize("s,hq,hkv,d", [(512, 4, 4, 128), (768, 8, 2, 128), (1024, 2, 2, 64)])
-def test_attention_backward_pair_matches_single_cta(s, hq, hkv, d):
-    """The 2-CTA backward (dQ halves added on chip before one reduce-add) against the single-CTA
-    backward and the fp32 reference: same inputs, every gradient."""
-    from placemoe_b200.ops import check_device_error, kernels
-    from placemoe_b200.ops.attention import attention_reference
-
-    kn = kernels()
-    torch.manual_seed(5)
-    t = 2 * s
-    q = torch.randn(t, hq, d, device="cuda").to(torch.bfloat16)
-    k = torch.randn(t, hkv, d, device="cuda").to(torch.bfloat16)
-    v = torch.randn(t, hkv, d, device="cuda").to(torch.bfloat16)
-    o, lse = kn.attn_fwd(q, k, v, s)
-    g = torch.randn_like(o)
-    old = kn.attn_bwd_set_pair(False)
-    try:
-        single = kn.attn_bwd(q, k, v, o, lse, g, s)
-        kn.attn_bwd_set_pair(True)
-        paired = kn.attn_bwd(q, k, v, o, lse, g, s)
-        again = kn.attn_bwd(q, k, v, o, lse, g, s)
-    finally:
-        kn.attn_bwd_set_pair(old)
-    torch.cuda.synchronize()
-    check_device_error()
-    qr, kr, vr = (z.float().requires_grad_() for z in (q, k, v))
-    attention_reference(qr, kr, vr, s).backward(g.float())
-    for got1, got2, got3, want in zip(single, paired, again, (qr.grad, kr.grad, vr.grad)):
-        assert rel(got2, want) < 5e-2
-        assert rel(got3, want) < 5e-2
-        assert rel(got2, got1) < 1e-2
-    # dK and dV are accumulated inside one CTA: the pairing does not change them at all
-    for i in (1, 2):
-        assert torch.equal(single[i], paired[i]) and torch.equal(paired[i], again[i])
-
-
 def test_sq_norm_matches_torch():
     from placemoe_b200.ops import kernels
 
