@@ -2,7 +2,9 @@
 
 Drives the reference through its public API and stock code path, in the
 order its BaseTrainer uses: ``init_parallel_state`` (FSDP2 data parallel +
-expert parallel = world size), ``configure_hiermoe`` (defaults),
+expert parallel = world size), ``configure_hiermoe`` (its defaults: HierMoE off; with
+``--ref-hiermoe dedup`` at N > 1 its token-deduplicated dispatch/combine on, direct all-to-all,
+expert swap off),
 ``build_foundation_model`` (meta init) -> ``build_parallelize_model`` (FSDP2,
 mixed precision, gradient checkpointing as in its trainer default) ->
 ``build_optimizer`` (fused AdamW) and, per step, forward/backward of every
@@ -109,7 +111,10 @@ def main(args) -> int:
     init_parallel_state(dp_size=world, dp_shard_size=world, extra_parallel_sizes=(world,),
                         extra_parallel_names=("ep",), dp_mode="fsdp2")
     ps = get_parallel_state()
-    configure_hiermoe(HierMoEConfig(), ep_group=ps.ep_group if getattr(ps, "ep_enabled", False) else None,
+    hier = getattr(args, "ref_hiermoe", "off") == "dedup" and world > 1
+    hcfg = (HierMoEConfig(enable=True, token_dedup=True, communication_mode="direct", expert_swap=False)
+            if hier else HierMoEConfig())
+    configure_hiermoe(hcfg, ep_group=ps.ep_group if getattr(ps, "ep_enabled", False) else None,
                       ep_fsdp_size=ps.ep_fsdp_size if getattr(ps, "ep_enabled", False) else 1,
                       activation_checkpointing_enabled=ckpt, fsdp_offload_enabled=False,
                       gradient_bytes_per_element=4)
@@ -195,7 +200,9 @@ def main(args) -> int:
                        else "bf16 parameters and optimizer states (no FSDP on one GPU)",
                        "micro_batch": mb, "parallelism": f"fsdp{world}+ep{world}",
                        "ops": "moe fused_triton, attention sdpa, gradient checkpointing "
-                              + ("on (its trainer default)" if ckpt else "off")},
+                              + ("on (its trainer default)" if ckpt else "off"),
+                       "hiermoe": ("token-deduplicated dispatch/combine (direct all-to-all, no expert swap)"
+                                   if hier else "off (its trainer default)")},
             "e2e": {"value": round(tokens / (ms_e2e / 1e3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": pool[0].numel() * 8, "d2h_bytes_per_step": 4, "last_loss": last},
         }), flush=True)

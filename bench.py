@@ -71,6 +71,9 @@ def parse():
     p.add_argument("--layout-every", type=int, default=100, help="adaptive run: full (layout) update interval")
     p.add_argument("--ref-no-recompute", action="store_true",
                    help="reference arm: gradient checkpointing off (its trainer default is on)")
+    p.add_argument("--ref-hiermoe", default="off", choices=("off", "dedup"),
+                   help="reference arm, N > 1: 'dedup' enables its HierMoE token-deduplicated dispatch/combine "
+                        "(direct all-to-all, no expert swap); its trainer default is off")
     p.add_argument("--ulysses", type=int, default=1,
                    help="Ulysses sequence-parallel group size (consecutive ranks share a batch; attention runs "
                         "on whole sequences over head groups)")
