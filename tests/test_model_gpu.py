@@ -104,3 +104,34 @@ def test_activation_offload_is_transparent():
     # dQ accumulates with unordered fp32 reduce-adds: runs agree to rounding, not bit for bit
     diff = (grads[0][1] - grads[1][1]).norm() / grads[0][1].norm()
     assert diff.item() < 1e-3
+
+
+def test_route_capture_on_cuda_matches_last_routes(tmp_path):
+    """Route capture on the CUDA path: routes are queued to pinned host memory without a host
+    synchronisation per layer; after ``record_step`` the bundles hold exactly every micro-batch's routes."""
+    from placemoe_b200.data import SyntheticTokens
+    from placemoe_b200.parallel.route_capture import RouteRecorder
+    from placemoe_b200.placemoe.routes import load_routes
+    from placemoe_b200.trainer.base import TrainConfig, Trainer
+
+    cfg = TrainConfig(model="small_qwen3_moe", seq_len=256, batch_per_rank=4, micro_batch_size=2, lr=1e-3,
+                      total_steps=4, warmup_steps=0)
+    tr = Trainer(cfg)
+    seen = {}
+
+    class Spy(RouteRecorder):
+        def collect(self, blk, route):
+            if self.enabled:
+                seen.setdefault(blk.layer_idx, []).append(route.detach().clone())
+            super().collect(blk, route)
+
+    rec = Spy(tr.model, str(tmp_path))
+    rec.enabled = True
+    data = SyntheticTokens(tr.model_cfg.vocab_size, 4, 256, seed=0)
+    tr.train_step(next(data))
+    paths = rec.record_step(0)
+    assert len(paths) == len(list(tr.model.moe_blocks()))
+    for blk in tr.model.moe_blocks():
+        want = torch.cat([r.long().cpu() for r in seen[blk.layer_idx]], 0)
+        (got,), = load_routes(tmp_path, steps=[0], layer=blk.layer_idx, ep_size=1)
+        assert want.shape[0] == 4 * 256 and torch.equal(got, want)
