@@ -14,6 +14,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   // norms / rotary
   m.def("rmsnorm_fwd", &pm::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &pm::rmsnorm_bwd);
+  m.def("add_rmsnorm_fwd", &pm::add_rmsnorm_fwd, "h = x + res (bf16), y = rmsnorm(h): returns [h, y, rstd]");
+  m.def("rmsnorm_bwd_add", &pm::rmsnorm_bwd_add, "rmsnorm backward plus the residual-path gradient");
   m.def("qkv_rope_fwd", &pm::qkv_rope_fwd);
   m.def("qkv_rope_bwd", &pm::qkv_rope_bwd);
   // routing

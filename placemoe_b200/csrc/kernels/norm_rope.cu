@@ -3,7 +3,9 @@
 // rmsnorm_fwd/bwd: persistent warp-per-row kernels that stream rows through a
 //   shared-memory ring (cp.async.bulk + mbarrier), fp32 math; the backward
 //   keeps d(weight) partials in registers and adds them to the fp32 output
-//   with one atomic per element per CTA.
+//   with one atomic per element per CTA.  add_rmsnorm_fwd / rmsnorm_bwd_add fold
+//   the decoder's residual add (forward) and the residual-gradient add (backward)
+//   into the same pass.
 // qkv_rope_fwd/bwd: CTAs stride over tokens and split the fused QKV projection into
 //   q/k/v, applies RMSNorm to q and k (groups of `q_group`/`k_group`
 //   elements: head_dim for Qwen3-MoE per-head norms, the full width for
@@ -56,23 +58,31 @@ __device__ __forceinline__ void row_issue(uint8_t* stage, uint64_t* bar, const _
   for (int t = 0; t < NT; ++t) bulk_load(stage + t * rb, src[t] + row * H, rb, bar);
 }
 
-template <int VPL, typename WT>
+// ADD: the row is h = x + res (rounded to bf16, as a bf16 tensor add would), written to `h`, and
+// normalised; the residual add before a norm then costs no separate pass over the rows.
+template <int VPL, typename WT, bool ADD = false>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
                                                           __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
-                                                          int rows, int H, float eps, int S) {
+                                                          int rows, int H, float eps, int S,
+                                                          const __nv_bfloat16* __restrict__ res,
+                                                          __nv_bfloat16* __restrict__ h) {
+  constexpr int NT = ADD ? 2 : 1;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NW = gridDim.x * kRowWarps, gw = blockIdx.x * kRowWarps + warp;
   const uint32_t rb = (uint32_t)H * 2;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kRowMaxStages;
   float* ws = reinterpret_cast<float*>(smem + kRowBarBytes);
-  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 4 + (size_t)warp * S * rb;
-  const __nv_bfloat16* src[1] = {x};
+  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 4 + (size_t)warp * S * NT * rb;
+  const __nv_bfloat16* src[NT];
+  src[0] = x;
+  if constexpr (ADD) src[NT - 1] = res;
   for (int i = threadIdx.x; i < H; i += blockDim.x) ws[i] = ldw(w, i);
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
-    for (int s = 0; s < S && gw + s * NW < rows; ++s) row_issue<1>(ring + s * rb, &bars[s], src, gw + s * NW, H);
+    for (int s = 0; s < S && gw + s * NW < rows; ++s)
+      row_issue<NT>(ring + s * NT * rb, &bars[s], src, gw + s * NW, H);
   }
   __syncthreads();
   for (int k = 0;; ++k) {
@@ -81,12 +91,20 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
     const int s = k % S;
     // warp-uniform exit when the wait runs out of budget (error recorded)
     if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (k / S) & 1))) break;
-    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * rb);
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * NT * rb);
     uint4 q[VPL];
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       q[i] = xs[i * 32 + lane];
+      if constexpr (ADD) {
+        const uint4 b = reinterpret_cast<const uint4*>(ring + s * NT * rb + rb)[i * 32 + lane];
+        q[i] = make_uint4(pack_bf16(bf16_lo(q[i].x) + bf16_lo(b.x), bf16_hi(q[i].x) + bf16_hi(b.x)),
+                          pack_bf16(bf16_lo(q[i].y) + bf16_lo(b.y), bf16_hi(q[i].y) + bf16_hi(b.y)),
+                          pack_bf16(bf16_lo(q[i].z) + bf16_lo(b.z), bf16_hi(q[i].z) + bf16_hi(b.z)),
+                          pack_bf16(bf16_lo(q[i].w) + bf16_lo(b.w), bf16_hi(q[i].w) + bf16_hi(b.w)));
+        reinterpret_cast<uint4*>(h + (size_t)row * H)[i * 32 + lane] = q[i];
+      }
       const uint32_t u[4] = {q[i].x, q[i].y, q[i].z, q[i].w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -95,7 +113,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
       }
     }
     __syncwarp();
-    if (lane == 0 && row + S * NW < rows) row_issue<1>(ring + s * rb, &bars[s], src, row + S * NW, H);
+    if (lane == 0 && row + S * NW < rows) row_issue<NT>(ring + s * NT * rb, &bars[s], src, row + S * NW, H);
     ss = warp_sum(ss);
     const float r = rsqrtf(ss / H + eps);
     if (lane == 0) rstd[row] = r;
@@ -119,11 +137,15 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const __nv_bfloat16* _
 // Stage s of a warp holds [x row | dy row]; d(weight) partials stay in
 // registers over all rows of the warp, are summed over the CTA's warps in
 // shared memory and added to the fp32 output with one atomic per column per CTA.
-template <int VPL, typename WT>
+// ADD: dx also receives `dres`, the gradient that reaches the norm's input through the residual
+// path (dx = norm backward + dres, one rounding), so no separate gradient add runs.
+template <int VPL, typename WT, bool ADD = false>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ dy,
                                                           const __nv_bfloat16* __restrict__ x, const WT* __restrict__ w,
                                                           const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                                          float* __restrict__ dw, int rows, int H, int S) {
+                                                          float* __restrict__ dw, int rows, int H, int S,
+                                                          const __nv_bfloat16* __restrict__ dres) {
+  constexpr int NT = ADD ? 3 : 2;
   extern __shared__ __align__(128) uint8_t smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NW = gridDim.x * kRowWarps, gw = blockIdx.x * kRowWarps + warp;
@@ -131,8 +153,11 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem) + warp * kRowMaxStages;
   float* ws = reinterpret_cast<float*>(smem + kRowBarBytes);
   float* sdw = ws + H;
-  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 8 + (size_t)warp * S * 2 * rb;
-  const __nv_bfloat16* src[2] = {x, dy};
+  uint8_t* ring = smem + kRowBarBytes + (size_t)H * 8 + (size_t)warp * S * NT * rb;
+  const __nv_bfloat16* src[NT];
+  src[0] = x;
+  src[1] = dy;
+  if constexpr (ADD) src[NT - 1] = dres;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {
     ws[i] = ldw(w, i);
     sdw[i] = 0.f;
@@ -140,7 +165,8 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
   if (lane == 0) {
     for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
-    for (int s = 0; s < S && gw + s * NW < rows; ++s) row_issue<2>(ring + s * 2 * rb, &bars[s], src, gw + s * NW, H);
+    for (int s = 0; s < S && gw + s * NW < rows; ++s)
+      row_issue<NT>(ring + s * NT * rb, &bars[s], src, gw + s * NW, H);
   }
   __syncthreads();
   constexpr bool kKeep = VPL <= 8;
@@ -157,8 +183,9 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
     const float r = rstd[row];
     // warp-uniform exit when the wait runs out of budget (error recorded)
     if (!__all_sync(0xffffffffu, mbar_wait(&bars[s], (k / S) & 1))) break;
-    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * 2 * rb);
-    const uint4* gs = reinterpret_cast<const uint4*>(ring + s * 2 * rb + rb);
+    const uint4* xs = reinterpret_cast<const uint4*>(ring + s * NT * rb);
+    const uint4* gs = reinterpret_cast<const uint4*>(ring + s * NT * rb + rb);
+    const uint4* rs = reinterpret_cast<const uint4*>(ring + s * NT * rb + 2 * rb);  // ADD only
     uint4 qx[VPL], qg[VPL];
     float dot = 0.f;
 #pragma unroll
@@ -182,33 +209,44 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
         }
       }
     }
-    if constexpr (kKeep) {
+    if constexpr (kKeep && !ADD) {
       __syncwarp();
-      if (lane == 0 && row + S * NW < rows) row_issue<2>(ring + s * 2 * rb, &bars[s], src, row + S * NW, H);
+      if (lane == 0 && row + S * NW < rows) row_issue<NT>(ring + s * NT * rb, &bars[s], src, row + S * NW, H);
     }
     dot = warp_sum(dot);
+    if constexpr (ADD) __syncwarp();  // the stage is read again below: keep those loads after this point
     const float cf = dot * r * r * r / H;
     uint4* dr = reinterpret_cast<uint4*>(dx + (size_t)row * H);
 #pragma unroll
     for (int i = 0; i < VPL; ++i) {
       const int c = i * 32 + lane;
-      if constexpr (!kKeep) {  // wide rows: read the stage again instead of holding it in registers
+      if constexpr (!kKeep || ADD) {  // read the stage again instead of holding it in registers
         qx[i] = xs[c];
         qg[i] = gs[c];
       }
       const uint32_t ux[4] = {qx[i].x, qx[i].y, qx[i].z, qx[i].w}, ug[4] = {qg[i].x, qg[i].y, qg[i].z, qg[i].w};
       uint32_t o[4];
+      uint32_t ur[4] = {0u, 0u, 0u, 0u};
+      if constexpr (ADD) {
+        const uint4 q = rs[c];
+        ur[0] = q.x; ur[1] = q.y; ur[2] = q.z; ur[3] = q.w;
+      }
 #pragma unroll
       for (int e2 = 0; e2 < 4; ++e2) {
         const float2 wv = reinterpret_cast<const float2*>(ws)[4 * c + e2];
-        o[e2] = pack_bf16(r * bf16_lo(ug[e2]) * wv.x - cf * bf16_lo(ux[e2]),
-                          r * bf16_hi(ug[e2]) * wv.y - cf * bf16_hi(ux[e2]));
+        float a = r * bf16_lo(ug[e2]) * wv.x - cf * bf16_lo(ux[e2]);
+        float b = r * bf16_hi(ug[e2]) * wv.y - cf * bf16_hi(ux[e2]);
+        if constexpr (ADD) {
+          a += bf16_lo(ur[e2]);
+          b += bf16_hi(ur[e2]);
+        }
+        o[e2] = pack_bf16(a, b);
       }
       dr[c] = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    if constexpr (!kKeep) {
+    if constexpr (!kKeep || ADD) {
       __syncwarp();
-      if (lane == 0 && row + S * NW < rows) row_issue<2>(ring + s * 2 * rb, &bars[s], src, row + S * NW, H);
+      if (lane == 0 && row + S * NW < rows) row_issue<NT>(ring + s * NT * rb, &bars[s], src, row + S * NW, H);
     }
   }
   if constexpr (kKeep) {
@@ -265,7 +303,7 @@ std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double 
     auto kern = rmsnorm_fwd_kernel<VPL, WT_>;                                                                      \
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));                 \
     kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)x.data_ptr(), WPTR, (__nv_bfloat16*)y.data_ptr(),      \
-                                      rstd.data_ptr<float>(), rows, H, (float)eps, S);                             \
+                                      rstd.data_ptr<float>(), rows, H, (float)eps, S, nullptr, nullptr);           \
   })
   if (w.scalar_type() == torch::kFloat32) {
     PM_RMS_FWD(float, w.data_ptr<float>());
@@ -303,7 +341,7 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));             \
     kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), \
                                       WPTR, rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(),             \
-                                      dw.data_ptr<float>(), rows, H, S);                                       \
+                                      dw.data_ptr<float>(), rows, H, S, nullptr);                              \
   })
   if (w.scalar_type() == torch::kFloat32) {
     PM_RMS_BWD(float, w.data_ptr<float>());
@@ -312,6 +350,88 @@ torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, to
     PM_RMS_BWD(__nv_bfloat16, (const __nv_bfloat16*)w.data_ptr());
   }
 #undef PM_RMS_BWD
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return dx;
+}
+
+// h = x + res (bf16) and y = rmsnorm(h): returns {h, y, rstd}.
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == torch::kBFloat16 && x.is_contiguous(), "x must be contiguous bf16");
+  TORCH_CHECK(res.sizes() == x.sizes() && res.scalar_type() == torch::kBFloat16 && res.is_contiguous(),
+              "res must be contiguous bf16 of x's shape");
+  PM_CHECK_CUDA(res);
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  TORCH_CHECK(w.numel() == H && w.is_contiguous(), "weight size");
+  PM_CHECK_CUDA(w);
+  check_row_ptr(x, "x");
+  check_row_ptr(res, "res");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto h = torch::empty_like(x);
+  auto y = torch::empty_like(x);
+  auto rstd = torch::empty({rows}, x.options().dtype(torch::kFloat32));
+  if (rows == 0) return {h, y, rstd};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int S, smem;
+  row_stream_shape(H, 2, 1, &S, &smem);
+  const int grid = std::min(sm_count(), (rows + kRowWarps - 1) / kRowWarps);
+#define PM_ADD_RMS_FWD(WT_, WPTR)                                                                                  \
+  PM_VPL_DISPATCH(H, {                                                                                             \
+    auto kern = rmsnorm_fwd_kernel<VPL, WT_, true>;                                                                \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));                 \
+    kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)x.data_ptr(), WPTR, (__nv_bfloat16*)y.data_ptr(),      \
+                                      rstd.data_ptr<float>(), rows, H, (float)eps, S,                              \
+                                      (const __nv_bfloat16*)res.data_ptr(), (__nv_bfloat16*)h.data_ptr());         \
+  })
+  if (w.scalar_type() == torch::kFloat32) {
+    PM_ADD_RMS_FWD(float, w.data_ptr<float>());
+  } else {
+    TORCH_CHECK(w.scalar_type() == torch::kBFloat16, "weight must be fp32 or bf16");
+    PM_ADD_RMS_FWD(__nv_bfloat16, (const __nv_bfloat16*)w.data_ptr());
+  }
+#undef PM_ADD_RMS_FWD
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return {h, y, rstd};
+}
+
+// rmsnorm backward whose dx also receives the residual-path gradient `dres`; accumulates into dw.
+torch::Tensor rmsnorm_bwd_add(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                              torch::Tensor dres) {
+  TORCH_CHECK(dy.is_contiguous() && x.is_contiguous() && dy.scalar_type() == torch::kBFloat16 &&
+                  x.scalar_type() == torch::kBFloat16, "dy/x contiguous bf16");
+  TORCH_CHECK(dres.is_contiguous() && dres.scalar_type() == torch::kBFloat16 && dres.numel() == x.numel(),
+              "dres contiguous bf16 of x's size");
+  TORCH_CHECK(dw.scalar_type() == torch::kFloat32 && dw.is_contiguous(), "dw must be fp32");
+  PM_CHECK_CUDA(dy); PM_CHECK_CUDA(x); PM_CHECK_CUDA(w); PM_CHECK_CUDA(rstd); PM_CHECK_CUDA(dw); PM_CHECK_CUDA(dres);
+  const int H = (int)x.size(-1);
+  const int rows = (int)(x.numel() / H);
+  TORCH_CHECK(dy.numel() == x.numel() && w.numel() == H && dw.numel() == H && rstd.numel() == rows,
+              "rmsnorm_bwd_add: shapes");
+  check_row_ptr(x, "x");
+  check_row_ptr(dy, "dy");
+  check_row_ptr(dres, "dres");
+  c10::cuda::CUDAGuard guard(x.device());
+  auto dx = torch::empty_like(x);
+  if (rows == 0) return dx;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int S, smem;
+  row_stream_shape(H, 3, 2, &S, &smem);
+  const int grid = std::min(sm_count(), (rows + kRowWarps - 1) / kRowWarps);
+#define PM_RMS_BWD_ADD(WT_, WPTR)                                                                              \
+  PM_VPL_DISPATCH(H, {                                                                                         \
+    auto kern = rmsnorm_bwd_kernel<VPL, WT_, true>;                                                            \
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));             \
+    kern<<<grid, 256, smem, stream>>>((const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(), \
+                                      WPTR, rstd.data_ptr<float>(), (__nv_bfloat16*)dx.data_ptr(),             \
+                                      dw.data_ptr<float>(), rows, H, S, (const __nv_bfloat16*)dres.data_ptr()); \
+  })
+  if (w.scalar_type() == torch::kFloat32) {
+    PM_RMS_BWD_ADD(float, w.data_ptr<float>());
+  } else {
+    TORCH_CHECK(w.scalar_type() == torch::kBFloat16, "weight must be fp32 or bf16");
+    PM_RMS_BWD_ADD(__nv_bfloat16, (const __nv_bfloat16*)w.data_ptr());
+  }
+#undef PM_RMS_BWD_ADD
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return dx;
 }

@@ -18,6 +18,9 @@ void moe_wgrad(torch::Tensor a, torch::Tensor b, torch::Tensor offsets, torch::T
 
 // norm_rope.cu
 std::vector<torch::Tensor> rmsnorm_fwd(torch::Tensor x, torch::Tensor w, double eps);
+std::vector<torch::Tensor> add_rmsnorm_fwd(torch::Tensor x, torch::Tensor res, torch::Tensor w, double eps);
+torch::Tensor rmsnorm_bwd_add(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw,
+                              torch::Tensor dres);
 torch::Tensor rmsnorm_bwd(torch::Tensor dy, torch::Tensor x, torch::Tensor w, torch::Tensor rstd, torch::Tensor dw);
 std::vector<torch::Tensor> qkv_rope_fwd(torch::Tensor qkv, torch::Tensor pos, torch::Tensor rope,
                                         c10::optional<torch::Tensor> qw, c10::optional<torch::Tensor> kw, int64_t Hq,

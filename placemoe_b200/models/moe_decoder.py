@@ -2,6 +2,7 @@
 
 Layer:  h = x + o_proj(attn(qk_norm_rope(qkv_proj(rmsnorm(x)))))
         y = h + moe(rmsnorm(h))
+        (each residual add runs inside the RMSNorm that follows it: ``forward_fused``)
 
 * Attention projections are one fused QKV weight ``[(Hq + 2 Hkv) D, H]``.
 * The MoE block keeps fp32 master expert weights for the physical slots this
@@ -43,6 +44,10 @@ class RMSNorm(nn.Module):
 
     def forward(self, x):
         return mp_ops.rmsnorm(x, self.weight, self.eps)
+
+    def add_norm(self, x, res):
+        """(x + res, norm(x + res)); (x, norm(x)) when ``res`` is None."""
+        return mp_ops.add_rmsnorm(x, res, self.weight, self.eps)
 
 
 class Attention(nn.Module):
@@ -199,9 +204,16 @@ class DecoderLayer(nn.Module):
         self.mlp = DenseMLP(cfg) if cfg.is_dense else MoEBlock(cfg, layer_idx, num_local_slots)
 
     def forward(self, x, pos, seq_len, docs=None):
-        x = x + self.self_attn(self.input_layernorm(x), pos, seq_len, docs)
-        x = x + self.mlp(self.post_attention_layernorm(x))
-        return x
+        h, m = self.forward_fused(x, None, pos, seq_len, docs)
+        return h + m
+
+    def forward_fused(self, x, branch, pos, seq_len, docs=None):
+        """The layer on the residual stream x + branch (branch: the previous layer's MLP output, not yet
+        added).  Returns (residual after attention, MLP output): each residual add runs inside the
+        norm that follows it."""
+        h, n = self.input_layernorm.add_norm(x, branch)
+        h, n = self.post_attention_layernorm.add_norm(h, self.self_attn(n, pos, seq_len, docs))
+        return h, self.mlp(n)
 
 
 class MoEForCausalLM(nn.Module):
@@ -285,12 +297,14 @@ class MoEForCausalLM(nn.Module):
         else:
             docs = attn_ops.doc_bounds(cu_seqlens.to(ids.device), b * s, s)
             pos = (torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b) - docs[0]).to(torch.int32)
+        branch = None
         for layer in self.layers:
             if self.gradient_checkpointing and self.training:
-                x = torch.utils.checkpoint.checkpoint(layer, x, pos, s, docs, use_reentrant=False)
+                x, branch = torch.utils.checkpoint.checkpoint(layer.forward_fused, x, branch, pos, s, docs,
+                                                              use_reentrant=False)
             else:
-                x = layer(x, pos, s, docs)
-        return self.norm(x)
+                x, branch = layer.forward_fused(x, branch, pos, s, docs)
+        return self.norm.add_norm(x, branch)[1]
 
     def set_sequence_parallel(self, sp) -> None:
         """Run attention with Ulysses sequence parallelism over ``sp`` (a parallel.ulysses.UlyssesGroup)."""

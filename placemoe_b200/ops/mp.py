@@ -102,6 +102,49 @@ class _RMSNormMP(torch.autograd.Function):
         return dx, None, None
 
 
+class _AddRMSNormMP(torch.autograd.Function):
+    """(h, y) = (x + res, rmsnorm(x + res)) in one pass; the backward folds the gradient reaching h
+    through the residual path into the norm's backward (dx = dres = norm backward + dh)."""
+
+    @staticmethod
+    def forward(ctx, x, res, master, eps):
+        h, y, rstd = kernels().add_rmsnorm_fwd(x.contiguous(), res.contiguous(), master.detach(), eps)
+        ctx.save_for_backward(h, rstd)
+        ctx.master = master
+        return h, y
+
+    @staticmethod
+    def backward(ctx, dh, dy):
+        h, rstd = ctx.saved_tensors
+        m = ctx.master
+        if dy is None:
+            return dh, dh, None, None
+        dw = main_grad(m) if m.requires_grad else torch.zeros(m.shape, device=m.device, dtype=torch.float32)
+        dy = dy.contiguous().to(torch.bfloat16)
+        if dh is None:
+            dx = kernels().rmsnorm_bwd(dy, h, m.detach(), rstd, dw)
+        else:
+            dx = kernels().rmsnorm_bwd_add(dy, h, m.detach(), rstd, dw, dh.contiguous().to(torch.bfloat16))
+        return dx, dx, None, None
+
+
+def add_rmsnorm(x: torch.Tensor, res: torch.Tensor | None, w: torch.Tensor, eps: float):
+    """(h, rmsnorm(h)) with h = x + res (h = x when ``res`` is None): the decoder's residual add fused
+    with the norm that follows it."""
+    if res is None:
+        return x, rmsnorm(x, w, eps)
+    if not x.is_cuda:
+        from .norm import rmsnorm_reference
+
+        h = x + res
+        return h, rmsnorm_reference(h, w, eps)
+    if x.dtype != torch.bfloat16:
+        x = x.to(torch.bfloat16)
+    if res.dtype != torch.bfloat16:
+        res = res.to(torch.bfloat16)
+    return _AddRMSNormMP.apply(x, res, w, eps)
+
+
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     if not x.is_cuda:
         from .norm import rmsnorm_reference

@@ -35,6 +35,36 @@ def test_rmsnorm_fwd_bwd(rows, hidden, wdtype):
     assert rel(w.grad, wr.grad) < 1e-2
 
 
+@pytest.mark.parametrize("rows,hidden,wdtype", [(20011, 2048, torch.float32), (9000, 4096, torch.float32),
+                                                (5, 256, torch.bfloat16), (3000, 1024, torch.float32)])
+def test_add_rmsnorm_fwd_bwd(rows, hidden, wdtype):
+    """Residual add fused into the RMSNorm (forward) and the residual-path gradient fused into its
+    backward, against the fp32 reference of h = x + res, y = rmsnorm(h) with h also used downstream."""
+    from placemoe_b200.ops import check_device_error
+    from placemoe_b200.ops.mp import add_rmsnorm
+    from placemoe_b200.ops.norm import rmsnorm_reference
+
+    torch.manual_seed(1)
+    x = torch.randn(rows, hidden, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    res = torch.randn(rows, hidden, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda")).to(wdtype).requires_grad_()
+    h, y = add_rmsnorm(x, res, w, 1e-6)
+    assert torch.equal(h, x.detach() + res.detach())  # the same bf16 rounding as a tensor add
+    gh, gy = torch.randn_like(h), torch.randn_like(y)
+    torch.autograd.backward([h, y], [gh, gy])
+    xr, rr = x.detach().float().requires_grad_(), res.detach().float().requires_grad_()
+    wr = w.detach().float().clone().requires_grad_()
+    hr = xr + rr
+    yr = rmsnorm_reference(hr, wr, 1e-6)
+    torch.autograd.backward([hr, yr], [gh.float(), gy.float()])
+    torch.cuda.synchronize()
+    check_device_error()
+    assert rel(y, yr) < 1e-2
+    assert rel(x.grad, xr.grad) < 2e-2 and rel(res.grad, rr.grad) < 2e-2
+    wg = w.main_grad if getattr(w, "main_grad", None) is not None else w.grad
+    assert rel(wg, wr.grad) < 1e-2
+
+
 # t = 5000 gives every CTA of the persistent grid several tokens, so every ring stage is reused
 @pytest.mark.parametrize("hq,hkv,d,mode,t", [(16, 16, 128, "full", 512), (32, 4, 128, "per_head", 512),
                                            (8, 2, 64, "per_head", 512), (64, 32, 128, "per_head", 512),
