@@ -411,6 +411,12 @@ torch::Tensor rmsnorm_bwd_add(torch::Tensor dy, torch::Tensor x, torch::Tensor w
   check_row_ptr(dy, "dy");
   check_row_ptr(dres, "dres");
   c10::cuda::CUDAGuard guard(x.device());
+  if (kRowBarBytes + 2 * H * 4 + kRowWarps * 3 * H * 2 > kRowSmemBudget) {
+    // rows too wide for a ring of three streamed rows per warp: the plain backward, then the add
+    auto dx = rmsnorm_bwd(dy, x, w, rstd, dw);
+    dx.add_(dres);
+    return dx;
+  }
   auto dx = torch::empty_like(x);
   if (rows == 0) return dx;
   auto stream = at::cuda::getCurrentCUDAStream();
