@@ -71,3 +71,25 @@ def _worker(rank, world, workdir):
 
 def test_dense_training_dp2_and_hf_roundtrip(tmp_path):
     run_distributed(_worker, 2, str(tmp_path))
+
+
+def test_gradient_checkpointing_matches_plain_backward():
+    """Recomputing every decoder layer in the backward (the layers carry the residual and the pending
+    branch output between them) gives the loss and gradients of the plain backward."""
+    from placemoe_b200.models.config import get_preset
+    from placemoe_b200.models.moe_decoder import build_model
+
+    cfg = get_preset("small_qwen3_moe")
+    ids = torch.randint(0, cfg.vocab_size, (2, 64), generator=torch.Generator().manual_seed(0))
+    out = []
+    for ckpt in (False, True):
+        m = build_model(cfg, device="cpu", seed=5)
+        m.train()
+        m.gradient_checkpointing = ckpt
+        loss, aux = m(ids, labels=ids)
+        (loss + aux).backward()
+        out.append((loss.item(), {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}))
+    (l0, g0), (l1, g1) = out
+    assert abs(l0 - l1) < 1e-6 and g0.keys() == g1.keys() and len(g0) > 0
+    for n in g0:
+        assert torch.allclose(g0[n], g1[n], rtol=1e-5, atol=1e-6), n
