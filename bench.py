@@ -170,11 +170,14 @@ def plan_placement(trainer, pool, args, rank, world):
     report = [None]
     if rank == 0:
         out = os.path.join(root, "layout.json")
+        ncpu = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+        workers = min(8, ncpu)
         plan_placemoe.main([
             "--route-root", root, "--optimize-steps", ",".join(str(i) for i in range(args.plan_steps)),
             "--ep-size", str(world), "--num-experts", str(cfg.num_experts),
             "--redundant-slots-per-rank", str(args.redundant_slots), "--hidden-size", str(cfg.hidden_size),
-            "--layers", str(cfg.num_hidden_layers), "--workers", str(min(8, os.cpu_count() or 1)),
+            "--layers", str(cfg.num_hidden_layers), "--workers", str(workers),
+            "--worker-threads", str(max(1, ncpu // workers)),
             "--output-layout", out, "--output-report", os.path.join(root, "report.json"),
             "--emit", "eplb" if args.placement == "eplb" else "placemoe",
         ])

@@ -36,6 +36,8 @@
 #include <tuple>
 #include <vector>
 
+#include "planner.h"
+
 namespace pmp {
 
 // ---------------------------------------------------------------------------------------- normalized
@@ -162,32 +164,58 @@ torch::Tensor community_intersection_hits(torch::Tensor hist) {
   return out;
 }
 
+namespace {
+template <typename Idx>
+bool mask_histogram_source(const Idx* rp, int64_t T, int64_t k, const int64_t* comm, int64_t E, int64_t* row) {
+  for (int64_t t = 0; t < T; ++t) {
+    int64_t mask = 0;
+    for (int64_t j = 0; j < k; ++j) {
+      const int64_t e = (int64_t)rp[t * k + j];
+      if (e < 0 || e >= E) return false;
+      if (comm[e] >= 0) mask |= int64_t(1) << comm[e];
+    }
+    row[mask] += 1;
+  }
+  return true;
+}
+}  // namespace
+
 torch::Tensor community_mask_histogram(std::vector<torch::Tensor> routes, torch::Tensor community,
-                                       int64_t ranks_per_unit, int64_t num_communities) {
+                                       int64_t ranks_per_unit, int64_t num_communities, int64_t sources_per_step) {
   TORCH_CHECK(num_communities > 0 && num_communities <= 20, "1..20 communities");
-  TORCH_CHECK(ranks_per_unit > 0 && (int64_t)routes.size() % ranks_per_unit == 0, "sources split into units");
-  auto cm = community.contiguous();
+  const int64_t n = (int64_t)routes.size();
+  const int64_t S = sources_per_step > 0 ? sources_per_step : n;
+  TORCH_CHECK(n % S == 0 && S % ranks_per_unit == 0 && ranks_per_unit > 0,
+              "routes hold whole steps of sources, split into units");
+  auto cm = community.to(torch::kInt64).contiguous();
   const int64_t* comm = cm.data_ptr<int64_t>();
   const int64_t E = cm.numel();
-  const int64_t U = (int64_t)routes.size() / ranks_per_unit, K = int64_t(1) << num_communities;
+  const int64_t U = S / ranks_per_unit, K = int64_t(1) << num_communities;
   auto out = torch::zeros({U, K}, torch::kInt64);
   int64_t* op = out.data_ptr<int64_t>();
+  std::vector<torch::Tensor> rt(routes.size());
   for (size_t s = 0; s < routes.size(); ++s) {
-    auto r = routes[s].contiguous();
-    TORCH_CHECK(r.dim() == 2 && r.dtype() == torch::kInt64, "routes: int64 [tokens, k]");
-    const int64_t T = r.size(0), k = r.size(1);
-    const int64_t* rp = r.data_ptr<int64_t>();
-    const int64_t u = (int64_t)s / ranks_per_unit;
-    for (int64_t t = 0; t < T; ++t) {
-      int64_t mask = 0;
-      for (int64_t j = 0; j < k; ++j) {
-        const int64_t e = rp[t * k + j];
-        TORCH_CHECK(e >= 0 && e < E, "expert id out of range");
-        if (comm[e] >= 0) mask |= int64_t(1) << comm[e];
-      }
-      op[u * K + mask] += 1;
-    }
+    auto r = routes[s];
+    if (r.scalar_type() != torch::kInt32 && r.scalar_type() != torch::kInt64) r = r.to(torch::kInt64);
+    rt[s] = r.contiguous();
+    TORCH_CHECK(rt[s].dim() == 2, "routes: [tokens, k]");
   }
+  // units own disjoint rows of the histogram: one unit per pool item, its sources of every step in order
+  std::vector<char> bad(U, 0);
+  run_pool(U, [&](int64_t u) {
+    std::vector<int64_t> row(K, 0);  // thread-local: short rows of neighbouring units share cache lines
+    for (int64_t i = 0; i < n; ++i) {
+      if ((i % S) / ranks_per_unit != u) continue;
+      const auto& r = rt[i];
+      const int64_t T = r.size(0), k = r.size(1);
+      const bool ok = r.scalar_type() == torch::kInt32
+                          ? mask_histogram_source(r.data_ptr<int32_t>(), T, k, comm, E, row.data())
+                          : mask_histogram_source(r.data_ptr<int64_t>(), T, k, comm, E, row.data());
+      if (!ok) bad[u] = 1;
+    }
+    std::copy(row.begin(), row.end(), op + u * K);
+  });
+  for (int64_t u = 0; u < U; ++u) TORCH_CHECK(!bad[u], "expert id out of range");
   return out;
 }
 

@@ -14,7 +14,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("optimize_mapping_normalized", &pmp::optimize_mapping_normalized,
         "scale-normalised mapping proposal (in place); returns [peak load, sweeps, changes]");
   m.def("community_intersection_hits", &pmp::community_intersection_hits, "tokens whose community mask meets X");
-  m.def("community_mask_histogram", &pmp::community_mask_histogram, "tokens per (source unit, community mask)");
+  m.def("community_mask_histogram", &pmp::community_mask_histogram,
+        "tokens per (source unit, community mask), summed over steps of `sources_per_step` sources",
+        py::arg("routes"), py::arg("community"), py::arg("ranks_per_unit"), py::arg("num_communities"),
+        py::arg("sources_per_step") = 0);
   m.def("optimize_community_mapping", &pmp::optimize_community_mapping,
         "block mapping of (source unit, community) -> destination unit");
 }

@@ -82,23 +82,6 @@ void replay_source(const Idx* r, int64_t T, int64_t K, const uint8_t* dest, int6
   c.total = T * K;
 }
 
-template <typename F>
-void run_pool(int64_t items, F&& fn) {
-  const int64_t nt = std::max<int64_t>(1, std::min<int64_t>(items, at::get_num_threads()));
-  if (nt == 1) {
-    for (int64_t i = 0; i < items; ++i) fn(i);
-    return;
-  }
-  std::atomic<int64_t> next{0};
-  std::vector<std::thread> pool;
-  pool.reserve(nt);
-  for (int64_t w = 0; w < nt; ++w)
-    pool.emplace_back([&] {
-      for (int64_t i = next.fetch_add(1); i < items; i = next.fetch_add(1)) fn(i);
-    });
-  for (auto& th : pool) th.join();
-}
-
 }  // namespace
 
 torch::Tensor evaluate_routes_batch(std::vector<torch::Tensor> routes, torch::Tensor mapping, torch::Tensor slot_rank,

@@ -100,12 +100,14 @@ def community_intersection_hits(mask_histogram: np.ndarray) -> np.ndarray:
 
 
 def community_mask_histogram(routes_by_source, communities: np.ndarray, *, ranks_per_unit: int,
-                             num_communities: int) -> np.ndarray:
+                             num_communities: int, sources_per_step: int = 0) -> np.ndarray:
     """Tokens per (source unit, set of communities the token's experts belong to); sources are grouped
-    ``ranks_per_unit`` at a time.  routes_by_source: one [tokens, k] logical-route tensor per source GPU."""
-    rs = [torch.as_tensor(r).to(torch.int64).contiguous() for r in routes_by_source]
+    ``ranks_per_unit`` at a time.  routes_by_source: one [tokens, k] logical-route tensor per source GPU,
+    or several steps of them back to back (``sources_per_step`` each), summed over the steps."""
+    rs = [torch.as_tensor(r) for r in routes_by_source]  # int32 or int64; the core converts anything else
     c = torch.from_numpy(np.ascontiguousarray(communities, dtype=np.int64))
-    return load_planner().community_mask_histogram(rs, c, int(ranks_per_unit), int(num_communities)).numpy()
+    return load_planner().community_mask_histogram(rs, c, int(ranks_per_unit), int(num_communities),
+                                                   int(sources_per_step)).numpy()
 
 
 @dataclass(frozen=True)

@@ -183,10 +183,9 @@ def _mapping_proposals(stats: ProfileStatistics, layout: np.ndarray, slot_rank: 
         comm = copy_set_communities(layout, slot_rank, topology.num_experts)
         if comm is not None:
             c = int(comm.max()) + 1
-            hist = None
-            for step in evaluator.samples:
-                h = community_mask_histogram(step, comm, ranks_per_unit=1, num_communities=c)
-                hist = h if hist is None else hist + h
+            flat = [r for step in evaluator.samples for r in step]
+            hist = community_mask_histogram(flat, comm, ranks_per_unit=1, num_communities=c,
+                                            sources_per_step=topology.ep_size)
             asg = np.zeros((topology.ep_size, c))
             for k in range(c):
                 asg[:, k] = stats.demand[:, comm == k].sum(axis=1)

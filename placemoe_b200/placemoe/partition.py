@@ -74,13 +74,33 @@ def spectral_embedding(affinity: np.ndarray, dims: int) -> np.ndarray:
     return emb / np.maximum(np.linalg.norm(emb, axis=1, keepdims=True), 1e-12)
 
 
+def _kmeans_centers(x: np.ndarray, k: int, seed: int, iters: int = 100) -> np.ndarray:
+    """Lloyd's k-means with k-means++ seeding (Arthur & Vassilvitskii, 2007) on a few hundred points:
+    small enough for numpy, and it keeps the planner processes free of a heavyweight import."""
+    rng = np.random.default_rng(seed)
+    n = x.shape[0]
+    centers = np.empty((k, x.shape[1]), dtype=np.float64)
+    centers[0] = x[rng.integers(n)]
+    d2 = ((x - centers[0]) ** 2).sum(1)
+    for c in range(1, k):
+        total = d2.sum()
+        i = int(rng.choice(n, p=d2 / total)) if total > 0 else int(rng.integers(n))
+        centers[c] = x[i]
+        d2 = np.minimum(d2, ((x - centers[c]) ** 2).sum(1))
+    for _ in range(iters):
+        lab = ((x[:, None, :] - centers[None, :, :]) ** 2).sum(-1).argmin(1)
+        new = np.stack([x[lab == c].mean(0) if (lab == c).any() else centers[c] for c in range(k)])
+        if np.allclose(new, centers):
+            break
+        centers = new
+    return centers
+
+
 def _capacity_assign(emb: np.ndarray, cfg: PartitionConfig, seed: int) -> np.ndarray:
     from scipy.optimize import linear_sum_assignment
-    from sklearn.cluster import KMeans
 
     g = len(cfg.capacities)
-    km = KMeans(n_clusters=g, random_state=seed, n_init=1, max_iter=100).fit(emb)
-    centers = np.asarray(km.cluster_centers_, dtype=np.float64)
+    centers = _kmeans_centers(np.asarray(emb, dtype=np.float64), g, seed)
     slot_group = np.repeat(np.arange(g), cfg.capacities)
     labels = np.zeros(emb.shape[0], dtype=np.int64)
     for _ in range(cfg.assignment_iterations):

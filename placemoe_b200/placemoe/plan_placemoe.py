@@ -102,6 +102,10 @@ def _topology(args):
 def plan_layer(job: dict) -> dict:
     """Plan one layer (runs in a worker process)."""
     os.environ.setdefault("OMP_NUM_THREADS", str(job["threads"]))
+    import torch
+
+    if job.get("pooled"):  # a worker process: the route replay runs on --worker-threads threads
+        torch.set_num_threads(max(1, int(job["threads"])))
     from .evaluator import RouteReplayEvaluator
     from .optimizer import OptimizerConfig, optimize_fixed_layout_mapping, optimize_replica_allocation
     from .routes import load_routes
@@ -189,6 +193,7 @@ def main(argv=None) -> int:
             "optimize_steps": _ints(args.optimize_steps), "validation_steps": _ints(args.validation_steps),
             "hidden": args.hidden_size, "bpe": args.bytes_per_element, "rounds": args.rounds, "seed": args.seed,
             "mode": args.update_mode, "threads": args.worker_threads,
+            "pooled": args.workers > 1 and nlayers > 1,
             "input_plan": input_plans[key].to_runtime_payload() if key in input_plans else None,
             "comparison": args.comparison_layout, "emit": args.emit,
             "comparison_plan": comparison_plans[key].to_runtime_payload() if key in comparison_plans else None,
