@@ -32,7 +32,9 @@ class _FusedLinearCE(torch.autograd.Function):
         labels = labels.reshape(-1).to(torch.int64).contiguous()
         loss_sum = torch.zeros((), device=h.device, dtype=torch.float32)
         dh = torch.empty_like(h2)
-        dw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+        dw = torch.empty(w.shape, device=w.device, dtype=torch.float32)  # the first chunk stores, later ones add
+        if n == 0:
+            dw.zero_()
         kn = kernels()
         scale = 1.0 / float(denom)
         for s in range(0, n, chunk):
@@ -40,7 +42,7 @@ class _FusedLinearCE(torch.autograd.Function):
             logits = gemm_nt(h2[s:e], wb)
             kn.ce_fwd_bwd(logits, labels[s:e], IGNORE_INDEX, scale, loss_sum, None)
             gemm_nn(logits, wb, out=dh[s:e])
-            gemm_tn(logits, h2[s:e], out=dw, accumulate=True)
+            gemm_tn(logits, h2[s:e], out=dw, accumulate=s > 0)
         ctx.save_for_backward(dh, dw)
         ctx.shape = h.shape
         ctx.master = w
@@ -54,7 +56,7 @@ class _FusedLinearCE(torch.autograd.Function):
         dh = (dh.float() * g).to(torch.bfloat16).reshape(ctx.shape)
         w = ctx.master
         if w.dtype == torch.float32 and w.requires_grad:
-            main_grad(w).add_(dw * g)
+            main_grad(w).addcmul_(dw, g)  # one pass, g stays on the device
             return dh, None, None, None, None
         return dh, (dw * g).to(w.dtype), None, None, None
 
