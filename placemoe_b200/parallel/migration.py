@@ -7,6 +7,11 @@ a copy on the destination GPU first, else the old owner, else the lowest
 slot holding it.  Every rank derives the same transfer list from the two
 plans, so no metadata exchange is needed.
 
+Consensus: before anything moves, one all-reduce checks that every rank installs the same plan
+from the same current layout and holds per-slot state of the same layout (tensor count, sizes,
+dtypes); otherwise every rank raises ``MigrationConsensusError`` and nothing changes (the
+reference does this in its debug mode, expert_swap.py:1302-1392).
+
 Atomicity: staging buffers are allocated first and every rank confirms (an
 all-reduce of a status word) before any transfer is posted, so a local
 failure aborts everywhere without leaving a peer waiting; transfers then land
@@ -84,6 +89,39 @@ def _agree(ok: bool, world: int, group) -> bool:
     return int(status.item()) == 0
 
 
+class MigrationConsensusError(RuntimeError):
+    """Ranks disagree on what a migration installs or moves; raised on every rank, nothing is changed."""
+
+
+def _same_on_all_ranks(values: list[int], world: int, group) -> list[bool]:
+    """Per value: did every rank pass the same integer?  (one MIN all-reduce of [v, -v])"""
+    t = torch.tensor(values + [-v for v in values], dtype=torch.int64)
+    if world > 1:
+        if dist.get_backend(group) == "nccl":
+            t = t.cuda()
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    t = t.cpu().tolist()
+    n = len(values)
+    return [t[i] == -t[n + i] for i in range(n)]
+
+
+def _digest(*arrays) -> int:
+    import zlib
+
+    h = 0
+    for a in arrays:
+        h = zlib.crc32(np.ascontiguousarray(a).tobytes(), h)
+    return h
+
+
+def _payload_signature(blk, opt) -> int:
+    """Layout of one slot's migrated state: tensor count, sizes and dtypes (identical on every rank
+    unless one rank's optimizer holds different state)."""
+    ts = _slot_state(blk, opt, 0)
+    return _digest(np.array([len(ts)] + [t.numel() for t in ts], dtype=np.int64),
+                   np.frombuffer(",".join(str(t.dtype) for t in ts).encode(), dtype=np.uint8))
+
+
 def _unpack_into(buf: torch.Tensor, ts: list[torch.Tensor]) -> None:
     off = 0
     for t in ts:
@@ -104,6 +142,18 @@ def migrate_layer(trainer, blk, new_plan: LayerPlan, group=None) -> int:
     world = dist.get_world_size(group) if dist.is_initialized() else 1
     old_layout, old_owners = pl.slot_to_logical.copy(), pl.owner_slots.copy()
     new_layout = np.asarray(new_plan.slot_to_logical)
+    # 0) consensus: every rank installs the same plan from the same old layout and moves state of the
+    #    same layout per slot; otherwise each rank would derive different transfers (mismatched
+    #    send/recv pairs).  Checked before anything is allocated or sent, and raised on every rank.
+    same_plan, same_old, same_payload = _same_on_all_ranks(
+        [_digest(new_layout, np.asarray(new_plan.source_logical_to_physical), np.asarray(new_plan.owner_slots)),
+         _digest(old_layout, old_owners), _payload_signature(blk, opt)], world, group)
+    if not (same_plan and same_old):
+        raise MigrationConsensusError(f"{blk.layer_key}: ranks disagree on the placement "
+                                      f"({'new plan' if not same_plan else 'current layout'}); nothing moved")
+    if not same_payload:
+        raise MigrationConsensusError(f"{blk.layer_key}: asymmetric migration payload (per-slot parameter / "
+                                      "optimizer-state layout differs between ranks); nothing moved")
     transfers = plan_transfers(old_layout, old_owners, new_layout, spr)
     # 1) preflight: every rank allocates its staging and send buffers; a failure anywhere
     #    aborts on every rank before any transfer is posted (nobody waits on a missing peer)

@@ -97,6 +97,30 @@ def _worker_migrate(rank, world, workdir):
         migration.allocate_staging = real
     assert np.array_equal(tr.model.moe_blocks()[0].placement.slot_to_logical, old[0])
 
+    # consensus: rank 1 is handed a different plan -> every rank raises, nothing changes
+    plans_a = validate_placemoe_artifact(_new_payload(tr, seed=11))
+    plans_b = validate_placemoe_artifact(_new_payload(tr, seed=12 if rank == 1 else 11))
+    with pytest.raises(migration.MigrationConsensusError, match="disagree"):
+        migration.migrate_layer(tr, blk, plans_b[blk.layer_key])
+    assert np.array_equal(blk.placement.slot_to_logical, old[0])
+    # consensus: rank 0's optimizer holds an extra state tensor per slot -> asymmetric payload everywhere
+    real_state = migration._slot_state
+
+    def extra(b, o, j):
+        ts = real_state(b, o, j)
+        return ts + [ts[0]] if rank == 0 else ts
+
+    migration._slot_state = extra
+    try:
+        with pytest.raises(migration.MigrationConsensusError, match="asymmetric"):
+            migration.migrate_layer(tr, blk, plans_a[blk.layer_key])
+    finally:
+        migration._slot_state = real_state
+    assert np.array_equal(blk.placement.slot_to_logical, old[0])
+    # and the same plan still installs afterwards
+    migration.migrate_layer(tr, blk, plans_a[blk.layer_key])
+    assert np.array_equal(blk.placement.slot_to_logical, np.asarray(plans_a[blk.layer_key].slot_to_logical))
+
 
 def test_full_install_migrates_state_atomically(tmp_path):
     run_distributed(_worker_migrate, 2, str(tmp_path))
