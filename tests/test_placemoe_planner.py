@@ -114,6 +114,24 @@ def test_partition_respects_capacity_and_uniqueness():
             assert len(set(r.labels[item_expert == e].tolist())) == 2
 
 
+def test_kmeans_seeding_is_deterministic_and_separates_clusters():
+    from placemoe_b200.placemoe.partition import _kmeans_centers
+
+    rng = np.random.default_rng(0)
+    true = np.array([[5.0, 0.0], [0.0, 5.0], [-5.0, -5.0]])
+    pts = np.concatenate([c + 0.1 * rng.standard_normal((40, 2)) for c in true])
+    a = _kmeans_centers(pts, 3, seed=7)
+    b = _kmeans_centers(pts, 3, seed=7)
+    assert np.array_equal(a, b)
+    # every true cluster centre has a found centre next to it
+    d = np.linalg.norm(true[:, None, :] - a[None, :, :], axis=-1)
+    assert (d.min(axis=1) < 0.2).all()
+    # degenerate input (all points equal) still returns k finite centres
+    same = np.ones((10, 2))
+    c = _kmeans_centers(same, 4, seed=0)
+    assert c.shape == (4, 2) and np.isfinite(c).all()
+
+
 def test_seed_plans_validate():
     t8 = PlaceMoETopology(8, 8, 64, 9)
     fixed_ep_plan(t8).validate(t8)
