@@ -85,13 +85,11 @@ class Attention(nn.Module):
             o = attn_ops.causal_attention(q, k, v, seq_len, docs)  # [T, Hq, D]
             o = o.reshape(o.shape[0], -1)
         else:
-            if docs is not None:
-                raise NotImplementedError("packed documents with sequence parallelism")
             from ..parallel.ulysses import heads_to_seq, seq_to_heads
 
             b = x.shape[0] // seq_len
             q, k, v = (seq_to_heads(t, sp, b, seq_len) for t in (q, k, v))
-            o = attn_ops.causal_attention(q, k, v, full)  # [B*S, Hq/P, D]
+            o = attn_ops.causal_attention(q, k, v, full, docs)  # [B*S, Hq/P, D]; docs of the whole rows
             o = heads_to_seq(o, sp, b, seq_len)
         return mp_ops.linear(o, self.o_proj)
 
@@ -288,9 +286,15 @@ class MoEForCausalLM(nn.Module):
         x = mp_ops.embedding(ids, self.embed_tokens, self._anchor(ids.device))
         docs = None
         sp = getattr(self, "sp", None)
-        if sp is not None:  # this rank's chunk of every sequence starts at position rank * s
-            if cu_seqlens is not None:
-                raise NotImplementedError("packed documents with sequence parallelism")
+        if sp is not None and cu_seqlens is not None:
+            # cu_seqlens covers the whole sequences of the group (b rows of P*s tokens); attention runs on
+            # whole sequences, so the document bounds are those of the full rows, and the positions are
+            # this rank's chunk of the full rows' in-document positions
+            full = s * sp.size
+            docs = attn_ops.doc_bounds(cu_seqlens.to(ids.device), b * full, full)
+            pos_full = torch.arange(full, device=ids.device, dtype=torch.int32).repeat(b) - docs[0]
+            pos = pos_full.view(b, full)[:, sp.rank * s:(sp.rank + 1) * s].reshape(-1).to(torch.int32).contiguous()
+        elif sp is not None:  # this rank's chunk of every sequence starts at position rank * s
             pos = (torch.arange(s, device=ids.device, dtype=torch.int32) + sp.rank * s).repeat(b)
         elif cu_seqlens is None:
             pos = torch.arange(s, device=ids.device, dtype=torch.int32).repeat(b)

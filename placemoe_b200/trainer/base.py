@@ -227,11 +227,11 @@ class Trainer:
 
         with ActivationOffload(enabled=self.cfg.activation_offload and self.device.type == "cuda"):
             if self.sp is not None:
-                if cu_seqlens is not None:
-                    raise NotImplementedError("packed documents with sequence parallelism")
                 # every rank of the SP group holds the same sequences: take this rank's chunk of the tokens and
                 # of the next-token targets of the whole sequence; the loss divisor is the group's target
-                # count over P, so the mean of the P chunk losses is the loss of the whole batch
+                # count over P, so the mean of the P chunk losses is the loss of the whole batch.  Packed rows:
+                # the last token of every document predicts nothing, and attention (on whole sequences after
+                # the exchange) stays inside each document.
                 from ..ops.loss import IGNORE_INDEX
 
                 b, s = input_ids.shape
@@ -239,9 +239,14 @@ class Trainer:
                 chunk = s // p
                 targets = torch.full_like(input_ids, IGNORE_INDEX)
                 targets[:, :-1] = input_ids[:, 1:]
+                n_targets = b * (s - 1)
+                if cu_seqlens is not None:
+                    ends = cu_seqlens.to(targets.device).long()[1:] - 1
+                    targets.view(-1)[ends] = IGNORE_INDEX
+                    n_targets = b * s - (cu_seqlens.numel() - 1)
                 sl = slice(r * chunk, (r + 1) * chunk)
                 loss, aux = self.model(input_ids[:, sl].contiguous(), shifted_labels=targets[:, sl].contiguous(),
-                                       loss_denom=b * (s - 1) / p)
+                                       loss_denom=n_targets / p, cu_seqlens=cu_seqlens)
             elif cu_seqlens is None:
                 loss, aux = self.model(input_ids, labels=input_ids)
             else:

@@ -55,3 +55,33 @@ def _train_worker(rank, world):
 
 def test_ulysses_training_matches_whole_sequences():
     run_distributed(_train_worker, 2)
+
+
+def _train_packed_worker(rank, world):
+    import torch.distributed as dist
+
+    from placemoe_b200.trainer.base import TrainConfig, Trainer
+
+    g = torch.Generator().manual_seed(6)
+    batches = [torch.randint(0, 1024, (2, 64), generator=g) for _ in range(3)]  # same on both ranks
+    # documents cross the chunk boundary (token 32 of each row), one is a single token
+    cu = torch.tensor([0, 10, 40, 41, 64, 64 + 30, 64 + 33, 128], dtype=torch.int32)
+    losses = {}
+    for sp in (1, 2):
+        cfg = TrainConfig(model="tiny_qwen3_moe", seq_len=64, batch_per_rank=2, micro_batch_size=2, lr=1e-3,
+                          device="cpu", seed=0, ulysses_size=sp, max_grad_norm=0.0)
+        tr = Trainer(cfg)
+        out = []
+        for ids in batches:
+            loss = torch.tensor(tr.train_step(ids, cu_seqlens=cu))
+            if sp > 1:
+                dist.all_reduce(loss)
+                loss = loss / sp
+            out.append(float(loss))
+        losses[sp] = out
+    for a, b in zip(losses[1], losses[2]):
+        assert abs(a - b) < 1e-4 * max(1.0, abs(a)), (losses[1], losses[2])
+
+
+def test_ulysses_training_with_packed_documents_matches_whole_sequences():
+    run_distributed(_train_packed_worker, 2)
