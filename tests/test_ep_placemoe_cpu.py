@@ -1,4 +1,4 @@
-"""BASELINE config 1 on CPU/gloo: EP=2 plumbing run with a planned PlaceMoE artifact.
+"""The CPU/gloo plumbing run of the benchmark plan: EP=2 with a planned PlaceMoE artifact.
 
 Tiny Qwen3-MoE (4 layers, hidden 256, 8q/2kv x 32, 16 experts top-4, I 128,
 vocab 1024), fp32, batch 2 x 256 uniform ids (seed 0), router bias
@@ -14,7 +14,7 @@ import torch
 
 from dist_utils import run_distributed
 
-STEPS = 6
+STEPS = 10  # the 10-step plumbing run of the benchmark plan
 
 
 def _trainer(artifact="", capture=False, redundant=0):
