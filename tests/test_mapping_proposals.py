@@ -80,6 +80,13 @@ def test_mask_histogram_and_copy_set_communities():
     assert hist.shape == (2, 8)
     assert hist[0, 0b011] == 1 and hist[0, 0b110] == 1 and hist[1, 0b100] == 1 and hist[1, 0b101] == 1
     assert copy_set_communities(np.arange(40), np.arange(40) // 5, 40, max_communities=4) is None  # 8 sets
+    # several steps in one call (sources_per_step each) equal the sum of the per-step histograms,
+    # for int32 and int64 routes alike
+    step2 = [torch.tensor([[1, 1], [0, 0]], dtype=torch.int32), torch.tensor([[1, 2]], dtype=torch.int32)]
+    both = community_mask_histogram(routes + step2, comm, ranks_per_unit=1, num_communities=3, sources_per_step=2)
+    assert np.array_equal(both, hist + community_mask_histogram(step2, comm, ranks_per_unit=1, num_communities=3))
+    units = community_mask_histogram(routes + step2, comm, ranks_per_unit=2, num_communities=3, sources_per_step=2)
+    assert units.shape == (1, 8) and np.array_equal(units[0], both.sum(0))
 
 
 def test_proposals_join_the_alternation_and_never_lose():
