@@ -106,10 +106,14 @@ def _same_on_all_ranks(values: list[int], world: int, group) -> list[bool]:
 
 
 def _digest(*arrays) -> int:
+    """CRC-32 over the arrays' values (integers as int64, so equal plans hash equally whatever their dtype)."""
     import zlib
 
     h = 0
     for a in arrays:
+        a = np.asarray(a)
+        if a.dtype.kind in "iub" and a.dtype != np.uint8:
+            a = a.astype(np.int64)
         h = zlib.crc32(np.ascontiguousarray(a).tobytes(), h)
     return h
 
